@@ -1,0 +1,196 @@
+// common.cuh -- device helpers shared by the t0b kernels (sm_100a only).
+//
+// Every wait on an mbarrier is bounded (T0B_WAIT_CYCLES SM cycles, ~2 s);
+// a wait that runs out records an error code in the caller-provided device
+// error word and returns false so the kernel can drain and exit.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define T0B_DEV __device__ __forceinline__
+
+#ifndef T0B_WAIT_CYCLES
+#define T0B_WAIT_CYCLES 4000000000LL
+#endif
+
+// device error codes written to the error word
+enum : int {
+  T0B_DEVERR_NONE = 0,
+  T0B_DEVERR_WAIT_X = 1,     // TMA X tile never arrived
+  T0B_DEVERR_WAIT_W = 2,     // raw weight tile never arrived
+  T0B_DEVERR_WAIT_DEQ = 3,   // dequantized tile never published
+  T0B_DEVERR_WAIT_EMPTY = 4, // MMA never released a stage
+  T0B_DEVERR_WAIT_ACC = 5,   // accumulator never completed
+  T0B_DEVERR_SHAPE = 6       // kernel launched with an unsupported shape
+};
+
+T0B_DEV void record_error(int *err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+T0B_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// ---------------------------------------------------------------- mbarrier
+T0B_DEV void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+T0B_DEV void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+T0B_DEV void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+T0B_DEV void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+T0B_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on phase `parity`.  Returns false (and records `code`) when
+// the wait runs out, or immediately when *abort is already set.
+T0B_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code, volatile int *abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (abort_flag && *abort_flag) return false;
+    if (clock64() - t0 > T0B_WAIT_CYCLES) {
+      record_error(err, code);
+      if (abort_flag) *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- fences
+T0B_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+T0B_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+T0B_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// ---------------------------------------------------------------- TMA
+// 2-D tiled bulk tensor load global -> shared, completion on an mbarrier.
+// The innermost coordinate x times the element size must be a multiple of
+// 16 bytes (callers guarantee it).
+T0B_DEV void tma_load_2d(void *dst, const void *tmap, uint64_t *bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"((uint64_t)tmap), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+T0B_DEV void prefetch_tmap(const void *tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)tmap) : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+T0B_DEV void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+T0B_DEV void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;"); }
+T0B_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem] (+)= A[smem] . B[smem]^T, both K-major, kind::f16 (f16 inputs,
+// f32 accumulate).  Issued by one thread.
+T0B_DEV void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on `bar` when all previously issued MMAs of this thread finish.
+T0B_DEV void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// 32 lanes x 32 consecutive f32 columns -> 32 registers per thread.
+T0B_DEV void tmem_ld32(uint32_t taddr, float *v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
+      "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows of 128 B
+// (64 f16), 8-row atoms of 1024 B stacked at a stride of 1024 B.  The atom
+// base must be 1024-byte aligned.
+T0B_DEV uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024u >> 4) << 32;  // stride byte offset: next 8-row atom
+  d |= (uint64_t)1 << 46;             // descriptor version for tcgen05
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+// Instruction descriptor, kind::f16: f16 A and B, f32 D, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// Byte offset of element (row r, k) in a K-major SW128 tile of 64-wide rows.
+T0B_DEV uint32_t sw128_offset(uint32_t r, uint32_t k) {
+  return (r >> 3) * 1024u + (r & 7u) * 128u + ((((k >> 3) ^ (r & 7u)) & 7u) << 4) + (k & 7u) * 2u;
+}
+
+// ---------------------------------------------------------------- mma.sync
+T0B_DEV void mma16816(float &d0, float &d1, float &d2, float &d3, uint32_t a0, uint32_t a1, uint32_t a2,
+                      uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---------------------------------------------------------------- cp.async
+T0B_DEV void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+T0B_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+T0B_DEV void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ---------------------------------------------------------------- numerics
+// Exact int8 pair (little-endian in the low 16 bits of w) -> f16x2, using
+// the f16 encoding 0x6400|u == 1024+u for u in [0,1024).
+T0B_DEV uint32_t i8x2_to_h2(uint32_t w) {
+  uint32_t u = __byte_perm(w ^ 0x8080u, 0x64646464u, 0x5140u);  // 1024 + q + 128
+  __half2 h = *reinterpret_cast<__half2 *>(&u);
+  h = __hsub2(h, __halves2half2(__float2half_rn(1152.0f), __float2half_rn(1152.0f)));
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+// Exact nibble pair -> f16x2 of (nibble - 8): low nibbles of the two bytes
+// of w (hi = 0) or their high nibbles (hi = 1).
+T0B_DEV uint32_t nib2_to_h2(uint32_t w, int hi) {
+  uint32_t s = hi ? (w >> 4) : w;
+  uint32_t u = (s & 0x000Fu) | ((s & 0x0F00u) << 8) | 0x64006400u;  // 1024 + n
+  __half2 h = *reinterpret_cast<__half2 *>(&u);
+  h = __hsub2(h, __halves2half2(__float2half_rn(1032.0f), __float2half_rn(1032.0f)));
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+// f32 -> (hi, lo) f16 pair with hi + lo == x to about 2^-22 relative.
+T0B_DEV void split_f16(float x, __half &hi, __half &lo) {
+  hi = __float2half_rn(x);
+  lo = __float2half_rn(x - __half2float(hi));
+}
+T0B_DEV float f16_bits_to_f32(uint16_t b) { return __half2float(__ushort_as_half(b)); }

@@ -1,0 +1,144 @@
+// epilogue.cuh -- fused GEMM epilogues shared by the small-M (mma.sync) and
+// large-M (tcgen05) dequant-GEMM paths.
+//
+// A thread owns one output row m and a run of consecutive columns.  The
+// accumulator it receives is sum_k A'[m,k] * W[n,k] where A' is the A
+// operand as stored (for the RMSNorm-fused GEMMs A' = x * g, the row's
+// 1/sqrt(mean(x^2)+eps) factor is applied here: rmsnorm(x)*g . W^T ==
+// (x*g . W^T) / sqrt(mean(x^2)+eps), ops.rs:12-17).
+#pragma once
+
+#include "common.cuh"
+
+enum : int { EPI_PLAIN = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_SWIGLU = 3 };
+
+struct Epi {
+  int kind;
+  int M, N;
+  const float *bias;  // [N] (SWIGLU: [2F], gate then up)
+  // optional fused RMSNorm row scale: partial sums of squares of the
+  // un-normalised row, ssq_in[m * ssq_in_nt + slot], over ssq_dim columns
+  const float *ssq_in;
+  int ssq_in_nt, ssq_dim;
+  // EPI_PLAIN: y [M, ldy]
+  float *y;
+  int ldy;
+  // EPI_QKV: y = fused q|k|v buffer [M, 3E]; per-head RMSNorm with qn / kn
+  // (eps 1e-8, ops.rs:175-177), then xpos RoPE (tables [p, hd], TIME layers
+  // only: rope != 0) with the k side using 1/scale (ops.rs:132-142).
+  const float *qn, *kn, *rcos, *rsin, *rsc;
+  int p, E, rope;
+  // EPI_RESID: x[m, n] += acc + bias (f32 residual stream, in place); then
+  // x*gnext split into f16 (xh, xl) for the next RMSNorm-fused GEMM and the
+  // sum of x^2 over this thread's columns written to ssq_out[m*nt + slot].
+  float *x;
+  const float *gnext;
+  __half *xh, *xl;
+  float *ssq_out;
+  int ssq_out_nt;
+  // EPI_SWIGLU: z = silu(gate) * up over F columns (ops.rs:49-62), split to
+  // (zh, zl) f16 and optionally written as f32 (z32).
+  int F;
+  __half *zh, *zl;
+  float *z32;
+};
+
+T0B_DEV float epi_row_denom(const Epi &e, int m) {
+  if (!e.ssq_in) return 1.0f;
+  float s = 0.0f;
+  for (int i = 0; i < e.ssq_in_nt; ++i) s += e.ssq_in[(size_t)m * e.ssq_in_nt + i];
+  return sqrtf(s / (float)e.ssq_dim + 1e-8f);
+}
+
+T0B_DEV void store_split(__half *hi, __half *lo, size_t off, const float *v, int n) {
+  for (int i = 0; i < n; i += 2) {
+    __half h0, l0, h1, l1;
+    split_f16(v[i], h0, l0);
+    split_f16(v[i + 1], h1, l1);
+    *reinterpret_cast<__half2 *>(hi + off + i) = __halves2half2(h0, h1);
+    *reinterpret_cast<__half2 *>(lo + off + i) = __halves2half2(l0, l1);
+  }
+}
+
+// 32 columns n0..n0+31 of row m, kinds PLAIN and RESID.  Returns the sum of
+// squares of the new residual row values (RESID) or 0.
+T0B_DEV float epi_cols32(const Epi &e, int m, int n0, float *v, float denom) {
+  if (e.kind == EPI_PLAIN) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = v[i] / denom + (e.bias ? e.bias[n0 + i] : 0.0f);
+    float4 *dst = reinterpret_cast<float4 *>(e.y + (size_t)m * e.ldy + n0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    return 0.0f;
+  }
+  // EPI_RESID
+  float *xr = e.x + (size_t)m * e.N + n0;
+  float ss = 0.0f;
+  float g[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float4 xo = reinterpret_cast<const float4 *>(xr)[i];
+    float xs[4] = {xo.x, xo.y, xo.z, xo.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int c = 4 * i + j;
+      float a = v[c] / denom + e.bias[n0 + c];
+      float xn = xs[j] + a;
+      v[c] = xn;
+      ss += xn * xn;
+      g[c] = xn * e.gnext[n0 + c];
+    }
+    reinterpret_cast<float4 *>(xr)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  }
+  store_split(e.xh, e.xl, (size_t)m * e.N + n0, g, 32);
+  return ss;
+}
+
+// One attention head (64 columns n0..n0+63, n0 % 64 == 0) of the QKV output.
+T0B_DEV void epi_qkv64(const Epi &e, int m, int n0, float *v, float denom) {
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = v[i] / denom + e.bias[n0 + i];
+  int seg = n0 / e.E;  // 0 = q, 1 = k, 2 = v
+  if (seg < 2) {
+    const float *g = seg == 0 ? e.qn : e.kn;
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) s += v[i] * v[i];
+    float dn = sqrtf(s / 64.0f + 1e-8f);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = v[i] / dn * g[i];
+    if (e.rope) {
+      int pos = m % e.p;
+      const float *c = e.rcos + pos * 64, *sn = e.rsin + pos * 64, *sc = e.rsc + pos * 64;
+      float o[64];
+#pragma unroll
+      for (int d = 0; d < 64; ++d) {
+        float s_d = seg == 0 ? sc[d] : 1.0f / sc[d];
+        float rot = (d & 1) ? v[d - 1] : -v[d + 1];
+        o[d] = v[d] * c[d] * s_d + rot * sn[d] * s_d;
+      }
+#pragma unroll
+      for (int d = 0; d < 64; ++d) v[d] = o[d];
+    }
+  }
+  float4 *dst = reinterpret_cast<float4 *>(e.y + (size_t)m * 3 * e.E + n0);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+// SwiGLU pair: gate columns f0..f0+31 and the matching up columns.
+T0B_DEV void epi_swiglu32(const Epi &e, int m, int f0, const float *gacc, const float *uacc, float denom) {
+  float z[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float g = gacc[i] / denom + (e.bias ? e.bias[f0 + i] : 0.0f);
+    float u = uacc[i] / denom + (e.bias ? e.bias[e.F + f0 + i] : 0.0f);
+    z[i] = g / (1.0f + expf(-g)) * u;
+  }
+  if (e.zh) store_split(e.zh, e.zl, (size_t)m * e.F + f0, z, 32);
+  if (e.z32) {
+    float4 *dst = reinterpret_cast<float4 *>(e.z32 + (size_t)m * e.F + f0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[i] = make_float4(z[4 * i], z[4 * i + 1], z[4 * i + 2], z[4 * i + 3]);
+  }
+}

@@ -1,0 +1,376 @@
+// k_misc.cu -- the non-GEMM kernels of the forecast path:
+//   * prep: padding + causal per-timestep scaler + patch features on device
+//     (data.rs:52-155, scaler.rs:44-118, model.rs:185-199);
+//   * sgemm_nt: f32 GEMM for the small f16-on-disk layers (patch encoder,
+//     decoder), ops.rs:24-42;
+//   * rownorm_split: x*g split into f16 hi/lo + sum of squares per row;
+//   * time / group attention with implicit masks (mask.rs:49-82, ops.rs:153-190);
+//   * decoder gather + out_norm, and the quantile head + inverse scaling +
+//     forecast-region slice (ops.rs:195-210, scaler.rs:125-148,
+//     model.rs:487-531).
+#include "common.cuh"
+#include <algorithm>
+
+#include "t0b_internal.h"
+
+// ============================================================== prep
+// One thread per variate row: a sequential Welford scan over the padded
+// row, exactly the reference recurrence in f32.
+__global__ void prep_kernel(PrepArgs a) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= a.R) return;
+  const int P = 32;
+  const int lead = a.row_lead[r];
+  const int len = a.row_len[r];
+  const float *src = a.ctx + a.row_off[r];
+  float count = 0.0f, mean = 0.0f, m2 = 0.0f;
+  float feat_v[32];
+  const int hp0 = a.p - a.hp - 1;  // first output patch
+  for (int patch = 0; patch < a.p; ++patch) {
+    float *f = a.feat + ((size_t)r * a.p + patch) * 96;
+    float lo = 0.0f, sc = 1.0f;
+    for (int k = 0; k < P; ++k) {
+      const int t = patch * P + k;
+      int mask;  // 0 valid, 1 pad, 2 missing, 4 withheld
+      float x = 0.0f;
+      if (t < lead) {
+        mask = 1;
+      } else if (t < lead + len) {
+        x = src[t - lead];
+        if (isnan(x)) {
+          mask = 2;
+          x = 0.0f;
+        } else {
+          mask = 0;
+        }
+      } else {
+        mask = 4;
+      }
+      if (mask == 0) {
+        count = __fadd_rn(count, 1.0f);
+        float delta = __fsub_rn(x, mean);
+        mean = __fadd_rn(mean, __fdiv_rn(delta, count));
+        float delta2 = __fsub_rn(x, mean);
+        m2 = __fadd_rn(m2, __fmul_rn(delta, delta2));
+      }
+      if (mask == 1) {  // padding sentinel: group id < 0
+        lo = 0.0f;
+        sc = 1.0f;
+      } else {
+        lo = mean;
+        float var = count > 1.0f ? fmaxf(__fdiv_rn(m2, __fsub_rn(count, 1.0f)), 0.0f) : 0.0f;
+        sc = a.variance_offset ? __fsqrt_rn(__fadd_rn(var, a.eps)) : fmaxf(__fsqrt_rn(var), a.eps);
+      }
+      float z = __fdiv_rn(__fsub_rn(x, lo), sc);
+      feat_v[k] = a.use_arcsinh ? asinhf(z) : z;
+      f[32 + k] = (float)k / 32.0f;
+      f[64 + k] = mask == 0 ? 1.0f : 0.0f;
+    }
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) f[k] = feat_v[k];
+    if (patch >= hp0 && patch < hp0 + a.hp) {  // stats at the patch's last step
+      const size_t o = (size_t)r * a.hp + (patch - hp0);
+      a.out_loc[o] = lo;
+      a.out_scale[o] = sc;
+    }
+  }
+}
+
+// ============================================================== sgemm
+// C[M,N] (+)= A[M,K] . B[N,K]^T + bias (+ bias2) (relu), all f32 row-major.
+// 64x64 tile, 256 threads, 4x4 outputs per thread, K tile 16.
+__global__ void __launch_bounds__(256) sgemm_nt_kernel(SgemmArgs a) {
+  __shared__ float As[16][64 + 4];
+  __shared__ float Bs[16][64 + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < a.K; k0 += 16) {
+    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+      int row = i / 16, kk = i % 16;
+      int m = m0 + row, n = n0 + row, k = k0 + kk;
+      As[kk][row] = (m < a.M && k < a.K) ? a.A[(size_t)m * a.lda + k] : 0.0f;
+      Bs[kk][row] = (n < a.N && k < a.K) ? a.B[(size_t)n * a.ldb + k] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int m = m0 + ty * 4 + i;
+    if (m >= a.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int n = n0 + tx * 4 + j;
+      if (n >= a.N) continue;
+      float v = acc[i][j];
+      if (a.bias) v = v + a.bias[n];
+      if (a.bias2) v = v + a.bias2[n];
+      if (a.bias3) v = v + a.bias3[n];
+      if (a.relu) v = fmaxf(v, 0.0f);
+      float *c = a.C + (size_t)m * a.ldc + n;
+      *c = a.accumulate ? (*c + v) : v;
+    }
+  }
+}
+
+// ============================================================== rownorm_split
+// One warp per row: xh/xl = split(x * g), ssq[r] = sum x^2 (single slot).
+__global__ void rownorm_split_kernel(const float *x, const float *g, __half *xh, __half *xl, float *ssq, int M,
+                                     int E) {
+  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const float *xr = x + (size_t)row * E;
+  float s = 0.0f;
+  for (int c = lane; c < E; c += 32) {
+    float v = xr[c];
+    s += v * v;
+    __half h, l;
+    split_f16(v * g[c], h, l);
+    xh[(size_t)row * E + c] = h;
+    xl[(size_t)row * E + c] = l;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) ssq[row] = s;
+}
+
+// ============================================================== attention
+// Time attention for one (variate row, head): causal over the row's p
+// patches, keys restricted to non-padding patches (mask.rs:49-65).  A query
+// in a whole-padding patch has every key blocked; the reference's softmax
+// then averages V over all p patches (scores all equal -1e9), reproduced
+// here.  K/V staged in shared memory with a 65-float pitch.
+__global__ void __launch_bounds__(128) attn_time_kernel(AttnArgs a) {
+  extern __shared__ float sm[];
+  const int r = blockIdx.x, h = blockIdx.y;
+  const int p = a.p, E = a.E;
+  const int LD = 65;
+  float *Ks = sm;
+  float *Vs = sm + p * LD;
+  float *Ps = sm + 2 * p * LD;  // [4 warps][p] probabilities
+  const size_t tok0 = (size_t)r * p;
+  for (int i = threadIdx.x; i < p * 64; i += blockDim.x) {
+    int j = i >> 6, d = i & 63;
+    const float *row = a.qkv + (tok0 + j) * 3 * E;
+    Ks[j * LD + d] = row[E + h * 64 + d];
+    Vs[j * LD + d] = row[2 * E + h * 64 + d];
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lo = a.row_first_valid[r];
+  float *pw = Ps + warp * p;
+  for (int i = warp; i < p; i += 4) {
+    const float *qrow = a.qkv + (tok0 + i) * 3 * E + h * 64;
+    float q[64];
+#pragma unroll
+    for (int d = 0; d < 64; ++d) q[d] = qrow[d];
+    const bool masked = i < lo;
+    const int j0 = masked ? 0 : lo, j1 = masked ? p - 1 : i;
+    float mx = -INFINITY;
+    for (int j = j0 + lane; j <= j1; j += 32) {
+      float s = 0.0f;
+#pragma unroll
+      for (int d = 0; d < 64; ++d) s = fmaf(q[d], Ks[j * LD + d], s);
+      s = masked ? -1.0e9f : s * 0.125f;
+      pw[j] = s;
+      mx = fmaxf(mx, s);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.0f;
+    for (int j = j0 + lane; j <= j1; j += 32) {
+      float e = expf(pw[j] - mx);
+      pw[j] = e;
+      sum += e;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    __syncwarp();
+    float o0 = 0.0f, o1 = 0.0f;
+    for (int j = j0; j <= j1; ++j) {
+      float pj = pw[j] / sum;
+      o0 = fmaf(pj, Vs[j * LD + lane], o0);
+      o1 = fmaf(pj, Vs[j * LD + lane + 32], o1);
+    }
+    __syncwarp();
+    const size_t oo = (tok0 + i) * E + h * 64;
+    __half hh, ll;
+    split_f16(o0, hh, ll);
+    a.oh[oo + lane] = hh;
+    a.ol[oo + lane] = ll;
+    split_f16(o1, hh, ll);
+    a.oh[oo + lane + 32] = hh;
+    a.ol[oo + lane + 32] = ll;
+    if (a.o32) {
+      a.o32[oo + lane] = o0;
+      a.o32[oo + lane + 32] = o1;
+    }
+  }
+}
+
+// Group attention for one (series, patch): every head (one warp each) over
+// the series' variate rows at that patch (mask.rs:69-82).  Rows whose patch
+// is whole padding are blocked keys; such a query averages V over the
+// series' rows.
+__global__ void __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
+  const int s = blockIdx.x, patch = blockIdx.y;
+  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (h >= a.H) return;
+  const int r0 = a.series_row0[s], nv = a.series_nrows[s];
+  const int p = a.p, E = a.E;
+  for (int qa = 0; qa < nv; ++qa) {
+    const size_t tq = (size_t)(r0 + qa) * p + patch;
+    const float *qrow = a.qkv + tq * 3 * E + h * 64;
+    const float q0 = qrow[lane], q1 = qrow[lane + 32];
+    const bool qmasked = patch < a.row_first_valid[r0 + qa];
+    // two passes over keys: max, then exp-sum and output (nv is small)
+    float mx = -INFINITY;
+    for (int kb = 0; kb < nv; ++kb) {
+      const bool kvalid = patch >= a.row_first_valid[r0 + kb];
+      const size_t tk = (size_t)(r0 + kb) * p + patch;
+      const float *krow = a.qkv + tk * 3 * E + E + h * 64;
+      float d = q0 * krow[lane] + q1 * krow[lane + 32];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      float sc = qmasked ? -1.0e9f : (kvalid ? d * 0.125f : -INFINITY);
+      mx = fmaxf(mx, sc);
+    }
+    float sum = 0.0f, o0 = 0.0f, o1 = 0.0f;
+    for (int kb = 0; kb < nv; ++kb) {
+      const bool kvalid = patch >= a.row_first_valid[r0 + kb];
+      const size_t tk = (size_t)(r0 + kb) * p + patch;
+      const float *krow = a.qkv + tk * 3 * E + E + h * 64;
+      float d = q0 * krow[lane] + q1 * krow[lane + 32];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      float sc = qmasked ? -1.0e9f : (kvalid ? d * 0.125f : -INFINITY);
+      float e = expf(sc - mx);
+      sum += e;
+      const float *vrow = a.qkv + tk * 3 * E + 2 * E + h * 64;
+      o0 = fmaf(e, vrow[lane], o0);
+      o1 = fmaf(e, vrow[lane + 32], o1);
+    }
+    o0 = o0 / sum;
+    o1 = o1 / sum;
+    const size_t oo = tq * E + h * 64;
+    __half hh, ll;
+    split_f16(o0, hh, ll);
+    a.oh[oo + lane] = hh;
+    a.ol[oo + lane] = ll;
+    split_f16(o1, hh, ll);
+    a.oh[oo + lane + 32] = hh;
+    a.ol[oo + lane + 32] = ll;
+    if (a.o32) {
+      a.o32[oo + lane] = o0;
+      a.o32[oo + lane + 32] = o1;
+    }
+  }
+}
+
+// ============================================================== decoder
+// Gather the output-patch tokens of every row and apply out_norm (one warp
+// per output token): xo[r*hp + j] = rmsnorm(x[r*p + p-hp-1+j]) * g.
+__global__ void dec_gather_kernel(const float *x, const float *g, float *xo, int R, int p, int hp, int E) {
+  const int o = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (o >= R * hp) return;
+  const int r = o / hp, j = o % hp;
+  const float *xr = x + ((size_t)r * p + (p - hp - 1 + j)) * E;
+  float s = 0.0f;
+  for (int c = lane; c < E; c += 32) s += xr[c] * xr[c];
+#pragma unroll
+  for (int k = 16; k; k >>= 1) s += __shfl_xor_sync(0xffffffffu, s, k);
+  const float dn = sqrtf(s / (float)E + 1e-8f);
+  for (int c = lane; c < E; c += 32) xo[(size_t)o * E + c] = xr[c] / dn * g[c];
+}
+
+// Quantile head (cumsum of softplus) + inverse scaling + forecast slice.
+// dec [R*hp, 32*nq]; out [R, horizon, nq] (rows remapped by out_row).
+__global__ void dec_head_kernel(const float *dec, const float *loc, const float *scale, float *out,
+                                const int *out_row, int R, int hp, int horizon, int nq, int use_arcsinh) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;  // (r, step)
+  if (idx >= R * hp * 32) return;
+  const int r = idx / (hp * 32), step = idx % (hp * 32);
+  if (step >= horizon) return;
+  const int j = step / 32, k = step % 32;
+  const float *src = dec + ((size_t)r * hp + j) * 32 * nq + k * nq;
+  const float lo = loc[(size_t)r * hp + j], sc = scale[(size_t)r * hp + j];
+  const int orow = out_row ? out_row[r] : r;
+  float *dst = out + ((size_t)orow * horizon + step) * nq;
+  float running = src[0];
+  dst[0] = (use_arcsinh ? sinhf(running) : running) * sc + lo;
+  for (int i = 1; i < nq; ++i) {
+    running = running + logf(1.0f + expf(src[i]));
+    dst[i] = (use_arcsinh ? sinhf(running) : running) * sc + lo;
+  }
+}
+
+// ============================================================== launchers
+cudaError_t t0b_launch_prep(const PrepArgs &a, cudaStream_t st) {
+  prep_kernel<<<(a.R + 127) / 128, 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t t0b_launch_sgemm(const SgemmArgs &a, cudaStream_t st) {
+  dim3 grid((a.N + 63) / 64, (a.M + 63) / 64);
+  sgemm_nt_kernel<<<grid, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t t0b_launch_rownorm_split(const float *x, const float *g, __half *xh, __half *xl, float *ssq, int M, int E,
+                                     cudaStream_t st) {
+  rownorm_split_kernel<<<(M + 7) / 8, 256, 0, st>>>(x, g, xh, xl, ssq, M, E);
+  return cudaGetLastError();
+}
+cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
+  size_t smem = (size_t)(2 * a.p * 65 + 4 * a.p) * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(attn_time_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(a.R, a.H);
+  attn_time_kernel<<<grid, 128, smem, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t t0b_launch_attn_group(const AttnArgs &a, cudaStream_t st) {
+  dim3 grid(a.n_series, a.p);
+  attn_group_kernel<<<grid, 32 * a.H, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t t0b_launch_dec_gather(const float *x, const float *g, float *xo, int R, int p, int hp, int E,
+                                  cudaStream_t st) {
+  int n = R * hp;
+  dec_gather_kernel<<<(n + 7) / 8, 256, 0, st>>>(x, g, xo, R, p, hp, E);
+  return cudaGetLastError();
+}
+cudaError_t t0b_launch_dec_head(const float *dec, const float *loc, const float *scale, float *out, const int *out_row,
+                                int R, int hp, int horizon, int nq, int use_arcsinh, cudaStream_t st) {
+  int n = R * hp * 32;
+  dec_head_kernel<<<(n + 255) / 256, 256, 0, st>>>(dec, loc, scale, out, out_row, R, hp, horizon, nq, use_arcsinh);
+  return cudaGetLastError();
+}
+
+// ============================================================== split
+__global__ void split_f32_kernel(const float *x, __half *h, __half *l, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    __half a, b;
+    split_f16(x[i], a, b);
+    h[i] = a;
+    l[i] = b;
+  }
+}
+cudaError_t t0b_launch_split_f32(const float *x, __half *xh, __half *xl, size_t n, cudaStream_t st) {
+  size_t blocks = std::min<size_t>((n + 255) / 256, 148 * 16);
+  split_f32_kernel<<<(unsigned)std::max<size_t>(blocks, 1), 256, 0, st>>>(x, xh, xl, n);
+  return cudaGetLastError();
+}

@@ -1,0 +1,70 @@
+// t0b_internal.h -- kernel argument blocks and launcher prototypes shared by
+// the host orchestration (t0b_model.cu) and the kernel files.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "epilogue.cuh"
+
+struct PrepArgs {
+  const float *ctx;      // raw context values (NaN = missing)
+  const int64_t *row_off;  // start of row r's values in ctx
+  const int *row_len;    // context steps of row r
+  const int *row_lead;   // leading padding steps of row r (patch-aligns the context)
+  int R, p, hp;          // rows, patches per row, horizon patches
+  int use_arcsinh, variance_offset;
+  float eps;
+  float *feat;           // [R*p, 96]
+  float *out_loc, *out_scale;  // [R*hp] stats at the last step of each output patch
+};
+
+struct SgemmArgs {
+  const float *A;
+  int lda;
+  const float *B;
+  int ldb;
+  float *C;
+  int ldc;
+  int M, N, K;
+  const float *bias, *bias2, *bias3;
+  int relu, accumulate;
+};
+
+struct AttnArgs {
+  const float *qkv;  // [T, 3E]
+  __half *oh, *ol;   // [T, E] split output
+  float *o32;        // optional f32 output
+  const int *row_first_valid;  // whole-padding patches at the start of each row
+  const int *series_row0, *series_nrows;
+  int R, p, E, H, n_series;
+};
+
+cudaError_t t0b_launch_gemm_small(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W,
+                                  const Epi &epi, int *err, cudaStream_t st);
+cudaError_t t0b_launch_gemm_tc(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
+                               int wshift, const Epi &epi, int *err, cudaStream_t st);
+cudaError_t t0b_launch_absmax_scale(const uint8_t *W, size_t nblocks, int bpb, unsigned int *out, cudaStream_t st);
+
+// Exponent s of the power-of-two weight prescale for the split-f16 tensor-core
+// path: the largest |d q| of the matrix (max_d * max|q|) times 2^s stays at
+// or below 2^14, so W*2^s splits into two normal f16 terms without overflow.
+inline int t0b_weight_shift(float max_d, int qt) {
+  const float wmax = max_d * (qt == 8 ? 128.0f : 8.0f);
+  if (!(wmax > 0.0f)) return 0;
+  int s = 0;
+  while (s < 24 && wmax * (float)(1 << (s + 1)) <= 16384.0f) ++s;
+  return s;
+}
+cudaError_t t0b_launch_prep(const PrepArgs &a, cudaStream_t st);
+cudaError_t t0b_launch_sgemm(const SgemmArgs &a, cudaStream_t st);
+cudaError_t t0b_launch_rownorm_split(const float *x, const float *g, __half *xh, __half *xl, float *ssq, int M, int E,
+                                     cudaStream_t st);
+cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st);
+cudaError_t t0b_launch_attn_group(const AttnArgs &a, cudaStream_t st);
+cudaError_t t0b_launch_dec_gather(const float *x, const float *g, float *xo, int R, int p, int hp, int E,
+                                  cudaStream_t st);
+cudaError_t t0b_launch_dec_head(const float *dec, const float *loc, const float *scale, float *out, const int *out_row,
+                                int R, int hp, int horizon, int nq, int use_arcsinh, cudaStream_t st);
+cudaError_t t0b_launch_split_f32(const float *x, __half *xh, __half *xl, size_t n, cudaStream_t st);

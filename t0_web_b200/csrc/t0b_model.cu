@@ -1,0 +1,1039 @@
+// t0b_model.cu -- engine / model / forecast drivers behind the C ABI (t0b.h).
+//
+// Host side of the forecast path (t0-fast lib.rs:50-248 + model.rs:302-808):
+// GGUF parse, weight residency (Q8_0 / Q4_0 blocks copied byte-for-byte to
+// device memory, every other tensor expanded from f16 to f32), the per-pass
+// launch sequence, and the batching drivers.  Independent series are packed
+// as variate rows of p patches each (p = context patches + horizon patches);
+// group attention is scoped per series, so no cross-series mask exists.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/t0b.h"
+#include "gguf_host.h"
+#include "t0b_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+t0b_status fail(t0b_status s, const std::string &msg) {
+  g_last_error = msg;
+  return s;
+}
+
+#define CUDA_TRY(expr)                                                                           \
+  do {                                                                                           \
+    cudaError_t e_ = (expr);                                                                     \
+    if (e_ != cudaSuccess) return fail(T0B_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+constexpr int kMaxHorizon = 1024;  // model.rs:26
+
+// grow-only device buffer
+struct DBuf {
+  void *p = nullptr;
+  size_t bytes = 0;
+  ~DBuf() {
+    if (p) cudaFree(p);
+  }
+  cudaError_t reserve(size_t n) {
+    if (n <= bytes) return cudaSuccess;
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+    cudaError_t e = cudaMalloc(&p, n);
+    if (e == cudaSuccess) bytes = n;
+    return e;
+  }
+  template <class T>
+  T *as() const {
+    return reinterpret_cast<T *>(p);
+  }
+};
+
+// grow-only pinned host buffer
+struct HBuf {
+  void *p = nullptr;
+  size_t bytes = 0;
+  ~HBuf() {
+    if (p) cudaFreeHost(p);
+  }
+  cudaError_t reserve(size_t n) {
+    if (n <= bytes) return cudaSuccess;
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    bytes = 0;
+    cudaError_t e = cudaMallocHost(&p, n);
+    if (e == cudaSuccess) bytes = n;
+    return e;
+  }
+};
+
+struct LayerW {
+  const uint8_t *wqkv, *wo, *w0, *w2;
+  int sh_qkv, sh_o, sh_0, sh_2;  // weight prescale exponents (t0b_weight_shift)
+  const float *bqkv, *bo, *b0, *b2, *g_attn, *g_mlp, *qn, *kn;
+  bool group;
+};
+
+}  // namespace
+
+struct t0b_engine {
+  int device = 0;
+  int *d_err = nullptr;
+  DBuf scratch_xh, scratch_xl, scratch_zh, scratch_zl, scratch_red;
+};
+
+struct t0b_model {
+  t0b_engine *eng = nullptr;
+  t0b_model_info info{};
+  int E = 0, H = 0, F = 0, L = 0, P = 0, nq = 0, qt = 8;
+  std::vector<LayerW> layers;
+  std::vector<void *> allocs;  // every device allocation of the weights
+  const float *enc_hw, *enc_hb, *enc_ow, *enc_ob, *enc_rw, *enc_rb, *temb, *out_g;
+  const float *dec_hw, *dec_hb, *dec_ow, *dec_ob, *dec_rw, *dec_rb;
+  int dec_out = 0, enc_in = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  int *d_err = nullptr;
+  size_t max_tokens = 262144;
+  int tc_min_tokens = 128;
+  std::map<int, float *> rope;  // p -> [3][p][hd] device tables
+  // workspace
+  DBuf x, qkv, feat, ssq, xo, dhid, dout, loc, scl;
+  DBuf xh, xl, ah, al, hh, hl;
+  DBuf meta;  // row/series metadata
+  HBuf hmeta;
+  DBuf ctx_stage, out_stage;
+  ~t0b_model() {
+    for (auto &kv : rope) cudaFree(kv.second);
+    for (void *p : allocs) cudaFree(p);
+    if (own_stream && stream) cudaStreamDestroy(stream);
+    if (d_err) cudaFree(d_err);
+  }
+};
+
+extern "C" const char *t0b_last_error(void) { return g_last_error.c_str(); }
+
+// =================================================================== engine
+extern "C" t0b_status t0b_engine_create(int device, t0b_engine **out) {
+  if (!out) return fail(T0B_ERR_INVALID, "t0b_engine_create: out is NULL");
+  *out = nullptr;
+  int n = 0;
+  CUDA_TRY(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n) return fail(T0B_ERR_INVALID, "t0b_engine_create: no such device");
+  CUDA_TRY(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return fail(T0B_ERR_UNSUPPORTED, "t0b: this engine is built for sm_100a (B200); device is sm_" +
+                                         std::to_string(prop.major) + std::to_string(prop.minor));
+  auto *e = new t0b_engine();
+  e->device = device;
+  if (cudaMalloc(&e->d_err, sizeof(int)) != cudaSuccess || cudaMemset(e->d_err, 0, sizeof(int)) != cudaSuccess) {
+    delete e;
+    return fail(T0B_ERR_OOM, "t0b_engine_create: device allocation failed");
+  }
+  *out = e;
+  return T0B_OK;
+}
+
+extern "C" void t0b_engine_destroy(t0b_engine *e) {
+  if (!e) return;
+  cudaSetDevice(e->device);
+  if (e->d_err) cudaFree(e->d_err);
+  delete e;
+}
+
+// ==================================================================== model
+namespace {
+
+t0b_status upload_f32(t0b_model *m, const t0b::GgufFile &f, const std::string &name, const float **dst,
+                      size_t expect) {
+  auto it = f.tensors.find(name);
+  if (it == f.tensors.end()) return fail(T0B_ERR_FORMAT, "gguf: missing tensor " + name);
+  const auto &t = it->second;
+  if (expect && t.n_elements != expect)
+    return fail(T0B_ERR_FORMAT, "gguf: tensor " + name + " has " + std::to_string(t.n_elements) +
+                                    " elements, expected " + std::to_string(expect));
+  std::vector<float> h(t.n_elements);
+  t0b::dequantize(t.type, t.data, t.n_elements, h.data());
+  void *d = nullptr;
+  if (cudaMalloc(&d, h.size() * 4) != cudaSuccess) return fail(T0B_ERR_OOM, "t0b: out of device memory");
+  m->allocs.push_back(d);
+  CUDA_TRY(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+  m->info.total_weight_bytes += h.size() * 4;
+  *dst = (const float *)d;
+  return T0B_OK;
+}
+
+t0b_status upload_q(t0b_model *m, const t0b::GgufFile &f, const std::string &name, int64_t rows, int64_t cols,
+                    const uint8_t **dst, int *shift) {
+  auto it = f.tensors.find(name);
+  if (it == f.tensors.end()) return fail(T0B_ERR_FORMAT, "gguf: missing tensor " + name);
+  const auto &t = it->second;
+  if (t.shape.size() != 2 || t.shape[0] != rows || t.shape[1] != cols)
+    return fail(T0B_ERR_FORMAT, "gguf: tensor " + name + " has an unexpected shape");
+  if (t.type != t0b::GG_Q8_0 && t.type != t0b::GG_Q4_0)
+    return fail(T0B_ERR_UNSUPPORTED, "t0b: tensor " + name +
+                                         " is not Q8_0/Q4_0; this engine keeps only quantized big matmuls resident");
+  void *d = nullptr;
+  // 16 extra bytes: vectorised tail reads past the last block stay in bounds
+  if (cudaMalloc(&d, t.nbytes + 16) != cudaSuccess) return fail(T0B_ERR_OOM, "t0b: out of device memory");
+  m->allocs.push_back(d);
+  CUDA_TRY(cudaMemcpy(d, t.data, t.nbytes, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemset((uint8_t *)d + t.nbytes, 0, 16));
+  m->info.quantizable_gpu_bytes += t.nbytes;
+  m->info.total_weight_bytes += t.nbytes;
+  *dst = (const uint8_t *)d;
+  // largest block scale of the matrix -> prescale exponent of the TC path
+  const int bpb = t.type == t0b::GG_Q8_0 ? 34 : 18;
+  float maxd = 0.0f;
+  for (size_t b = 0; b < t.n_elements / 32; ++b) {
+    uint16_t bits;
+    std::memcpy(&bits, t.data + b * bpb, 2);
+    maxd = std::max(maxd, std::fabs(t0b::f16_to_f32(bits)));
+  }
+  *shift = t0b_weight_shift(maxd, bpb == 34 ? 8 : 4);
+  return T0B_OK;
+}
+
+bool meta_u32(const t0b::GgufFile &f, const char *k, int32_t *v) {
+  auto it = f.meta.find(k);
+  if (it == f.meta.end() || it->second.type != 4) return false;
+  *v = (int32_t)it->second.u;
+  return true;
+}
+
+t0b_status parse_config(const t0b::GgufFile &f, t0b_model *m);
+t0b_status upload_all(t0b_model *m, const t0b::GgufFile &f);
+
+t0b_status load_model(t0b_model *m, const uint8_t *bytes, size_t len) {
+  t0b::GgufFile f;
+  std::string err;
+  if (!t0b::parse_gguf(bytes, len, f, err)) return fail(T0B_ERR_FORMAT, err);
+  t0b_status s = parse_config(f, m);
+  if (s != T0B_OK) return s;
+  return upload_all(m, f);
+}
+
+t0b_status parse_config(const t0b::GgufFile &f, t0b_model *m) {
+  // weights.rs:69-112 config_from_gguf_metadata
+  auto &I = m->info;
+  static const char *req[6] = {"t0.embed_dim", "t0.num_layers", "t0.num_heads", "t0.mlp_hidden_dim",
+                               "t0.patch_size", "t0.group_every_n"};
+  int32_t *dst[6] = {&I.embed_dim, &I.num_layers, &I.num_heads, &I.mlp_hidden_dim, &I.patch_size, &I.group_every_n};
+  for (int i = 0; i < 6; ++i)
+    if (!meta_u32(f, req[i], dst[i]))
+      return fail(T0B_ERR_FORMAT, std::string("gguf: missing or wrong-typed metadata key ") + req[i]);
+  auto q = f.meta.find("t0.quantile_levels");
+  if (q == f.meta.end() || q->second.type != 9) return fail(T0B_ERR_FORMAT, "gguf: missing t0.quantile_levels metadata");
+  if (q->second.arr.empty() || q->second.arr.size() > 32)
+    return fail(T0B_ERR_UNSUPPORTED, "t0b: 1..32 quantile levels supported");
+  I.n_quantiles = (int32_t)q->second.arr.size();
+  for (size_t i = 0; i < q->second.arr.size(); ++i) I.quantile_levels[i] = q->second.arr[i];
+  auto getf = [&](const char *k, float d) {
+    auto it = f.meta.find(k);
+    return (it != f.meta.end() && it->second.type == 6) ? it->second.f : d;
+  };
+  I.dropout = getf("t0.dropout", 0.0f);
+  I.scaler_eps = getf("t0.scaler_eps", 0.1f);
+  auto ab = f.meta.find("t0.scaler_use_arcsinh");
+  I.scaler_use_arcsinh = (ab != f.meta.end() && ab->second.type == 7) ? ab->second.b : 1;
+  auto em = f.meta.find("t0.scaler_eps_mode");
+  I.variance_offset = (em != f.meta.end() && em->second.type == 8) ? (em->second.s != "std_clamp") : 1;
+  I.weight_type = -1;
+
+  m->E = I.embed_dim;
+  m->H = I.num_heads;
+  m->F = I.mlp_hidden_dim;
+  m->P = I.patch_size;
+  m->nq = I.n_quantiles;
+  // config.rs:45-56: TIME x (n-1), GROUP; only whole blocks of n layers run
+  const int gen = I.group_every_n;
+  m->L = gen > 0 ? (I.num_layers / gen) * gen : I.num_layers;
+  if (m->P != 32) return fail(T0B_ERR_UNSUPPORTED, "t0b: patch_size must be 32");
+  if (m->H <= 0 || m->E % m->H || m->E / m->H != 64)
+    return fail(T0B_ERR_UNSUPPORTED, "t0b: head_dim must be 64 (embed_dim / num_heads)");
+  if (m->E % 256 || m->F % 256)
+    return fail(T0B_ERR_UNSUPPORTED, "t0b: embed_dim and mlp_hidden_dim must be multiples of 256");
+  if (m->H > 8) return fail(T0B_ERR_UNSUPPORTED, "t0b: at most 8 heads");
+  // every tensor the forward pass needs, with its shape and type
+  const int E = m->E, F = m->F, P = m->P, nq = m->nq;
+  auto need = [&](const std::string &name, int64_t r, int64_t c, bool quant) -> t0b_status {
+    auto it = f.tensors.find(name);
+    if (it == f.tensors.end()) return fail(T0B_ERR_FORMAT, "gguf: missing tensor " + name);
+    const auto &t = it->second;
+    const size_t ne = (size_t)r * (size_t)(c ? c : 1);
+    if (t.n_elements != ne || (c && (t.shape.size() != 2 || t.shape[0] != r || t.shape[1] != c)))
+      return fail(T0B_ERR_FORMAT, "gguf: tensor " + name + " has an unexpected shape");
+    if (quant) {
+      if (t.type != t0b::GG_Q8_0 && t.type != t0b::GG_Q4_0)
+        return fail(T0B_ERR_UNSUPPORTED, "t0b: tensor " + name +
+                                             " is not Q8_0/Q4_0; this engine keeps only quantized big matmuls resident");
+      if (m->info.weight_type == -1) m->info.weight_type = t.type;
+      if (t.type != m->info.weight_type) return fail(T0B_ERR_UNSUPPORTED, "t0b: mixed Q8_0/Q4_0 big matmuls");
+      m->info.quantizable_gpu_bytes += t.nbytes;
+    }
+    return T0B_OK;
+  };
+  t0b_status s;
+#define NEED(name, r, c, q) \
+  if ((s = need(name, r, c, q)) != T0B_OK) return s
+  NEED("patch_encoder.projection.mlp.hidden_layer.weight", E, 3 * P, false);
+  NEED("patch_encoder.projection.mlp.output_layer.weight", E, E, false);
+  NEED("patch_encoder.projection.residual_layer.weight", E, 3 * P, false);
+  NEED("patch_encoder.type_embeddings.weight", 3, E, false);
+  NEED("decoder.mlp.hidden_layer.weight", E, E, false);
+  NEED("decoder.mlp.output_layer.weight", P * nq, E, false);
+  NEED("decoder.residual_layer.weight", P * nq, E, false);
+  for (int l = 0; l < m->L; ++l) {
+    const std::string p = "transformer.layers." + std::to_string(l);
+    NEED(p + ".attention_block.attention.wQKV.weight", 3 * E, E, true);
+    NEED(p + ".attention_block.attention.wO.weight", E, E, true);
+    NEED(p + ".mlp.0.weight", 2 * F, E, true);
+    NEED(p + ".mlp.2.weight", E, F, true);
+  }
+#undef NEED
+  if (m->info.weight_type == -1) return fail(T0B_ERR_FORMAT, "gguf: model has no layers");
+  m->qt = m->info.weight_type == t0b::GG_Q8_0 ? 8 : 4;
+  return T0B_OK;
+}
+
+t0b_status upload_all(t0b_model *m, const t0b::GgufFile &f) {
+  const int E = m->E, F = m->F, P = m->P, nq = m->nq, gen = m->info.group_every_n;
+  m->info.quantizable_gpu_bytes = 0;
+  m->info.total_weight_bytes = 0;
+  t0b_status s;
+#define UP(name, ptr, n) \
+  if ((s = upload_f32(m, f, name, &(ptr), (n))) != T0B_OK) return s
+  UP("patch_encoder.projection.mlp.hidden_layer.weight", m->enc_hw, (size_t)E * 3 * P);
+  UP("patch_encoder.projection.mlp.hidden_layer.bias", m->enc_hb, (size_t)E);
+  UP("patch_encoder.projection.mlp.output_layer.weight", m->enc_ow, (size_t)E * E);
+  UP("patch_encoder.projection.mlp.output_layer.bias", m->enc_ob, (size_t)E);
+  UP("patch_encoder.projection.residual_layer.weight", m->enc_rw, (size_t)E * 3 * P);
+  UP("patch_encoder.projection.residual_layer.bias", m->enc_rb, (size_t)E);
+  UP("patch_encoder.type_embeddings.weight", m->temb, (size_t)3 * E);
+  UP("transformer.out_norm.scale", m->out_g, (size_t)E);
+  UP("decoder.mlp.hidden_layer.weight", m->dec_hw, (size_t)E * E);
+  UP("decoder.mlp.hidden_layer.bias", m->dec_hb, (size_t)E);
+  UP("decoder.mlp.output_layer.weight", m->dec_ow, (size_t)P * nq * E);
+  UP("decoder.mlp.output_layer.bias", m->dec_ob, (size_t)P * nq);
+  UP("decoder.residual_layer.weight", m->dec_rw, (size_t)P * nq * E);
+  UP("decoder.residual_layer.bias", m->dec_rb, (size_t)P * nq);
+  m->dec_out = P * nq;
+  m->enc_in = 3 * P;
+  for (int l = 0; l < m->L; ++l) {
+    LayerW w{};
+    const std::string p = "transformer.layers." + std::to_string(l);
+    w.group = gen > 0 && (l % gen) == gen - 1;
+    if ((s = upload_q(m, f, p + ".attention_block.attention.wQKV.weight", 3 * E, E, &w.wqkv, &w.sh_qkv)) != T0B_OK) return s;
+    if ((s = upload_q(m, f, p + ".attention_block.attention.wO.weight", E, E, &w.wo, &w.sh_o)) != T0B_OK) return s;
+    if ((s = upload_q(m, f, p + ".mlp.0.weight", 2 * F, E, &w.w0, &w.sh_0)) != T0B_OK) return s;
+    if ((s = upload_q(m, f, p + ".mlp.2.weight", E, F, &w.w2, &w.sh_2)) != T0B_OK) return s;
+    UP(p + ".attention_block.attention.wQKV.bias", w.bqkv, (size_t)3 * E);
+    UP(p + ".attention_block.attention.wO.bias", w.bo, (size_t)E);
+    UP(p + ".mlp.0.bias", w.b0, (size_t)2 * F);
+    UP(p + ".mlp.2.bias", w.b2, (size_t)E);
+    UP(p + ".attention_block.norm.scale", w.g_attn, (size_t)E);
+    UP(p + ".norm.scale", w.g_mlp, (size_t)E);
+    UP(p + ".attention_block.attention.q_norm.scale", w.qn, (size_t)64);
+    UP(p + ".attention_block.attention.k_norm.scale", w.kn, (size_t)64);
+    m->layers.push_back(w);
+  }
+#undef UP
+  return T0B_OK;
+}
+
+// RoPE tables for p patches, ops.rs:78-115 (f64 math, cast to f32).
+t0b_status rope_tables(t0b_model *m, int p, const float **out) {
+  auto it = m->rope.find(p);
+  if (it != m->rope.end()) {
+    *out = it->second;
+    return T0B_OK;
+  }
+  const int hd = 64, half = 32;
+  std::vector<float> h((size_t)3 * p * hd);
+  float *cs = h.data(), *sn = cs + (size_t)p * hd, *sc = sn + (size_t)p * hd;
+  const double theta = 10000.0, base512 = 512.0;
+  const double max_half = std::floor((double)(p - 1) / 2.0);
+  for (int pos = 0; pos < p; ++pos) {
+    const double power = ((double)pos - max_half) / base512;
+    for (int j = 0; j < half; ++j) {
+      const double inv_freq = 1.0 / std::pow(theta, (double)(2 * j) / (double)hd);
+      const double ang = (double)pos * inv_freq;
+      const double b = (2.0 * j + 0.4 * hd) / (1.4 * hd);
+      const float s = (float)std::pow(b, power);
+      cs[pos * hd + 2 * j] = cs[pos * hd + 2 * j + 1] = (float)std::cos(ang);  // interleaved pairs
+      sn[pos * hd + 2 * j] = sn[pos * hd + 2 * j + 1] = (float)std::sin(ang);
+      sc[pos * hd + j] = sc[pos * hd + half + j] = s;  // concatenated halves
+    }
+  }
+  float *d = nullptr;
+  if (cudaMalloc(&d, h.size() * 4) != cudaSuccess) return fail(T0B_ERR_OOM, "t0b: out of device memory");
+  CUDA_TRY(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+  m->rope[p] = d;
+  *out = d;
+  return T0B_OK;
+}
+
+// ------------------------------------------------------------------ passes
+struct Pass {
+  int R = 0, p = 0, hp = 0, horizon = 0;
+  std::vector<int64_t> row_off;
+  std::vector<int> row_len, row_lead, row_fv, s_row0, s_nrows;
+  const float *ctx = nullptr;  // device
+  float *out = nullptr;        // device [R, horizon, nq]
+};
+
+bool use_tc(const t0b_model *m, int M) { return M >= m->tc_min_tokens; }
+
+cudaError_t qgemm(t0b_model *m, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
+                  int wshift, Epi &epi) {
+  if (use_tc(m, M)) {
+    if (epi.kind == EPI_RESID) epi.ssq_out_nt = epi.N / 256;
+    return t0b_launch_gemm_tc(m->qt, ah, al, M, K, W, wrows, wshift, epi, m->d_err, m->stream);
+  }
+  if (epi.kind == EPI_RESID) epi.ssq_out_nt = epi.N / 64;
+  return t0b_launch_gemm_small(m->qt, ah, al, M, K, W, epi, m->d_err, m->stream);
+}
+
+t0b_status ensure_ws(t0b_model *m, size_t T, size_t R, size_t nout) {
+  const size_t E = m->E, F = m->F;
+  CUDA_TRY(m->x.reserve(T * E * 4));
+  CUDA_TRY(m->qkv.reserve(T * 3 * E * 4));
+  CUDA_TRY(m->feat.reserve(T * 96 * 4));
+  CUDA_TRY(m->ssq.reserve(T * 16 * 4));
+  CUDA_TRY(m->xh.reserve(T * E * 2));
+  CUDA_TRY(m->xl.reserve(T * E * 2));
+  CUDA_TRY(m->ah.reserve(T * E * 2));
+  CUDA_TRY(m->al.reserve(T * E * 2));
+  CUDA_TRY(m->hh.reserve(T * F * 2));
+  CUDA_TRY(m->hl.reserve(T * F * 2));
+  CUDA_TRY(m->xo.reserve(nout * E * 4));
+  CUDA_TRY(m->dhid.reserve(nout * E * 4));
+  CUDA_TRY(m->dout.reserve(nout * m->dec_out * 4));
+  CUDA_TRY(m->loc.reserve(nout * 4));
+  CUDA_TRY(m->scl.reserve(nout * 4));
+  (void)R;
+  return T0B_OK;
+}
+
+#define LAUNCH(expr)                                                                                    \
+  do {                                                                                                  \
+    cudaError_t e_ = (expr);                                                                            \
+    if (e_ != cudaSuccess) return fail(T0B_ERR_CUDA, std::string("launch failed: ") + cudaGetErrorString(e_)); \
+  } while (0)
+
+t0b_status run_pass(t0b_model *m, const Pass &ps) {
+  const int R = ps.R, p = ps.p, hp = ps.hp, E = m->E, F = m->F;
+  const size_t T = (size_t)R * p;
+  const int ns = (int)ps.s_row0.size();
+  if (T == 0) return T0B_OK;
+  // the previous pass must be done before buffers are grown or the pinned
+  // metadata staging buffer is rewritten
+  CUDA_TRY(cudaStreamSynchronize(m->stream));
+  t0b_status st = ensure_ws(m, T, R, (size_t)R * hp);
+  if (st != T0B_OK) return st;
+  // metadata: row_off (i64) | row_len | row_lead | row_fv | s_row0 | s_nrows,
+  // each section padded to 16 bytes
+  const size_t mbytes = (size_t)R * 20 + (size_t)ns * 8 + 256;
+  CUDA_TRY(m->meta.reserve(mbytes));
+  CUDA_TRY(m->hmeta.reserve(mbytes));
+  uint8_t *hb = (uint8_t *)m->hmeta.p;
+  size_t o = 0;
+  auto put = [&](const void *src, size_t n) {
+    std::memcpy(hb + o, src, n);
+    size_t at = o;
+    o += (n + 15) / 16 * 16;
+    return at;
+  };
+  const size_t o_off = put(ps.row_off.data(), (size_t)R * 8);
+  const size_t o_len = put(ps.row_len.data(), (size_t)R * 4);
+  const size_t o_lead = put(ps.row_lead.data(), (size_t)R * 4);
+  const size_t o_fv = put(ps.row_fv.data(), (size_t)R * 4);
+  const size_t o_s0 = put(ps.s_row0.data(), (size_t)ns * 4);
+  const size_t o_sn = put(ps.s_nrows.data(), (size_t)ns * 4);
+  CUDA_TRY(cudaMemcpyAsync(m->meta.p, hb, o, cudaMemcpyHostToDevice, m->stream));
+  uint8_t *db = (uint8_t *)m->meta.p;
+
+  const float *rope = nullptr;
+  if ((st = rope_tables(m, p, &rope)) != T0B_OK) return st;
+
+  // 1. pad + causal scaler + patch features
+  PrepArgs pa{};
+  pa.ctx = ps.ctx;
+  pa.row_off = (const int64_t *)(db + o_off);
+  pa.row_len = (const int *)(db + o_len);
+  pa.row_lead = (const int *)(db + o_lead);
+  pa.R = R;
+  pa.p = p;
+  pa.hp = hp;
+  pa.use_arcsinh = m->info.scaler_use_arcsinh;
+  pa.variance_offset = m->info.variance_offset;
+  pa.eps = m->info.scaler_eps;
+  pa.feat = m->feat.as<float>();
+  pa.out_loc = m->loc.as<float>();
+  pa.out_scale = m->scl.as<float>();
+  LAUNCH(t0b_launch_prep(pa, m->stream));
+
+  // 2. patch encoder: x = relu(f.hw^T+hb).ow^T + ob + f.rw^T + rb + type_emb[0]
+  float *x = m->x.as<float>();
+  float *hid = m->qkv.as<float>();  // scratch [T, E]
+  SgemmArgs g{};
+  g.A = m->feat.as<float>();
+  g.lda = 96;
+  g.B = m->enc_hw;
+  g.ldb = 96;
+  g.C = hid;
+  g.ldc = E;
+  g.M = (int)T;
+  g.N = E;
+  g.K = 96;
+  g.bias = m->enc_hb;
+  g.relu = 1;
+  LAUNCH(t0b_launch_sgemm(g, m->stream));
+  g.B = m->enc_rw;
+  g.C = x;
+  g.bias = m->enc_rb;
+  g.bias2 = m->enc_ob;
+  g.bias3 = m->temb;  // row 0: TARGET type embedding (every patch of a target row)
+  g.relu = 0;
+  LAUNCH(t0b_launch_sgemm(g, m->stream));
+  g.A = hid;
+  g.lda = E;
+  g.B = m->enc_ow;
+  g.ldb = E;
+  g.K = E;
+  g.bias = g.bias2 = g.bias3 = nullptr;
+  g.accumulate = 1;
+  LAUNCH(t0b_launch_sgemm(g, m->stream));
+  LAUNCH(t0b_launch_rownorm_split(x, m->layers[0].g_attn, m->xh.as<__half>(), m->xl.as<__half>(), m->ssq.as<float>(),
+                                  (int)T, E, m->stream));
+  int ssq_nt = 1;
+
+  AttnArgs aa{};
+  aa.qkv = m->qkv.as<float>();
+  aa.oh = m->ah.as<__half>();
+  aa.ol = m->al.as<__half>();
+  aa.row_first_valid = (const int *)(db + o_fv);
+  aa.series_row0 = (const int *)(db + o_s0);
+  aa.series_nrows = (const int *)(db + o_sn);
+  aa.R = R;
+  aa.p = p;
+  aa.E = E;
+  aa.H = m->H;
+  aa.n_series = ns;
+  const int M = (int)T;
+  const int resid_nt = use_tc(m, M) ? E / 256 : E / 64;
+
+  for (int l = 0; l < m->L; ++l) {
+    const LayerW &w = m->layers[l];
+    Epi e{};
+    e.kind = EPI_QKV;
+    e.M = M;
+    e.N = 3 * E;
+    e.bias = w.bqkv;
+    e.ssq_in = m->ssq.as<float>();
+    e.ssq_in_nt = ssq_nt;
+    e.ssq_dim = E;
+    e.y = m->qkv.as<float>();
+    e.qn = w.qn;
+    e.kn = w.kn;
+    e.rcos = rope;
+    e.rsin = rope + (size_t)p * 64;
+    e.rsc = rope + (size_t)2 * p * 64;
+    e.p = p;
+    e.E = E;
+    e.rope = w.group ? 0 : 1;
+    LAUNCH(qgemm(m, m->xh.as<__half>(), m->xl.as<__half>(), M, E, w.wqkv, 3 * E, w.sh_qkv, e));
+    LAUNCH(w.group ? t0b_launch_attn_group(aa, m->stream) : t0b_launch_attn_time(aa, m->stream));
+
+    Epi r{};
+    r.kind = EPI_RESID;
+    r.M = M;
+    r.N = E;
+    r.bias = w.bo;
+    r.x = x;
+    r.gnext = w.g_mlp;
+    r.xh = m->xh.as<__half>();
+    r.xl = m->xl.as<__half>();
+    r.ssq_out = m->ssq.as<float>();
+    LAUNCH(qgemm(m, m->ah.as<__half>(), m->al.as<__half>(), M, E, w.wo, E, w.sh_o, r));
+    ssq_nt = resid_nt;
+
+    Epi sg{};
+    sg.kind = EPI_SWIGLU;
+    sg.M = M;
+    sg.N = 2 * F;
+    sg.F = F;
+    sg.bias = w.b0;
+    sg.ssq_in = m->ssq.as<float>();
+    sg.ssq_in_nt = ssq_nt;
+    sg.ssq_dim = E;
+    sg.zh = m->hh.as<__half>();
+    sg.zl = m->hl.as<__half>();
+    LAUNCH(qgemm(m, m->xh.as<__half>(), m->xl.as<__half>(), M, E, w.w0, 2 * F, w.sh_0, sg));
+
+    Epi r2 = r;
+    r2.bias = w.b2;
+    r2.gnext = (l + 1 < m->L) ? m->layers[l + 1].g_attn : m->out_g;
+    LAUNCH(qgemm(m, m->hh.as<__half>(), m->hl.as<__half>(), M, F, w.w2, E, w.sh_2, r2));
+  }
+
+  // decoder on the output patches only: rmsnorm(out_norm) -> residual block
+  const int nout = R * hp;
+  LAUNCH(t0b_launch_dec_gather(x, m->out_g, m->xo.as<float>(), R, p, hp, E, m->stream));
+  SgemmArgs d{};
+  d.A = m->xo.as<float>();
+  d.lda = E;
+  d.B = m->dec_hw;
+  d.ldb = E;
+  d.C = m->dhid.as<float>();
+  d.ldc = E;
+  d.M = nout;
+  d.N = E;
+  d.K = E;
+  d.bias = m->dec_hb;
+  d.relu = 1;
+  LAUNCH(t0b_launch_sgemm(d, m->stream));
+  d.B = m->dec_rw;
+  d.C = m->dout.as<float>();
+  d.ldc = m->dec_out;
+  d.N = m->dec_out;
+  d.bias = m->dec_rb;
+  d.bias2 = m->dec_ob;
+  d.relu = 0;
+  LAUNCH(t0b_launch_sgemm(d, m->stream));
+  d.A = m->dhid.as<float>();
+  d.B = m->dec_ow;
+  d.bias = d.bias2 = nullptr;
+  d.accumulate = 1;
+  LAUNCH(t0b_launch_sgemm(d, m->stream));
+  LAUNCH(t0b_launch_dec_head(m->dout.as<float>(), m->loc.as<float>(), m->scl.as<float>(), ps.out, nullptr, R, hp,
+                             ps.horizon, m->nq, m->info.scaler_use_arcsinh, m->stream));
+  return T0B_OK;
+}
+
+t0b_status check_horizon(size_t horizon) {
+  if (horizon == 0) return fail(T0B_ERR_INVALID, "t0b: horizon must be >= 1");
+  if ((horizon + 31) / 32 * 32 > (size_t)kMaxHorizon)
+    return fail(T0B_ERR_INVALID,
+                "single-window forecast can't exceed max_horizon (1024) in one pass -- use forecast_rollout");
+  return T0B_OK;
+}
+
+t0b_status sync_model(t0b_model *m) {
+  CUDA_TRY(cudaStreamSynchronize(m->stream));
+  int herr = 0;
+  CUDA_TRY(cudaMemcpy(&herr, m->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (herr) {
+    cudaMemset(m->d_err, 0, sizeof(int));
+    return fail(T0B_ERR_DEVICE, "t0b: a kernel reported device error code " + std::to_string(herr));
+  }
+  return T0B_OK;
+}
+
+// One group of whole series into one or more passes.  rows: (ctx offset,
+// length) per variate row; series: consecutive row counts.  All rows of one
+// call share the padded context width `ctx_w` (a multiple of 32).
+struct RowSpec {
+  int64_t off;
+  int len;
+};
+
+t0b_status run_series(t0b_model *m, const float *ctx_dev, const std::vector<RowSpec> &rows,
+                      const std::vector<int> &series_nrows, int ctx_w, int horizon, float *out_dev,
+                      size_t max_rows_hint) {
+  const int hpad = (horizon + 31) / 32 * 32;
+  const int p = (ctx_w + hpad) / 32, hp = hpad / 32;
+  size_t max_rows = std::max<size_t>(1, m->max_tokens / (size_t)p);
+  if (max_rows_hint) max_rows = std::min(max_rows, max_rows_hint);
+  size_t s = 0, row = 0;
+  while (s < series_nrows.size()) {
+    Pass ps;
+    ps.p = p;
+    ps.hp = hp;
+    ps.horizon = horizon;
+    ps.ctx = ctx_dev;
+    size_t row0 = row;
+    while (s < series_nrows.size()) {
+      const int nv = series_nrows[s];
+      if (ps.R > 0 && (size_t)(ps.R + nv) > max_rows) break;
+      ps.s_row0.push_back(ps.R);
+      ps.s_nrows.push_back(nv);
+      for (int v = 0; v < nv; ++v, ++row) {
+        const RowSpec &rs = rows[row];
+        ps.row_off.push_back(rs.off);
+        ps.row_len.push_back(rs.len);
+        const int lead = ctx_w - rs.len;
+        ps.row_lead.push_back(lead);
+        ps.row_fv.push_back(lead / 32);
+      }
+      ps.R += nv;
+      ++s;
+    }
+    ps.out = out_dev + row0 * (size_t)horizon * m->nq;
+    t0b_status st = run_pass(m, ps);
+    if (st != T0B_OK) return st;
+  }
+  return T0B_OK;
+}
+
+struct Staged {
+  float *ctx;
+  float *out;
+};
+
+t0b_status stage_io(t0b_model *m, const float *ctx, size_t n_ctx, size_t n_out, Staged *sg) {
+  CUDA_TRY(m->ctx_stage.reserve(std::max<size_t>(n_ctx, 1) * 4));
+  CUDA_TRY(m->out_stage.reserve(std::max<size_t>(n_out, 1) * 4));
+  CUDA_TRY(cudaMemcpyAsync(m->ctx_stage.p, ctx, n_ctx * 4, cudaMemcpyHostToDevice, m->stream));
+  sg->ctx = m->ctx_stage.as<float>();
+  sg->out = m->out_stage.as<float>();
+  return T0B_OK;
+}
+
+t0b_status finish_io(t0b_model *m, const Staged &sg, float *out, size_t n_out) {
+  CUDA_TRY(cudaMemcpyAsync(out, sg.out, n_out * 4, cudaMemcpyDeviceToHost, m->stream));
+  return sync_model(m);
+}
+
+}  // namespace
+
+extern "C" t0b_status t0b_gguf_validate(const uint8_t *bytes, size_t len, t0b_model_info *out) {
+  if (!bytes || !out) return fail(T0B_ERR_INVALID, "t0b_gguf_validate: NULL argument");
+  t0b::GgufFile f;
+  std::string err;
+  if (!t0b::parse_gguf(bytes, len, f, err)) return fail(T0B_ERR_FORMAT, err);
+  t0b_model m;
+  t0b_status s = parse_config(f, &m);
+  if (s != T0B_OK) return s;
+  *out = m.info;
+  out->total_weight_bytes = 0;
+  return T0B_OK;
+}
+
+extern "C" t0b_status t0b_model_load_gguf(t0b_engine *e, const uint8_t *bytes, size_t len, t0b_model **out) {
+  if (!e || !bytes || !out) return fail(T0B_ERR_INVALID, "t0b_model_load_gguf: NULL argument");
+  *out = nullptr;
+  CUDA_TRY(cudaSetDevice(e->device));
+  std::unique_ptr<t0b_model> m(new t0b_model());
+  m->eng = e;
+  t0b_status s = load_model(m.get(), bytes, len);
+  if (s != T0B_OK) return s;
+  CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+  m->own_stream = true;
+  CUDA_TRY(cudaMalloc(&m->d_err, sizeof(int)));
+  CUDA_TRY(cudaMemset(m->d_err, 0, sizeof(int)));
+  *out = m.release();
+  return T0B_OK;
+}
+
+extern "C" void t0b_model_destroy(t0b_model *m) {
+  if (!m) return;
+  cudaSetDevice(m->eng->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  delete m;
+}
+
+extern "C" t0b_status t0b_model_info_get(const t0b_model *m, t0b_model_info *out) {
+  if (!m || !out) return fail(T0B_ERR_INVALID, "t0b_model_info_get: NULL argument");
+  *out = m->info;
+  return T0B_OK;
+}
+
+extern "C" t0b_status t0b_model_set_stream(t0b_model *m, void *stream) {
+  if (!m) return fail(T0B_ERR_INVALID, "t0b_model_set_stream: NULL model");
+  if (stream) {
+    if (m->own_stream && m->stream) cudaStreamDestroy(m->stream);
+    m->own_stream = false;
+    m->stream = (cudaStream_t)stream;
+  }
+  return T0B_OK;
+}
+
+extern "C" void *t0b_model_stream(const t0b_model *m) { return m ? (void *)m->stream : nullptr; }
+
+extern "C" t0b_status t0b_model_set_max_tokens(t0b_model *m, size_t max_tokens) {
+  if (!m || max_tokens < 64) return fail(T0B_ERR_INVALID, "t0b_model_set_max_tokens: need >= 64");
+  m->max_tokens = max_tokens;
+  return T0B_OK;
+}
+
+extern "C" t0b_status t0b_model_sync(t0b_model *m) {
+  if (!m) return fail(T0B_ERR_INVALID, "t0b_model_sync: NULL model");
+  CUDA_TRY(cudaSetDevice(m->eng->device));
+  return sync_model(m);
+}
+
+extern "C" t0b_status t0b_forecast_multiseries_device(t0b_model *m, const float *ctx_dev, const int32_t *n_variates,
+                                                      size_t n_series, size_t t_ctx, size_t horizon,
+                                                      float *out_dev) {
+  if (!m || !ctx_dev || !n_variates || !out_dev) return fail(T0B_ERR_INVALID, "t0b_forecast_multiseries: NULL argument");
+  t0b_status s = check_horizon(horizon);
+  if (s != T0B_OK) return s;
+  if (t_ctx == 0) return fail(T0B_ERR_INVALID, "t0b: context length must be >= 1");
+  CUDA_TRY(cudaSetDevice(m->eng->device));
+  const int pad_left = (int)((32 - t_ctx % 32) % 32);  // data.rs:112
+  std::vector<RowSpec> rows;
+  std::vector<int> nr;
+  int64_t off = 0;
+  for (size_t i = 0; i < n_series; ++i) {
+    if (n_variates[i] < 1) return fail(T0B_ERR_INVALID, "t0b: every series needs >= 1 variate");
+    nr.push_back(n_variates[i]);
+    for (int v = 0; v < n_variates[i]; ++v, off += (int64_t)t_ctx) rows.push_back({off, (int)t_ctx});
+  }
+  return run_series(m, ctx_dev, rows, nr, (int)t_ctx + pad_left, (int)horizon, out_dev, 0);
+}
+
+extern "C" t0b_status t0b_forecast_multiseries(t0b_model *m, const float *ctx, const int32_t *n_variates,
+                                               size_t n_series, size_t t_ctx, size_t horizon, float *out) {
+  if (!m || !ctx || !n_variates || !out) return fail(T0B_ERR_INVALID, "t0b_forecast_multiseries: NULL argument");
+  size_t rows = 0;
+  for (size_t i = 0; i < n_series; ++i) rows += (size_t)std::max(n_variates[i], 0);
+  CUDA_TRY(cudaSetDevice(m->eng->device));
+  Staged sg;
+  t0b_status s = stage_io(m, ctx, rows * t_ctx, rows * horizon * m->nq, &sg);
+  if (s != T0B_OK) return s;
+  s = t0b_forecast_multiseries_device(m, sg.ctx, n_variates, n_series, t_ctx, horizon, sg.out);
+  if (s != T0B_OK) return s;
+  return finish_io(m, sg, out, rows * horizon * m->nq);
+}
+
+extern "C" t0b_status t0b_forecast(t0b_model *m, const float *ctx, size_t v, size_t t_ctx, size_t horizon,
+                                   float *out) {
+  if (v == 0) return fail(T0B_ERR_INVALID, "t0b_forecast: v must be >= 1");
+  int32_t nv = (int32_t)v;
+  return t0b_forecast_multiseries(m, ctx, &nv, 1, t_ctx, horizon, out);
+}
+
+extern "C" t0b_status t0b_forecast_batch(t0b_model *m, const float *ctx, size_t n, size_t t_ctx, size_t horizon,
+                                         size_t chunk, float *out) {
+  if (!m || !ctx || !out) return fail(T0B_ERR_INVALID, "t0b_forecast_batch: NULL argument");
+  t0b_status s = check_horizon(horizon);
+  if (s != T0B_OK) return s;
+  if (t_ctx == 0) return fail(T0B_ERR_INVALID, "t0b: context length must be >= 1");
+  CUDA_TRY(cudaSetDevice(m->eng->device));
+  Staged sg;
+  if ((s = stage_io(m, ctx, n * t_ctx, n * horizon * m->nq, &sg)) != T0B_OK) return s;
+  const int pad_left = (int)((32 - t_ctx % 32) % 32);
+  std::vector<RowSpec> rows(n);
+  std::vector<int> nr(n, 1);  // data.rs:96-105: a distinct group per signal
+  for (size_t i = 0; i < n; ++i) rows[i] = {(int64_t)(i * t_ctx), (int)t_ctx};
+  if ((s = run_series(m, sg.ctx, rows, nr, (int)t_ctx + pad_left, (int)horizon, sg.out, chunk)) != T0B_OK) return s;
+  return finish_io(m, sg, out, n * horizon * m->nq);
+}
+
+extern "C" t0b_status t0b_forecast_batch_rows(t0b_model *m, const float *ctx, const size_t *lengths, size_t n,
+                                              size_t horizon, size_t chunk, float *out) {
+  if (!m || !ctx || !lengths || !out) return fail(T0B_ERR_INVALID, "t0b_forecast_batch_rows: NULL argument");
+  t0b_status s = check_horizon(horizon);
+  if (s != T0B_OK) return s;
+  size_t total = 0;
+  for (size_t i = 0; i < n; ++i) {
+    if (lengths[i] == 0) return fail(T0B_ERR_INVALID, "t0b_forecast_batch_rows: empty row");
+    total += lengths[i];
+  }
+  CUDA_TRY(cudaSetDevice(m->eng->device));
+  Staged sg;
+  if ((s = stage_io(m, ctx, total, n * horizon * m->nq, &sg)) != T0B_OK) return s;
+  // lib.rs:183-240: each chunk is padded to its common patch-aligned width
+  const size_t cs = (chunk == 0 || chunk > n) ? n : chunk;
+  int64_t off = 0;
+  for (size_t start = 0; start < n; start += cs) {
+    const size_t k = std::min(cs, n - start);
+    int common = 0;
+    for (size_t i = 0; i < k; ++i) common = std::max(common, (int)((lengths[start + i] + 31) / 32 * 32));
+    std::vector<RowSpec> rows(k);
+    std::vector<int> nr(k, 1);
+    for (size_t i = 0; i < k; ++i) {
+      rows[i] = {off, (int)lengths[start + i]};
+      off += (int64_t)lengths[start + i];
+    }
+    if ((s = run_series(m, sg.ctx, rows, nr, common, (int)horizon, sg.out + start * horizon * m->nq, 0)) != T0B_OK)
+      return s;
+  }
+  return finish_io(m, sg, out, n * horizon * m->nq);
+}
+
+// ======================================================= standalone GEMMs
+namespace {
+t0b_status split_input(t0b_engine *e, const float *x, size_t n, cudaStream_t st) {
+  CUDA_TRY(e->scratch_xh.reserve(n * 2));
+  CUDA_TRY(e->scratch_xl.reserve(n * 2));
+  CUDA_TRY(t0b_launch_split_f32(x, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), n, st));
+  return T0B_OK;
+}
+int qt_of(int ggml_type) { return ggml_type == T0B_Q8_0 ? 8 : (ggml_type == T0B_Q4_0 ? 4 : 0); }
+
+// Prescale exponent of a device-resident weight matrix (one reduction + copy).
+t0b_status device_weight_shift(t0b_engine *e, int qt, const uint8_t *W, size_t n_elements, cudaStream_t st,
+                               int *shift) {
+  CUDA_TRY(e->scratch_red.reserve(sizeof(unsigned int)));
+  const int bpb = qt == 8 ? 34 : 18;
+  CUDA_TRY(t0b_launch_absmax_scale(W, n_elements / 32, bpb, e->scratch_red.as<unsigned int>(), st));
+  unsigned int bits = 0;
+  CUDA_TRY(cudaMemcpyAsync(&bits, e->scratch_red.p, sizeof(bits), cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  float maxd;
+  std::memcpy(&maxd, &bits, 4);
+  *shift = t0b_weight_shift(maxd, qt);
+  return T0B_OK;
+}
+
+cudaError_t engine_qgemm(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
+                         int wshift, Epi &epi, int *err, cudaStream_t st) {
+  const bool tc = M >= 128;
+  if (tc) return t0b_launch_gemm_tc(qt, ah, al, M, K, W, wrows, wshift, epi, err, st);
+  return t0b_launch_gemm_small(qt, ah, al, M, K, W, epi, err, st);
+}
+
+t0b_status engine_check(t0b_engine *e, cudaStream_t st) {
+  CUDA_TRY(cudaStreamSynchronize(st));
+  int herr = 0;
+  CUDA_TRY(cudaMemcpy(&herr, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (herr) {
+    cudaMemset(e->d_err, 0, sizeof(int));
+    return fail(T0B_ERR_DEVICE, "t0b: a kernel reported device error code " + std::to_string(herr));
+  }
+  return T0B_OK;
+}
+}  // namespace
+
+extern "C" t0b_status t0b_gemm_q(t0b_engine *e, int ggml_type, const void *w_dev, int N, int K, const float *x_dev,
+                                 int M, const float *bias_dev, float *y_dev, void *stream) {
+  if (!e || !w_dev || !x_dev || !y_dev) return fail(T0B_ERR_INVALID, "t0b_gemm_q: NULL argument");
+  const int qt = qt_of(ggml_type);
+  if (!qt) return fail(T0B_ERR_UNSUPPORTED, "t0b_gemm_q: weight type must be Q8_0 or Q4_0");
+  if (M < 1 || N < 1 || K < 1) return fail(T0B_ERR_INVALID, "t0b_gemm_q: empty shape");
+  if (K % 256) return fail(T0B_ERR_UNSUPPORTED, "t0b_gemm_q: K must be a multiple of 256");
+  if (N % 256) return fail(T0B_ERR_UNSUPPORTED, "t0b_gemm_q: N must be a multiple of 256");
+  CUDA_TRY(cudaSetDevice(e->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  t0b_status s = split_input(e, x_dev, (size_t)M * K, st);
+  if (s != T0B_OK) return s;
+  int sh = 0;
+  if ((s = device_weight_shift(e, qt, (const uint8_t *)w_dev, (size_t)N * K, st, &sh)) != T0B_OK) return s;
+  Epi ep{};
+  ep.kind = EPI_PLAIN;
+  ep.M = M;
+  ep.N = N;
+  ep.bias = bias_dev;
+  ep.y = y_dev;
+  ep.ldy = N;
+  CUDA_TRY(engine_qgemm(qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, (const uint8_t *)w_dev, N,
+                        sh, ep, e->d_err, st));
+  return engine_check(e, st);
+}
+
+extern "C" t0b_status t0b_swiglu_q(t0b_engine *e, int ggml_type, const void *w0_dev, const void *w2_dev, int F, int K,
+                                   int N2, const float *x_dev, int M, const float *b0_dev, const float *b2_dev,
+                                   float *z_dev, float *y_dev, void *stream) {
+  if (!e || !w0_dev || !w2_dev || !x_dev || !y_dev) return fail(T0B_ERR_INVALID, "t0b_swiglu_q: NULL argument");
+  const int qt = qt_of(ggml_type);
+  if (!qt) return fail(T0B_ERR_UNSUPPORTED, "t0b_swiglu_q: weight type must be Q8_0 or Q4_0");
+  if (M < 1 || F < 1 || K < 1 || N2 < 1) return fail(T0B_ERR_INVALID, "t0b_swiglu_q: empty shape");
+  if (K % 256 || F % 256 || N2 % 256)
+    return fail(T0B_ERR_UNSUPPORTED, "t0b_swiglu_q: K, F and N2 must be multiples of 256");
+  CUDA_TRY(cudaSetDevice(e->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  t0b_status s = split_input(e, x_dev, (size_t)M * K, st);
+  if (s != T0B_OK) return s;
+  int sh0 = 0, sh2 = 0;
+  if ((s = device_weight_shift(e, qt, (const uint8_t *)w0_dev, (size_t)2 * F * K, st, &sh0)) != T0B_OK) return s;
+  if ((s = device_weight_shift(e, qt, (const uint8_t *)w2_dev, (size_t)N2 * F, st, &sh2)) != T0B_OK) return s;
+  CUDA_TRY(e->scratch_zh.reserve((size_t)M * F * 2));
+  CUDA_TRY(e->scratch_zl.reserve((size_t)M * F * 2));
+  Epi sg{};
+  sg.kind = EPI_SWIGLU;
+  sg.M = M;
+  sg.N = 2 * F;
+  sg.F = F;
+  sg.bias = b0_dev;
+  sg.zh = e->scratch_zh.as<__half>();
+  sg.zl = e->scratch_zl.as<__half>();
+  sg.z32 = z_dev;
+  CUDA_TRY(engine_qgemm(qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, (const uint8_t *)w0_dev,
+                        2 * F, sh0, sg, e->d_err, st));
+  Epi dn{};
+  dn.kind = EPI_PLAIN;
+  dn.M = M;
+  dn.N = N2;
+  dn.bias = b2_dev;
+  dn.y = y_dev;
+  dn.ldy = N2;
+  CUDA_TRY(engine_qgemm(qt, e->scratch_zh.as<__half>(), e->scratch_zl.as<__half>(), M, F, (const uint8_t *)w2_dev, N2,
+                        sh2, dn, e->d_err, st));
+  return engine_check(e, st);
+}
+
+// ============================================================ host codecs
+extern "C" size_t t0b_row_bytes(int ggml_type, size_t n) { return t0b::row_bytes(ggml_type, n); }
+
+extern "C" t0b_status t0b_quantize(int ggml_type, const float *x, size_t n, uint8_t *out) {
+  if (!x || !out) return fail(T0B_ERR_INVALID, "t0b_quantize: NULL argument");
+  if (n % 32) return fail(T0B_ERR_INVALID, "t0b_quantize: n must be a multiple of 32");
+  if (ggml_type == T0B_Q8_0)
+    t0b::quantize_q8_0(x, n, out);
+  else if (ggml_type == T0B_Q4_0)
+    t0b::quantize_q4_0(x, n, out);
+  else
+    return fail(T0B_ERR_UNSUPPORTED, "t0b_quantize: type must be Q8_0 or Q4_0");
+  return T0B_OK;
+}
+
+extern "C" t0b_status t0b_dequantize(int ggml_type, const uint8_t *bytes, size_t n, float *out) {
+  if (!bytes || !out) return fail(T0B_ERR_INVALID, "t0b_dequantize: NULL argument");
+  if ((ggml_type == T0B_Q8_0 || ggml_type == T0B_Q4_0) && n % 32)
+    return fail(T0B_ERR_INVALID, "t0b_dequantize: n must be a multiple of 32");
+  if (ggml_type != T0B_F32 && ggml_type != T0B_F16 && ggml_type != T0B_Q8_0 && ggml_type != T0B_Q4_0)
+    return fail(T0B_ERR_UNSUPPORTED, "t0b_dequantize: unsupported type");
+  t0b::dequantize(ggml_type, bytes, n, out);
+  return T0B_OK;
+}
+
+extern "C" t0b_status t0b_export_gguf(size_t n, const char *const *names, const int32_t *ndims, const int64_t *shapes,
+                                      const float *const *data, int big_type, const t0b_model_info *cfg, uint8_t *out,
+                                      size_t *out_len) {
+  if (!names || !ndims || !shapes || !data || !cfg || !out_len)
+    return fail(T0B_ERR_INVALID, "t0b_export_gguf: NULL argument");
+  if (big_type != T0B_F16 && big_type != T0B_Q8_0 && big_type != T0B_Q4_0)
+    return fail(T0B_ERR_UNSUPPORTED, "t0b_export_gguf: big_type must be F16, Q8_0 or Q4_0");
+  std::vector<t0b::ExportTensor> ts(n);
+  for (size_t i = 0; i < n; ++i) {
+    if (ndims[i] < 1 || ndims[i] > 2) return fail(T0B_ERR_INVALID, "t0b_export_gguf: tensors must be 1-D or 2-D");
+    ts[i].name = names[i];
+    ts[i].shape.assign(shapes + 2 * i, shapes + 2 * i + ndims[i]);
+    ts[i].data = data[i];
+    const bool q = ndims[i] == 2 && (big_type == T0B_Q8_0 || big_type == T0B_Q4_0);
+    if (q && ts[i].n_elements() % 32) return fail(T0B_ERR_INVALID, "t0b_export_gguf: quantized tensor size % 32 != 0");
+  }
+  t0b::ModelMeta mm;
+  mm.embed_dim = cfg->embed_dim;
+  mm.num_layers = cfg->num_layers;
+  mm.num_heads = cfg->num_heads;
+  mm.mlp_hidden_dim = cfg->mlp_hidden_dim;
+  mm.patch_size = cfg->patch_size;
+  mm.group_every_n = cfg->group_every_n;
+  mm.dropout = cfg->dropout;
+  mm.quantile_levels.assign(cfg->quantile_levels, cfg->quantile_levels + cfg->n_quantiles);
+  mm.scaler_use_arcsinh = cfg->scaler_use_arcsinh != 0;
+  mm.scaler_eps = cfg->scaler_eps;
+  mm.variance_offset = cfg->variance_offset != 0;
+  std::vector<uint8_t> b = t0b::export_gguf(ts, big_type, mm);
+  if (!out) {
+    *out_len = b.size();
+    return T0B_OK;
+  }
+  if (*out_len < b.size()) return fail(T0B_ERR_INVALID, "t0b_export_gguf: output buffer too small");
+  std::memcpy(out, b.data(), b.size());
+  *out_len = b.size();
+  return T0B_OK;
+}

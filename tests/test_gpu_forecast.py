@@ -1,0 +1,113 @@
+"""End-to-end forecast parity on the GPU against the C oracle (t0-core
+restatement), on the same GGUF bytes and the same seeded inputs.
+
+Tolerance: quantile outputs within 1e-3 max-abs after
+the model's own scaling.  Quantiles of the random-init model reach ~200, so
+1e-3 is ~5e-6 relative: f32-class arithmetic is required end to end.
+"""
+import numpy as np
+import pytest
+
+from t0_web_b200 import T0bError, synthetic as S, t0_fast
+
+from conftest import max_abs
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+@pytest.mark.parametrize("quant", ["q8_0", "q4_0"])
+def test_single_forecast_config1(engine, gpu_model, oracle_model, quant):
+    """Configuration 1: univariate sine (period 24) + 0.1 N(0,1), ctx 512, h 96."""
+    ctx = S.sine_context(512, seed=0)
+    got = t0_fast.forecast(engine, gpu_model(quant), ctx, 1, 512, 96)
+    ref = oracle_model(quant).forecast(ctx, 96)
+    assert got.shape == (1, 96, 5)
+    assert np.isfinite(got).all()
+    assert max_abs(got, ref) <= TOL
+
+
+def test_multivariate_joint(engine, gpu_model, oracle_model):
+    ctx, _ = S.multiseries(1, 512, seed=1, n_variates=3)
+    got = t0_fast.forecast(engine, gpu_model("q8_0"), ctx, 3, 512, 96)
+    ref = oracle_model("q8_0").forecast(ctx, 96)
+    assert max_abs(got, ref) <= TOL
+
+
+def test_batch_chunked(engine, gpu_model, oracle_model):
+    ctx = np.concatenate([S.sine_context(300, seed=s) for s in range(5)])
+    got = t0_fast.forecast_batch_chunked(engine, gpu_model("q8_0"), ctx, 5, 300, 64, chunk_size=2)
+    ref = oracle_model("q8_0").forecast_batch(ctx, 64, chunk=2)
+    assert max_abs(got, ref) <= TOL
+
+
+def test_batch_rows_ragged(engine, gpu_model, oracle_model):
+    rng = np.random.default_rng(5)
+    lengths = [100, 512, 37, 250, 64]
+    rows = [rng.standard_normal(n).astype(np.float32).cumsum() * 0.1 for n in lengths]
+    rows[2][5:9] = np.nan
+    got = t0_fast.forecast_batch_rows_chunked(engine, gpu_model("q8_0"), np.concatenate(rows), lengths, 40,
+                                              chunk_size=3)
+    ref = oracle_model("q8_0").forecast_batch_rows(rows, 40, chunk=3)
+    assert max_abs(got, ref) <= TOL
+
+
+@pytest.mark.parametrize("quant", ["q8_0", "q4_0"])
+def test_multiseries_gaps_tensor_core_path(engine, gpu_model, oracle_model, quant):
+    """Configuration-4 style series (2-3 sinusoids + trend + noise, 5% NaN gap),
+    enough tokens (6 x 3 x 67 = 1206) for the tcgen05 GEMM path."""
+    ctx, nv = S.multiseries(6, 2048, seed=2, n_variates=3)
+    got = t0_fast.forecast_multiseries(engine, gpu_model(quant), ctx, nv, 2048, 96)
+    ref = oracle_model(quant).forecast_multiseries(ctx, nv, 96, threads=8)
+    assert np.isfinite(got).all()
+    assert max_abs(got, ref) <= TOL
+
+
+def test_multiseries_ragged_variates(engine, gpu_model, oracle_model):
+    ctx, nv = S.multiseries(9, 512, seed=3, n_variates=(1, 8))
+    got = t0_fast.forecast_multiseries(engine, gpu_model("q8_0"), ctx, nv, 512, 96)
+    ref = oracle_model("q8_0").forecast_multiseries(ctx, nv, 96, threads=8)
+    assert max_abs(got, ref) <= TOL
+
+
+def test_unaligned_context_and_horizon(engine, gpu_model, oracle_model):
+    ctx = S.sine_context(77, seed=9)
+    got = t0_fast.forecast(engine, gpu_model("q8_0"), ctx, 1, 77, 30)
+    ref = oracle_model("q8_0").forecast(ctx, 30)
+    assert got.shape == (1, 30, 5)
+    assert max_abs(got, ref) <= TOL
+
+
+def test_all_missing_row(engine, gpu_model, oracle_model):
+    ctx, _ = S.multiseries(1, 256, seed=4, n_variates=2)
+    ctx[1, :] = np.nan
+    got = t0_fast.forecast(engine, gpu_model("q8_0"), ctx, 2, 256, 32)
+    ref = oracle_model("q8_0").forecast(ctx, 32)
+    assert np.isfinite(got).all()
+    assert max_abs(got, ref) <= TOL
+
+
+def test_chunking_is_invisible(engine, gpu_model):
+    """Passes split by the token budget give the same result as one pass."""
+    m = gpu_model("q8_0")
+    ctx, nv = S.multiseries(12, 512, seed=6, n_variates=(1, 4))
+    one = t0_fast.forecast_multiseries(engine, m, ctx, nv, 512, 96)
+    m.set_max_tokens(64)
+    try:
+        many = t0_fast.forecast_multiseries(engine, m, ctx, nv, 512, 96)
+    finally:
+        m.set_max_tokens(262144)
+    assert max_abs(one, many) <= TOL
+
+
+def test_horizon_limit_is_an_error(engine, gpu_model):
+    with pytest.raises(T0bError):
+        t0_fast.forecast(engine, gpu_model("q8_0"), S.sine_context(64), 1, 64, 1025)
+
+
+def test_model_bytes(gpu_model):
+    m = gpu_model("q8_0")
+    assert m.quantizable_gpu_bytes() == 106_954_752  # 100,663,296 values x 34/32
+    assert gpu_model("q4_0").quantizable_gpu_bytes() == 56_623_104
+    assert m.total_weight_bytes() > m.quantizable_gpu_bytes()
