@@ -111,6 +111,25 @@ t0b_status t0b_forecast_multiseries_device(t0b_model *m, const float *ctx_dev, c
 /* Block until the model's stream is idle and report any kernel-side error. */
 t0b_status t0b_model_sync(t0b_model *m);
 
+/* ---- measurement (no reference counterpart: the reference times whole
+ * forecasts with Instant, main.rs:719-740) ----
+ * With profiling on, every kernel launch of the model is bracketed by CUDA
+ * events on the model's stream; t0b_model_profile_read synchronizes and
+ * returns, per kernel class, launches, total device time and algorithmic
+ * work.  Classes: 0 gemm_tc, 1 gemm_small, 2 attn_time, 3 attn_group, 4 prep,
+ * 5 sgemm, 6 other. */
+typedef struct {
+  char name[16];
+  uint64_t launches;
+  double total_ms;
+  double flops; /* algorithmic (useful) FLOPs summed over launches */
+  double bytes; /* algorithmic HBM bytes summed over launches */
+} t0b_kernel_stats;
+t0b_status t0b_model_profile_enable(t0b_model *m, int on); /* also resets the statistics */
+t0b_status t0b_model_profile_read(t0b_model *m, t0b_kernel_stats *out, int max_classes, int *n_classes);
+/* Kernel launches issued by this model since it was created. */
+uint64_t t0b_model_launch_count(const t0b_model *m);
+
 /* ---- standalone dequant-GEMMs (device pointers, model-independent) ----
  * y[M,N] = x[M,K] . deq(W)[N,K]^T (+ bias[N]); W is raw Q8_0/Q4_0 blocks in
  * llama.cpp layout, row n at n * (K/32) * block_bytes.  Replaces t0-fast's

@@ -20,8 +20,14 @@ EXPORTED = [
     "t0b_model_info_get", "t0b_model_set_stream", "t0b_model_stream", "t0b_model_set_max_tokens",
     "t0b_forecast", "t0b_forecast_batch", "t0b_forecast_batch_rows", "t0b_forecast_multiseries",
     "t0b_forecast_multiseries_device", "t0b_model_sync", "t0b_gemm_q", "t0b_swiglu_q", "t0b_gguf_validate",
-    "t0b_quantize", "t0b_dequantize", "t0b_row_bytes", "t0b_export_gguf",
+    "t0b_quantize", "t0b_dequantize", "t0b_row_bytes", "t0b_export_gguf", "t0b_model_profile_enable",
+    "t0b_model_profile_read", "t0b_model_launch_count",
 ]
+
+
+class KernelStats(C.Structure):
+    _fields_ = [("name", C.c_char * 16), ("launches", C.c_uint64), ("total_ms", C.c_double),
+                ("flops", C.c_double), ("bytes", C.c_double)]
 
 
 class ModelInfo(C.Structure):
@@ -77,6 +83,10 @@ def lib() -> C.CDLL:
     L.t0b_row_bytes.argtypes = [st, sz]
     L.t0b_row_bytes.restype = sz
     L.t0b_export_gguf.argtypes = [sz, vp, vp, vp, vp, st, C.POINTER(ModelInfo), vp, C.POINTER(sz)]
+    L.t0b_model_profile_enable.argtypes = [vp, C.c_int]
+    L.t0b_model_profile_read.argtypes = [vp, C.POINTER(KernelStats), C.c_int, C.POINTER(C.c_int)]
+    L.t0b_model_launch_count.argtypes = [vp]
+    L.t0b_model_launch_count.restype = C.c_uint64
     _lib = L
     return L
 

@@ -141,6 +141,22 @@ T0B_DEV uint64_t sw128_desc(uint32_t saddr) {
   d |= (uint64_t)2 << 61;             // SWIZZLE_128B
   return d;
 }
+// Same for a 64-byte swizzle: rows of 64 B (32 f16), 8-row atoms of 512 B
+// stacked at a stride of 512 B.
+T0B_DEV uint64_t sw64_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(512u >> 4) << 32;   // stride byte offset: next 8-row atom
+  d |= (uint64_t)1 << 46;             // descriptor version for tcgen05
+  d |= (uint64_t)4 << 61;             // SWIZZLE_64B
+  return d;
+}
+// Byte offset of element (row r, k) in a K-major SW64 tile of 32-wide rows:
+// the 16-byte chunk index is XORed with bits 1-2 of the row.
+T0B_DEV uint32_t sw64_offset(uint32_t r, uint32_t k) {
+  return (r >> 3) * 512u + (r & 7u) * 64u + ((((k >> 3) ^ (r >> 1)) & 3u) << 4) + (k & 7u) * 2u;
+}
 // Instruction descriptor, kind::f16: f16 A and B, f32 D, both K-major.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
   return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
@@ -187,6 +203,39 @@ T0B_DEV uint32_t nib2_to_h2(uint32_t w, int hi) {
   __half2 h = *reinterpret_cast<__half2 *>(&u);
   h = __hsub2(h, __halves2half2(__float2half_rn(1032.0f), __float2half_rn(1032.0f)));
   return *reinterpret_cast<uint32_t *>(&h);
+}
+// Four int8 values (one 32-bit word) -> two f16x2 words, exactly.
+T0B_DEV void i8x4_to_h2x2(uint32_t w, uint32_t &lo, uint32_t &hi) {
+  const uint32_t x = w ^ 0x80808080u;                 // q + 128 per byte
+  uint32_t a = __byte_perm(x, 0x64646464u, 0x5140u);  // bytes 0,1 -> 1024 + q + 128
+  uint32_t b = __byte_perm(x, 0x64646464u, 0x5342u);  // bytes 2,3
+  const __half2 k = __halves2half2(__float2half_rn(1152.0f), __float2half_rn(1152.0f));
+  __half2 ha = __hsub2(*reinterpret_cast<__half2 *>(&a), k);
+  __half2 hb = __hsub2(*reinterpret_cast<__half2 *>(&b), k);
+  lo = *reinterpret_cast<uint32_t *>(&ha);
+  hi = *reinterpret_cast<uint32_t *>(&hb);
+}
+// Eight nibbles of one word (bytes b0..b3) -> four f16x2 words of (n - 8):
+// low nibbles of (b0,b1), (b2,b3) then high nibbles of (b0,b1), (b2,b3).
+T0B_DEV void nib8_to_h2x4(uint32_t w, uint32_t *out) {
+  const uint32_t l = w & 0x0F0F0F0Fu, h = (w >> 4) & 0x0F0F0F0Fu;
+  uint32_t r[4] = {__byte_perm(l, 0x64646464u, 0x5140u), __byte_perm(l, 0x64646464u, 0x5342u),
+                   __byte_perm(h, 0x64646464u, 0x5140u), __byte_perm(h, 0x64646464u, 0x5342u)};
+  const __half2 k = __halves2half2(__float2half_rn(1032.0f), __float2half_rn(1032.0f));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 v = __hsub2(*reinterpret_cast<__half2 *>(&r[i]), k);
+    out[i] = *reinterpret_cast<uint32_t *>(&v);
+  }
+}
+// Register reconfiguration for warp-specialized kernels (whole warpgroup).
+template <int N>
+T0B_DEV void regs_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+T0B_DEV void regs_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 // f32 -> (hi, lo) f16 pair with hi + lo == x to about 2^-22 relative.
 T0B_DEV void split_f16(float x, __half &hi, __half &lo) {

@@ -3,23 +3,34 @@
 //
 // Y[M, N] = A[M, K] . deq(W)[N, K]^T with f32-class accuracy from f16 MMAs:
 //   A = Ah + Al (two f16 terms, written by the producing kernel) and
-//   W = Wh + Wl (two f16 terms from the exact product d * q, made here);
-//   D = Ah.Wh + Ah.Wl + Al.Wh accumulated in f32 in tensor memory (the
-//   dropped Al.Wl term is ~2^-22 relative).  Single-term f16 or bf16 MMAs
-//   miss the 1e-3 quantile tolerance on t0-alpha-shaped models.
+//   W = Wh + Wl (two f16 terms from the exact product 2^s d q, made here);
+//   D = Ah.Wh (main accumulator) + [Ah.Wl + Al.Wh] (correction accumulator),
+//   both f32 in tensor memory.  The dropped Al.Wl term is ~2^-22 relative.
+//   Single-term f16 or bf16 MMAs miss the 1e-3 quantile tolerance on
+//   t0-alpha-shaped models, and chaining all three terms into one
+//   accumulator triples the tensor core's accumulation error.
 //
-// CTA tile 128 tokens x 256 weight rows, 64 K-values per pipeline stage,
-// two stages.  Warp roles (192 threads):
-//   warp 0      TMA producer: Ah/Al tiles (128x64 f16, 128-byte swizzle) and
-//               the raw blocks of the 256 weight rows (one 32-value block
-//               column per load, 16-byte aligned superset of the 34/18-byte
-//               block), both with mbarrier completion.
-//   warp 1      allocates 256 TMEM columns; lane 0 issues tcgen05.mma and
+// Persistent kernel: one CTA per SM walks a queue of 128-token x 256-row
+// output tiles (weight-row tiles fastest so the CTAs in flight share their
+// activation tiles in L2).  One 32-value block column of K per pipeline
+// stage; separate rings for the activation tiles (TMA, 64-byte swizzle), the
+// raw weight blocks (TMA) and the dequantized weight tiles.  The two
+// accumulators fill all 512 TMEM columns, so the epilogue drains them into
+// registers first and hands TMEM back to the MMA warp before doing its math
+// and stores, which then overlap the next tile's MMAs.
+//
+// Warp roles (512 threads, four warpgroups, registers rebalanced with
+// setmaxnreg):
+//   warp 0      TMA producer: Ah/Al tiles and the raw blocks of the tile's
+//               weight rows (16-byte aligned superset window of the 34/18-byte
+//               block), with mbarrier completion.
+//   warp 1      allocates 512 TMEM columns; lane 0 issues tcgen05.mma and
 //               tcgen05.commit.
-//   warps 2-5   dequantize raw blocks -> Wh/Wl tiles in the canonical K-major
-//               SW128 layout (generic stores + proxy fence), then run the
-//               fused epilogue from TMEM (tcgen05.ld, one token row per
-//               thread).
+//   warps 4-7   dequantize raw blocks -> Wh/Wl tiles in the canonical K-major
+//               SW64 layout (generic stores + proxy fence).
+//   warps 8-15  epilogue, two warps per TMEM lane quadrant (128 columns
+//               each): fused bias / RMSNorm row scale / QK-norm + RoPE /
+//               residual / SwiGLU, 16-byte stores.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -27,14 +38,16 @@
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 2;
-constexpr uint32_t X_TILE = BM * BK * 2;  // 16 KB
-constexpr uint32_t W_TILE = BN * BK * 2;  // 32 KB
+constexpr int BM = 128, BN = 256, BK = 32;  // BK: one Q8_0/Q4_0 block column of K per stage
+constexpr int XS = 5, WS = 3, RS = 3;
+constexpr int NTHREADS = 512;
+constexpr uint32_t X_TILE = BM * BK * 2;  // 8 KB, one of hi / lo
+constexpr uint32_t W_TILE = BN * BK * 2;  // 16 KB, one of hi / lo
 constexpr uint32_t OFF_XH = 0;
-constexpr uint32_t OFF_XL = OFF_XH + STAGES * X_TILE;
-constexpr uint32_t OFF_WH = OFF_XL + STAGES * X_TILE;
-constexpr uint32_t OFF_WL = OFF_WH + STAGES * W_TILE;
-constexpr uint32_t OFF_RAW = OFF_WL + STAGES * W_TILE;  // 192 KB
+constexpr uint32_t OFF_XL = OFF_XH + XS * X_TILE;
+constexpr uint32_t OFF_WH = OFF_XL + XS * X_TILE;
+constexpr uint32_t OFF_WL = OFF_WH + WS * W_TILE;
+constexpr uint32_t OFF_RAW = OFF_WL + WS * W_TILE;  // 176 KB
 
 template <int QT>
 struct TQ;
@@ -48,76 +61,154 @@ struct TQ<4> {
 };
 
 template <int QT>
-__host__ __device__ constexpr uint32_t raw_slot_bytes() {
-  return (uint32_t)TQ<QT>::rawb * BN;
-}
-template <int QT>
-__host__ __device__ constexpr uint32_t smem_bytes() {
-  return OFF_RAW + 2 * raw_slot_bytes<QT>() + 256 /* barriers */ + 1024 /* alignment slack */;
-}
+struct Cfg {
+  static constexpr uint32_t RAW_SLOT = (uint32_t)TQ<QT>::rawb * BN;
+  static constexpr uint32_t OFF_EPI = OFF_RAW + RS * RAW_SLOT;  // tile bias + gains for the epilogue
+  static constexpr uint32_t OFF_BAR = OFF_EPI + 2 * BN * 4;
+  static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;       // barriers + alignment slack
+};
 
 struct TcParams {
   int M, N, K;
+  int swiglu_F;  // > 0: a tile is 128 gate rows + the matching 128 up rows
+  int n_tiles_n, n_tiles;
   // power-of-two weight prescale: W is split as (2^s d q) = Wh + Wl so that Wl
   // stays a normal f16; the accumulator is multiplied by 2^-s (both exact)
   float wscale, acc_scale;
-  int swiglu_F;  // >0: SWIGLU tile = 128 gate rows + 128 up rows
   Epi epi;
   int *err;
 };
 
 // 32 columns of (main + correction) accumulator for this thread's row.
-T0B_DEV void tmem_ld_pair(uint32_t taddr, float *v) {
+T0B_DEV void tmem_ld_pair(uint32_t taddr, float *v, float scale) {
   float c[32];
   tmem_ld32(taddr, v);
   tmem_ld32(taddr + BN, c);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] += c[i];
+  for (int i = 0; i < 32; ++i) v[i] = (v[i] + c[i]) * scale;
 }
 
+// 32 values as f16 hi/lo pairs, 8 per 16-byte store.
+T0B_DEV void store_split32(__half *hi, __half *lo, size_t off, const float *v) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __half h0, l0, h1, l1;
+      split_f16(v[i + 2 * j], h0, l0);
+      split_f16(v[i + 2 * j + 1], h1, l1);
+      __half2 hh = __halves2half2(h0, h1), ll = __halves2half2(l0, l1);
+      h[j] = *reinterpret_cast<uint32_t *>(&hh);
+      l[j] = *reinterpret_cast<uint32_t *>(&ll);
+    }
+    *reinterpret_cast<uint4 *>(hi + off + i) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4 *>(lo + off + i) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+T0B_DEV void store_f32x32(float *dst, const float *v) {
+  float4 *d = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+// Dequantize one 32-value block of one weight row (raw window `src`, block
+// starting `off` bytes in) into 16 f16x2 hi words and 16 lo words:
+// hi = f16(2^s d q), lo = f16(2^s d q - hi).
 template <int QT>
-__global__ void __launch_bounds__(192, 1)
+T0B_DEV void dequant_block(const uint8_t *src, int off, float wscale, uint32_t *hv, uint32_t *lv) {
+  constexpr int RAWB = TQ<QT>::rawb;
+  uint32_t wv[RAWB / 4 + 1];
+#pragma unroll
+  for (int i = 0; i < RAWB / 16; ++i) {
+    uint4 q4 = reinterpret_cast<const uint4 *>(src)[i];
+    wv[4 * i] = q4.x;
+    wv[4 * i + 1] = q4.y;
+    wv[4 * i + 2] = q4.z;
+    wv[4 * i + 3] = q4.w;
+  }
+  wv[RAWB / 4] = 0u;
+  auto word_at = [&](int byte) -> uint32_t {  // 4 bytes starting at `byte`
+    int w = byte >> 2, sh = (byte & 3) * 8;
+    return sh ? __funnelshift_r(wv[w], wv[w + 1], sh) : wv[w];
+  };
+  const uint32_t dbits = word_at(off) & 0xFFFFu;
+  const __half dh = __float2half_rn(__half2float(__ushort_as_half((unsigned short)dbits)) * wscale);  // exact
+  const __half2 d2 = __halves2half2(dh, dh);
+  auto emit = [&](uint32_t qv, int pair) {
+    __half2 h = __hmul2(d2, *reinterpret_cast<__half2 *>(&qv));
+    __half2 l = __hfma2(d2, *reinterpret_cast<__half2 *>(&qv), __hneg2(h));  // exact residual, rounded once
+    hv[pair] = *reinterpret_cast<uint32_t *>(&h);
+    lv[pair] = *reinterpret_cast<uint32_t *>(&l);
+  };
+  if (QT == 8) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      uint32_t a, b;
+      i8x4_to_h2x2(word_at(off + 2 + 4 * i), a, b);  // int8 values 4i..4i+3
+      emit(a, 2 * i);
+      emit(b, 2 * i + 1);
+    }
+  } else {
+    // byte b holds value b (low nibble) and value b+16 (high nibble)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t r[4];
+      nib8_to_h2x4(word_at(off + 2 + 4 * i), r);
+      emit(r[0], 2 * i);          // values 4i, 4i+1
+      emit(r[1], 2 * i + 1);      // values 4i+2, 4i+3
+      emit(r[2], 8 + 2 * i);      // values 16+4i, 16+4i+1
+      emit(r[3], 8 + 2 * i + 1);  // values 16+4i+2, 16+4i+3
+    }
+  }
+}
+
+T0B_DEV void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }  // the 8 epilogue warps only
+
+template <int QT>
+__global__ void __launch_bounds__(NTHREADS, 1)
     gemm_q_tc_kernel(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
                      const __grid_constant__ CUtensorMap tm_w, TcParams prm) {
+  using C = Cfg<QT>;
   constexpr int BPB = TQ<QT>::bpb, RAWB = TQ<QT>::rawb;
-  constexpr uint32_t RAW_SLOT = raw_slot_bytes<QT>();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t *smem = smem_raw + (base_u32 - smem_u32(smem_raw));
 
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_RAW + 2 * RAW_SLOT);
-  uint64_t *x_full = bars + 0;     // [2]
-  uint64_t *raw_full = bars + 2;   // [2]
-  uint64_t *raw_empty = bars + 4;  // [2]
-  uint64_t *w_full = bars + 6;     // [2]
-  uint64_t *empty = bars + 8;      // [2] MMA released stage
-  uint64_t *acc_full = bars + 10;  // [1]
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 12);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
+  uint64_t *x_full = bars;              // [XS] TMA -> MMA
+  uint64_t *x_empty = x_full + XS;      // [XS] MMA -> TMA
+  uint64_t *raw_full = x_empty + XS;    // [RS] TMA -> dequant
+  uint64_t *raw_empty = raw_full + RS;  // [RS] dequant -> TMA
+  uint64_t *w_full = raw_empty + RS;    // [WS] dequant -> MMA
+  uint64_t *w_empty = w_full + WS;      // [WS] MMA -> dequant
+  uint64_t *acc_full = w_empty + WS;    // MMA -> epilogue
+  uint64_t *acc_empty = acc_full + 1;   // epilogue -> MMA (TMEM drained)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(acc_empty + 2);
+  float *epi_s = reinterpret_cast<float *>(smem + C::OFF_EPI);  // [2][BN]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int M = prm.M, K = prm.K;
   const int S = K / BK;
-  const int m0 = blockIdx.y * BM;
-  // weight rows of the two 128-row halves of this tile
-  int wr0, wr1;
-  if (prm.swiglu_F > 0) {
-    wr0 = blockIdx.x * 128;
-    wr1 = prm.swiglu_F + blockIdx.x * 128;
-  } else {
-    wr0 = blockIdx.x * BN;
-    wr1 = wr0 + 128;
-  }
+  const bool swiglu = prm.swiglu_F > 0;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < XS; ++i) {
       mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], 1);
+    }
+    for (int i = 0; i < RS; ++i) {
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], 128);
+    }
+    for (int i = 0; i < WS; ++i) {
       mbar_init(&w_full[i], 128);
-      mbar_init(&empty[i], 1);
+      mbar_init(&w_empty[i], 1);
     }
     mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 256);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -128,7 +219,7 @@ __global__ void __launch_bounds__(192, 1)
     prefetch_tmap(&tm_w);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * BN);  // main accumulator + correction accumulator
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -136,189 +227,216 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      for (int s = 0; s < S && !*abort_flag; ++s) {
-        // raw weight blocks of this stage: block columns 2s, 2s+1 -> slots 0, 1
-        for (int h = 0; h < 2; ++h) {
-          if (s >= 1 && !mbar_wait(&raw_empty[h], (s - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag)) break;
-          int j = 2 * s + h;
-          int x = (j * BPB) & ~15;
-          mbar_arrive_expect_tx(&raw_full[h], RAW_SLOT);
-          uint8_t *dst = smem + OFF_RAW + h * RAW_SLOT;
-          tma_load_2d(dst, &tm_w, &raw_full[h], x, wr0);
-          tma_load_2d(dst + RAWB * 128, &tm_w, &raw_full[h], x, wr1);
-        }
-        const int xs = s & 1;
-        if (s >= 2 && !mbar_wait(&empty[xs], ((s >> 1) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag))
-          break;
-        mbar_arrive_expect_tx(&x_full[xs], 2 * X_TILE);
-        tma_load_2d(smem + OFF_XH + xs * X_TILE, &tm_xh, &x_full[xs], s * BK, m0);
-        tma_load_2d(smem + OFF_XL + xs * X_TILE, &tm_xl, &x_full[xs], s * BK, m0);
-      }
+  // tile -> (first token, weight rows of the two 128-row halves, n tile)
+  auto tile_rows = [&](int tile, int &m0, int &wr0, int &wr1, int &nt) {
+    nt = tile % prm.n_tiles_n;
+    m0 = (tile / prm.n_tiles_n) * BM;
+    if (swiglu) {
+      wr0 = nt * 128;
+      wr1 = prm.swiglu_F + nt * 128;
+    } else {
+      wr0 = nt * BN;
+      wr1 = wr0 + 128;
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+  };
+
+  const int wg = warp >> 2;
+  if (wg == 0) {
+    regs_dealloc<40>();
+    if (warp == 0 && lane == 0) {
+      // ---------------------------------------------------------- producer
+      uint32_t g = 0;  // global stage counter across tiles
+      for (int tile = blockIdx.x; tile < prm.n_tiles && !*abort_flag; tile += gridDim.x) {
+        int m0, wr0, wr1, nt;
+        tile_rows(tile, m0, wr0, wr1, nt);
+        for (int s = 0; s < S && !*abort_flag; ++s, ++g) {
+          const uint32_t rs = g % RS;
+          if (g >= RS && !mbar_wait(&raw_empty[rs], ((g / RS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag))
+            break;
+          const int x = (s * BPB) & ~15;  // aligned window holding block column s
+          mbar_arrive_expect_tx(&raw_full[rs], C::RAW_SLOT);
+          uint8_t *dst = smem + OFF_RAW + rs * C::RAW_SLOT;
+          tma_load_2d(dst, &tm_w, &raw_full[rs], x, wr0);
+          tma_load_2d(dst + RAWB * 128, &tm_w, &raw_full[rs], x, wr1);
+          const uint32_t xs = g % XS;
+          if (g >= XS && !mbar_wait(&x_empty[xs], ((g / XS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag))
+            break;
+          mbar_arrive_expect_tx(&x_full[xs], 2 * X_TILE);
+          tma_load_2d(smem + OFF_XH + xs * X_TILE, &tm_xh, &x_full[xs], s * BK, m0);
+          tma_load_2d(smem + OFF_XL + xs * X_TILE, &tm_xl, &x_full[xs], s * BK, m0);
+        }
+      }
+    } else if (warp == 1 && lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
-      bool ok = true;
-      for (int s = 0; s < S; ++s) {
-        const int xs = s & 1;
-        if (!mbar_wait(&x_full[xs], (s >> 1) & 1, prm.err, T0B_DEVERR_WAIT_X, abort_flag) ||
-            !mbar_wait(&w_full[xs], (s >> 1) & 1, prm.err, T0B_DEVERR_WAIT_DEQ, abort_flag)) {
-          ok = false;
-          break;
-        }
+      uint32_t g = 0, it = 0;
+      for (int tile = blockIdx.x; tile < prm.n_tiles && !*abort_flag; tile += gridDim.x, ++it) {
+        if (it >= 1 && !mbar_wait(acc_empty, (it - 1) & 1, prm.err, T0B_DEVERR_WAIT_ACC, abort_flag)) break;
         tc_fence_after();
-        const uint32_t xh = base_u32 + OFF_XH + xs * X_TILE, xl = base_u32 + OFF_XL + xs * X_TILE;
-        const uint32_t wh = base_u32 + OFF_WH + xs * W_TILE, wl = base_u32 + OFF_WL + xs * W_TILE;
+        for (int s = 0; s < S; ++s, ++g) {
+          const uint32_t xs = g % XS, ws = g % WS;
+          if (!mbar_wait(&x_full[xs], (g / XS) & 1, prm.err, T0B_DEVERR_WAIT_X, abort_flag) ||
+              !mbar_wait(&w_full[ws], (g / WS) & 1, prm.err, T0B_DEVERR_WAIT_DEQ, abort_flag))
+            break;
+          tc_fence_after();
+          const uint32_t xh = base_u32 + OFF_XH + xs * X_TILE, xl = base_u32 + OFF_XL + xs * X_TILE;
+          const uint32_t wh = base_u32 + OFF_WH + ws * W_TILE, wl = base_u32 + OFF_WL + ws * W_TILE;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint32_t ko = kk * 32;  // 16 f16 along K inside the 128-byte swizzled row
-          const uint32_t acc = (s > 0 || kk > 0) ? 1u : 0u;
-          // main term and the two ~2^-11 correction terms go to separate
-          // accumulators: the tensor core's f32 accumulation error grows with
-          // the number of MMAs chained into one accumulator
-          umma_f16(tmem, sw128_desc(xh + ko), sw128_desc(wh + ko), idesc, acc);
-          umma_f16(tmem + BN, sw128_desc(xh + ko), sw128_desc(wl + ko), idesc, acc);
-          umma_f16(tmem + BN, sw128_desc(xl + ko), sw128_desc(wh + ko), idesc, 1u);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint32_t ko = kk * 32;  // 16 f16 along K inside the 64-byte swizzled row
+            const uint32_t acc = (s > 0 || kk > 0) ? 1u : 0u;
+            umma_f16(tmem, sw64_desc(xh + ko), sw64_desc(wh + ko), idesc, acc);
+            umma_f16(tmem + BN, sw64_desc(xh + ko), sw64_desc(wl + ko), idesc, acc);
+            umma_f16(tmem + BN, sw64_desc(xl + ko), sw64_desc(wh + ko), idesc, 1u);
+          }
+          umma_commit(&x_empty[xs]);
+          umma_commit(&w_empty[ws]);
         }
-        umma_commit(&empty[xs]);
+        umma_commit(acc_full);
       }
-      umma_commit(acc_full);  // also fires after an abort, once issued MMAs drain
-      (void)ok;
     }
-  } else {
+  } else if (wg == 1) {
     // ------------------------------------------------------------ dequant
-    const int t = threadIdx.x - 64;  // 0..127
-    for (int s = 0; s < S && !*abort_flag; ++s) {
-      const int ws = s & 1;
-      if (s >= 2 && !mbar_wait(&empty[ws], ((s >> 1) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag)) break;
-      uint8_t *whs = smem + OFF_WH + ws * W_TILE;
-      uint8_t *wls = smem + OFF_WL + ws * W_TILE;
-      bool ok = true;
-      for (int h = 0; h < 2; ++h) {
-        if (!mbar_wait(&raw_full[h], s & 1, prm.err, T0B_DEVERR_WAIT_W, abort_flag)) {
+    const int t = threadIdx.x - 128;  // 0..127
+    uint32_t g = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < prm.n_tiles && ok && !*abort_flag; tile += gridDim.x) {
+      for (int s = 0; s < S; ++s, ++g) {
+        const uint32_t ws = g % WS, rs = g % RS;
+        if ((g >= WS && !mbar_wait(&w_empty[ws], ((g / WS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag)) ||
+            !mbar_wait(&raw_full[rs], (g / RS) & 1, prm.err, T0B_DEVERR_WAIT_W, abort_flag)) {
           ok = false;
           break;
         }
-        const int j = 2 * s + h;
-        const int off = (j * BPB) & 15;  // block start inside the aligned window
-        const uint8_t *slot = smem + OFF_RAW + h * RAW_SLOT;
+        uint8_t *whs = smem + OFF_WH + ws * W_TILE;
+        uint8_t *wls = smem + OFF_WL + ws * W_TILE;
+        const int off = (s * BPB) & 15;  // block start inside the aligned window
+        const uint8_t *slot = smem + OFF_RAW + rs * C::RAW_SLOT;
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
           const int r = t + 128 * rr;  // tile row 0..255
-          const uint32_t *src = reinterpret_cast<const uint32_t *>(slot + r * RAWB);
-          uint32_t wv[RAWB / 4 + 1];
-#pragma unroll
-          for (int i = 0; i < RAWB / 16; ++i) {
-            uint4 q4 = reinterpret_cast<const uint4 *>(src)[i];
-            wv[4 * i] = q4.x;
-            wv[4 * i + 1] = q4.y;
-            wv[4 * i + 2] = q4.z;
-            wv[4 * i + 3] = q4.w;
-          }
-          wv[RAWB / 4] = 0u;
-          auto word_at = [&](int byte) -> uint32_t {  // 4 bytes starting at `byte`
-            int w = byte >> 2, sh = (byte & 3) * 8;
-            return sh ? __funnelshift_r(wv[w], wv[w + 1], sh) : wv[w];
-          };
-          const uint32_t dbits = word_at(off) & 0xFFFFu;
-          const __half dh =
-              __float2half_rn(__half2float(__ushort_as_half((unsigned short)dbits)) * prm.wscale);  // exact
-          const __half2 d2 = __halves2half2(dh, dh);
-          // 32 values of this block -> 4 chunks of 8 f16 at k = 32h + 8c
           uint32_t hv[16], lv[16];
-          if (QT == 8) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              uint32_t q = word_at(off + 2 + 4 * i);  // 4 int8 values
-              uint32_t qa = i8x2_to_h2(q & 0xFFFFu), qb = i8x2_to_h2(q >> 16);
-              __half2 ha = __hmul2(d2, *reinterpret_cast<__half2 *>(&qa));
-              __half2 hb = __hmul2(d2, *reinterpret_cast<__half2 *>(&qb));
-              __half2 la = __hfma2(d2, *reinterpret_cast<__half2 *>(&qa), __hneg2(ha));
-              __half2 lb = __hfma2(d2, *reinterpret_cast<__half2 *>(&qb), __hneg2(hb));
-              hv[2 * i] = *reinterpret_cast<uint32_t *>(&ha);
-              hv[2 * i + 1] = *reinterpret_cast<uint32_t *>(&hb);
-              lv[2 * i] = *reinterpret_cast<uint32_t *>(&la);
-              lv[2 * i + 1] = *reinterpret_cast<uint32_t *>(&lb);
-            }
-          } else {
-            // bytes b0..b15: low nibble = value b, high nibble = value b+16
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint32_t q = word_at(off + 2 + 4 * i);  // bytes 4i..4i+3
-#pragma unroll
-              for (int hi = 0; hi < 2; ++hi) {
-                uint32_t qa = nib2_to_h2(q & 0xFFFFu, hi), qb = nib2_to_h2(q >> 16, hi);
-                __half2 ha = __hmul2(d2, *reinterpret_cast<__half2 *>(&qa));
-                __half2 hb = __hmul2(d2, *reinterpret_cast<__half2 *>(&qb));
-                __half2 la = __hfma2(d2, *reinterpret_cast<__half2 *>(&qa), __hneg2(ha));
-                __half2 lb = __hfma2(d2, *reinterpret_cast<__half2 *>(&qb), __hneg2(hb));
-                const int v0 = 16 * hi + 4 * i;  // value index of qa.x
-                hv[v0 / 2] = *reinterpret_cast<uint32_t *>(&ha);
-                hv[v0 / 2 + 1] = *reinterpret_cast<uint32_t *>(&hb);
-                lv[v0 / 2] = *reinterpret_cast<uint32_t *>(&la);
-                lv[v0 / 2 + 1] = *reinterpret_cast<uint32_t *>(&lb);
-              }
-            }
-          }
+          dequant_block<QT>(slot + r * RAWB, off, prm.wscale, hv, lv);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            const uint32_t o = sw128_offset(r, 32 * h + 8 * c);
+            const uint32_t o = sw64_offset(r, 8 * c);
             *reinterpret_cast<uint4 *>(whs + o) = make_uint4(hv[4 * c], hv[4 * c + 1], hv[4 * c + 2], hv[4 * c + 3]);
             *reinterpret_cast<uint4 *>(wls + o) = make_uint4(lv[4 * c], lv[4 * c + 1], lv[4 * c + 2], lv[4 * c + 3]);
           }
         }
-        mbar_arrive(&raw_empty[h]);
+        mbar_arrive(&raw_empty[rs]);
+        fence_proxy_async_smem();
+        mbar_arrive(&w_full[ws]);
       }
-      if (!ok) break;
-      fence_proxy_async_smem();
-      mbar_arrive(&w_full[ws]);
     }
-
+  } else {
     // ------------------------------------------------------------ epilogue
-    const bool have = mbar_wait(acc_full, 0, prm.err, T0B_DEVERR_WAIT_ACC, abort_flag) && !*abort_flag;
-    tc_fence_after();
-    if (have) {
-      const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    regs_alloc<168>();
+    const int q = warp & 3;              // TMEM lane quadrant this warp may access
+    const int half = (warp - 8) >> 2;    // which 128 of the tile's 256 columns
+    const int et = threadIdx.x - 256;    // 0..255
+    const Epi &e = prm.epi;
+    float *sb = epi_s;       // tile bias  [BN]
+    float *sg = epi_s + BN;  // tile gains [BN] (RESID: next norm gain)
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < prm.n_tiles; tile += gridDim.x, ++it) {
+      int m0, wr0, wr1, nt;
+      tile_rows(tile, m0, wr0, wr1, nt);
+      epi_bar();  // every epilogue thread is done with the previous tile's constants
+      {
+        const int c = et;  // 256 threads, 256 columns
+        if (swiglu) {
+          const int f = c < 128 ? nt * 128 + c : e.F + nt * 128 + (c - 128);
+          sb[c] = e.bias ? e.bias[f] : 0.0f;
+        } else {
+          sb[c] = e.bias ? e.bias[nt * BN + c] : 0.0f;
+          if (e.kind == EPI_RESID) sg[c] = e.gnext[nt * BN + c];
+        }
+      }
+      epi_bar();
       const int m = m0 + 32 * q + lane;
-      const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
-      const Epi &e = prm.epi;
       const bool live = m < M;
-      const float denom = live ? epi_row_denom(e, m) : 1.0f;
-      if (e.kind == EPI_QKV) {
-        for (int hh = 0; hh < 4; ++hh) {
-          float v[64];
-          tmem_ld_pair(trow + 64 * hh, v);
-          tmem_ld_pair(trow + 64 * hh + 32, v + 32);
+      const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
+      const bool have = mbar_wait(acc_full, it & 1, prm.err, T0B_DEVERR_WAIT_ACC, abort_flag) && !*abort_flag;
+      tc_fence_after();
+      // drain: this thread's 128 accumulator columns into registers
+      // (SWIGLU: gate columns 64*half.. and the matching up columns)
+      float v[128];
+      const float rinv = (have && live) ? 1.0f / epi_row_denom(e, m) : 1.0f;
+      const float sc = prm.acc_scale * rinv;
+      const int c0 = swiglu ? 64 * half : 128 * half;
+      if (have) {
+        if (swiglu) {
+          tmem_ld_pair(trow + c0, v, sc);
+          tmem_ld_pair(trow + c0 + 32, v + 32, sc);
+          tmem_ld_pair(trow + 128 + c0, v + 64, sc);
+          tmem_ld_pair(trow + 128 + c0 + 32, v + 96, sc);
+        } else {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) v[i] *= prm.acc_scale;
-          if (live) epi_qkv64(e, m, blockIdx.x * BN + 64 * hh, v, denom);
+          for (int c = 0; c < 4; ++c) tmem_ld_pair(trow + c0 + 32 * c, v + 32 * c, sc);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty);  // TMEM is free for the next tile's MMAs
+      // no early exit: every epilogue thread runs every iteration so the
+      // named barrier above always sees all 256 of them (after an abort the
+      // waits return at once and no work is done)
+      if (!have || !live) continue;
+      if (e.kind == EPI_QKV) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float *vh = v + 64 * hh;
+#pragma unroll
+          for (int i = 0; i < 64; ++i) vh[i] += sb[c0 + 64 * hh + i];
+          epi_qkv64_nobias(e, m, nt * BN + c0 + 64 * hh, vh);
         }
       } else if (e.kind == EPI_SWIGLU) {
-        for (int c = 0; c < 4; ++c) {
-          float gv[32], uv[32];
-          tmem_ld_pair(trow + 32 * c, gv);
-          tmem_ld_pair(trow + 128 + 32 * c, uv);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float z[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            gv[i] *= prm.acc_scale;
-            uv[i] *= prm.acc_scale;
+            const float gg = v[32 * c + i] + sb[c0 + 32 * c + i];
+            const float uu = v[64 + 32 * c + i] + sb[128 + c0 + 32 * c + i];
+            z[i] = gg / (1.0f + expf(-gg)) * uu;
           }
-          if (live) epi_swiglu32(e, m, blockIdx.x * 128 + 32 * c, gv, uv, denom);
+          const size_t f0 = (size_t)nt * 128 + c0 + 32 * c;
+          if (e.zh) store_split32(e.zh, e.zl, (size_t)m * e.F + f0, z);
+          if (e.z32) store_f32x32(e.z32 + (size_t)m * e.F + f0, z);
         }
-      } else {
-        float ss = 0.0f;
-        for (int c = 0; c < 8; ++c) {
-          float v[32];
-          tmem_ld_pair(trow + 32 * c, v);
+      } else if (e.kind == EPI_PLAIN) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= prm.acc_scale;
-          if (live) ss += epi_cols32(e, m, blockIdx.x * BN + 32 * c, v, denom);
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[32 * c + i] += sb[c0 + 32 * c + i];
+          store_f32x32(e.y + (size_t)m * e.ldy + nt * BN + c0 + 32 * c, v + 32 * c);
         }
-        if (live && e.kind == EPI_RESID) e.ssq_out[(size_t)m * e.ssq_out_nt + blockIdx.x] = ss;
+      } else {  // EPI_RESID: x += acc + bias; (x * gnext) split; sum of x^2
+        const int n0 = nt * BN + c0;
+        const float4 *xr = reinterpret_cast<const float4 *>(e.x + (size_t)m * e.N + n0);
+        float ss = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float4 xa[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) xa[i] = xr[8 * c + i];
+          float gx[32];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float xs4[4] = {xa[i].x, xa[i].y, xa[i].z, xa[i].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int col = c0 + 32 * c + 4 * i + j;
+              const float xn = xs4[j] + (v[32 * c + 4 * i + j] + sb[col]);
+              v[32 * c + 4 * i + j] = xn;
+              ss += xn * xn;
+              gx[4 * i + j] = xn * sg[col];
+            }
+          }
+          store_f32x32(e.x + (size_t)m * e.N + n0 + 32 * c, v + 32 * c);
+          store_split32(e.xh, e.xl, (size_t)m * e.N + n0 + 32 * c, gx);
+        }
+        e.ssq_out[(size_t)m * e.ssq_out_nt + 2 * nt + half] = ss;
       }
     }
   }
@@ -327,7 +445,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * BN);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -348,30 +466,41 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-bool make_tmap_2d(CUtensorMap *tm, CUtensorMapDataType dt, int esize, const void *ptr, uint64_t inner,
-                  uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+bool make_tmap_2d(CUtensorMap *tm, CUtensorMapDataType dt, const void *ptr, uint64_t inner, uint64_t outer,
+                  uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  (void)esize;
   CUresult r = fn(tm, dt, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
+int sm_count() {
+  static int n_sm = 0;
+  if (!n_sm) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    if (n_sm <= 0) n_sm = 148;
+  }
+  return n_sm;
+}
+
 template <int QT>
 cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows, int wshift,
                         const Epi &epi, int *err, cudaStream_t st) {
+  using C = Cfg<QT>;
   CUtensorMap txh, txl, tw;
   const uint64_t rb = (uint64_t)(K / 32) * TQ<QT>::bpb;
-  if (!make_tmap_2d(&txh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ah, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BM,
-                    CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_tmap_2d(&txl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, al, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BM,
-                    CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, rb, (uint64_t)wrows, rb, TQ<QT>::rawb, 128,
+  if (!make_tmap_2d(&txh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ah, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BM,
+                    CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !make_tmap_2d(&txl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, al, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BM,
+                    CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, rb, (uint64_t)wrows, rb, TQ<QT>::rawb, 128,
                     CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
   TcParams prm;
@@ -379,16 +508,17 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
   prm.N = epi.N;
   prm.K = K;
   prm.swiglu_F = epi.kind == EPI_SWIGLU ? epi.F : 0;
+  prm.n_tiles_n = epi.kind == EPI_SWIGLU ? epi.F / 128 : epi.N / BN;
+  prm.n_tiles = prm.n_tiles_n * ((M + BM - 1) / BM);
   prm.wscale = ldexpf(1.0f, wshift);
   prm.acc_scale = ldexpf(1.0f, -wshift);
   prm.epi = epi;
   prm.err = err;
-  constexpr uint32_t smem = smem_bytes<QT>();
   auto kfn = gemm_q_tc_kernel<QT>;
-  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
   if (e != cudaSuccess) return e;
-  dim3 grid(epi.kind == EPI_SWIGLU ? epi.F / 128 : epi.N / BN, (M + BM - 1) / BM);
-  kfn<<<grid, 192, smem, st>>>(txh, txl, tw, prm);
+  const int grid = prm.n_tiles < sm_count() ? prm.n_tiles : sm_count();  // persistent: one CTA per SM
+  kfn<<<grid, NTHREADS, C::SMEM, st>>>(txh, txl, tw, prm);
   return cudaGetLastError();
 }
 
@@ -397,12 +527,16 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
 // Host entry.  qt: 8 = Q8_0, 4 = Q4_0.  Requires K % 256 == 0, N % 256 == 0
 // (SWIGLU: F % 128 == 0), M >= 1, 16-byte aligned A rows.  `wrows` is the
 // number of rows of W (N, or 2F for SWIGLU); `wshift` the weight prescale
-// exponent from t0b_weight_shift.
+// exponent from t0b_weight_shift.  RESID writes two partial sums of squares
+// per 256-column tile (one per 128-column half).
 cudaError_t t0b_launch_gemm_tc(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
                                int wshift, const Epi &epi, int *err, cudaStream_t st) {
   if (qt == 8) return launch_tc_t<8>(ah, al, M, K, W, wrows, wshift, epi, err, st);
   return launch_tc_t<4>(ah, al, M, K, W, wrows, wshift, epi, err, st);
 }
+
+// Columns per RESID partial sum of squares in the tensor-core path.
+int t0b_tc_tile_width() { return 128; }
 
 // Largest |scale| of a Q8_0 / Q4_0 matrix (device), as the f32 bit pattern of
 // a non-negative float (so an integer max is a float max).

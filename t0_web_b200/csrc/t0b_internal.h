@@ -45,6 +45,7 @@ cudaError_t t0b_launch_gemm_small(int qt, const __half *ah, const __half *al, in
                                   const Epi &epi, int *err, cudaStream_t st);
 cudaError_t t0b_launch_gemm_tc(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
                                int wshift, const Epi &epi, int *err, cudaStream_t st);
+int t0b_tc_tile_width();
 cudaError_t t0b_launch_absmax_scale(const uint8_t *W, size_t nblocks, int bpb, unsigned int *out, cudaStream_t st);
 
 // Exponent s of the power-of-two weight prescale for the split-f16 tensor-core

@@ -6,6 +6,7 @@
 // launch sequence, and the batching drivers.  Independent series are packed
 // as variate rows of p patches each (p = context patches + horizon patches);
 // group attention is scoped per series, so no cross-series mask exists.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -104,14 +105,30 @@ struct t0b_model {
   int *d_err = nullptr;
   size_t max_tokens = 262144;
   int tc_min_tokens = 128;
-  std::map<int, float *> rope;  // p -> [3][p][hd] device tables
+  std::map<int, float *> rope;  // p -> [4][p][hd] device tables: cos, sin, scale, 1/scale
   // workspace
   DBuf x, qkv, feat, ssq, xo, dhid, dout, loc, scl;
   DBuf xh, xl, ah, al, hh, hl;
   DBuf meta;  // row/series metadata
   HBuf hmeta;
   DBuf ctx_stage, out_stage;
+  // measurement
+  uint64_t launches = 0;
+  bool prof = false;
+  struct Rec {
+    int cls;
+    cudaEvent_t a, b;
+    double flops, bytes;
+  };
+  std::vector<Rec> recs;
+  std::vector<cudaEvent_t> ev_pool;
+  t0b_kernel_stats stats[7];
   ~t0b_model() {
+    for (auto &r : recs) {
+      cudaEventDestroy(r.a);
+      cudaEventDestroy(r.b);
+    }
+    for (auto e : ev_pool) cudaEventDestroy(e);
     for (auto &kv : rope) cudaFree(kv.second);
     for (void *p : allocs) cudaFree(p);
     if (own_stream && stream) cudaStreamDestroy(stream);
@@ -359,8 +376,8 @@ t0b_status rope_tables(t0b_model *m, int p, const float **out) {
     return T0B_OK;
   }
   const int hd = 64, half = 32;
-  std::vector<float> h((size_t)3 * p * hd);
-  float *cs = h.data(), *sn = cs + (size_t)p * hd, *sc = sn + (size_t)p * hd;
+  std::vector<float> h((size_t)4 * p * hd);
+  float *cs = h.data(), *sn = cs + (size_t)p * hd, *sc = sn + (size_t)p * hd, *si = sc + (size_t)p * hd;
   const double theta = 10000.0, base512 = 512.0;
   const double max_half = std::floor((double)(p - 1) / 2.0);
   for (int pos = 0; pos < p; ++pos) {
@@ -373,6 +390,7 @@ t0b_status rope_tables(t0b_model *m, int p, const float **out) {
       cs[pos * hd + 2 * j] = cs[pos * hd + 2 * j + 1] = (float)std::cos(ang);  // interleaved pairs
       sn[pos * hd + 2 * j] = sn[pos * hd + 2 * j + 1] = (float)std::sin(ang);
       sc[pos * hd + j] = sc[pos * hd + half + j] = s;  // concatenated halves
+      si[pos * hd + j] = si[pos * hd + half + j] = 1.0f / s;  // k side (ops.rs:135-136 recip)
     }
   }
   float *d = nullptr;
@@ -394,14 +412,67 @@ struct Pass {
 
 bool use_tc(const t0b_model *m, int M) { return M >= m->tc_min_tokens; }
 
+enum { KC_GEMM_TC = 0, KC_GEMM_SMALL, KC_ATTN_TIME, KC_ATTN_GROUP, KC_PREP, KC_SGEMM, KC_OTHER, KC_N };
+const char *kKcNames[KC_N] = {"gemm_tc", "gemm_small", "attn_time", "attn_group", "prep", "sgemm", "other"};
+
+cudaEvent_t take_event(t0b_model *m) {
+  if (!m->ev_pool.empty()) {
+    cudaEvent_t e = m->ev_pool.back();
+    m->ev_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// Every kernel launch of a pass goes through here: counts it and, when
+// profiling is on, brackets it with events on the model's stream.
+template <class F>
+cudaError_t launch(t0b_model *m, int cls, double flops, double bytes, F &&fn) {
+  ++m->launches;
+  if (!m->prof) return fn();
+  t0b_model::Rec r{cls, take_event(m), take_event(m), flops, bytes};
+  cudaEventRecord(r.a, m->stream);
+  cudaError_t e = fn();
+  cudaEventRecord(r.b, m->stream);
+  m->recs.push_back(r);
+  return e;
+}
+
+void fold_records(t0b_model *m) {
+  for (auto &r : m->recs) {
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) {
+      auto &st = m->stats[r.cls];
+      st.launches += 1;
+      st.total_ms += ms;
+      st.flops += r.flops;
+      st.bytes += r.bytes;
+    }
+    m->ev_pool.push_back(r.a);
+    m->ev_pool.push_back(r.b);
+  }
+  m->recs.clear();
+}
+
 cudaError_t qgemm(t0b_model *m, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
                   int wshift, Epi &epi) {
+  // algorithmic work: 2 M N K flops; bytes = raw weight blocks + A (as f32) +
+  // the f32 output (SWIGLU writes F columns; RESID also reads the residual)
+  const double wbytes = (double)wrows * K / 32.0 * (m->qt == 8 ? 34.0 : 18.0);
+  const double outc = epi.kind == EPI_SWIGLU ? (double)epi.F : (double)epi.N;
+  const double flops = 2.0 * M * (double)wrows * K;
+  const double bytes = wbytes + 4.0 * M * K + 4.0 * M * outc * (epi.kind == EPI_RESID ? 2.0 : 1.0);
   if (use_tc(m, M)) {
-    if (epi.kind == EPI_RESID) epi.ssq_out_nt = epi.N / 256;
-    return t0b_launch_gemm_tc(m->qt, ah, al, M, K, W, wrows, wshift, epi, m->d_err, m->stream);
+    if (epi.kind == EPI_RESID) epi.ssq_out_nt = epi.N / t0b_tc_tile_width();
+    return launch(m, KC_GEMM_TC, flops, bytes, [&] {
+      return t0b_launch_gemm_tc(m->qt, ah, al, M, K, W, wrows, wshift, epi, m->d_err, m->stream);
+    });
   }
   if (epi.kind == EPI_RESID) epi.ssq_out_nt = epi.N / 64;
-  return t0b_launch_gemm_small(m->qt, ah, al, M, K, W, epi, m->d_err, m->stream);
+  return launch(m, KC_GEMM_SMALL, flops, bytes,
+                [&] { return t0b_launch_gemm_small(m->qt, ah, al, M, K, W, epi, m->d_err, m->stream); });
 }
 
 t0b_status ensure_ws(t0b_model *m, size_t T, size_t R, size_t nout) {
@@ -481,7 +552,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   pa.feat = m->feat.as<float>();
   pa.out_loc = m->loc.as<float>();
   pa.out_scale = m->scl.as<float>();
-  LAUNCH(t0b_launch_prep(pa, m->stream));
+  LAUNCH(launch(m, KC_PREP, 0.0, (double)R * p * 32 * 4 + T * 96.0 * 4, [&] { return t0b_launch_prep(pa, m->stream); }));
 
   // 2. patch encoder: x = relu(f.hw^T+hb).ow^T + ob + f.rw^T + rb + type_emb[0]
   float *x = m->x.as<float>();
@@ -498,14 +569,14 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   g.K = 96;
   g.bias = m->enc_hb;
   g.relu = 1;
-  LAUNCH(t0b_launch_sgemm(g, m->stream));
+  LAUNCH(launch(m, KC_SGEMM, 2.0 * g.M * g.N * g.K, 0.0, [&] { return t0b_launch_sgemm(g, m->stream); }));
   g.B = m->enc_rw;
   g.C = x;
   g.bias = m->enc_rb;
   g.bias2 = m->enc_ob;
   g.bias3 = m->temb;  // row 0: TARGET type embedding (every patch of a target row)
   g.relu = 0;
-  LAUNCH(t0b_launch_sgemm(g, m->stream));
+  LAUNCH(launch(m, KC_SGEMM, 2.0 * g.M * g.N * g.K, 0.0, [&] { return t0b_launch_sgemm(g, m->stream); }));
   g.A = hid;
   g.lda = E;
   g.B = m->enc_ow;
@@ -513,9 +584,11 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   g.K = E;
   g.bias = g.bias2 = g.bias3 = nullptr;
   g.accumulate = 1;
-  LAUNCH(t0b_launch_sgemm(g, m->stream));
-  LAUNCH(t0b_launch_rownorm_split(x, m->layers[0].g_attn, m->xh.as<__half>(), m->xl.as<__half>(), m->ssq.as<float>(),
-                                  (int)T, E, m->stream));
+  LAUNCH(launch(m, KC_SGEMM, 2.0 * g.M * g.N * g.K, 0.0, [&] { return t0b_launch_sgemm(g, m->stream); }));
+  LAUNCH(launch(m, KC_OTHER, 0.0, T * E * 8.0, [&] {
+    return t0b_launch_rownorm_split(x, m->layers[0].g_attn, m->xh.as<__half>(), m->xl.as<__half>(),
+                                    m->ssq.as<float>(), (int)T, E, m->stream);
+  }));
   int ssq_nt = 1;
 
   AttnArgs aa{};
@@ -531,7 +604,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   aa.H = m->H;
   aa.n_series = ns;
   const int M = (int)T;
-  const int resid_nt = use_tc(m, M) ? E / 256 : E / 64;
+  const int resid_nt = use_tc(m, M) ? E / t0b_tc_tile_width() : E / 64;
 
   for (int l = 0; l < m->L; ++l) {
     const LayerW &w = m->layers[l];
@@ -549,11 +622,18 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
     e.rcos = rope;
     e.rsin = rope + (size_t)p * 64;
     e.rsc = rope + (size_t)2 * p * 64;
+    e.rsc_inv = rope + (size_t)3 * p * 64;
     e.p = p;
     e.E = E;
     e.rope = w.group ? 0 : 1;
     LAUNCH(qgemm(m, m->xh.as<__half>(), m->xl.as<__half>(), M, E, w.wqkv, 3 * E, w.sh_qkv, e));
-    LAUNCH(w.group ? t0b_launch_attn_group(aa, m->stream) : t0b_launch_attn_time(aa, m->stream));
+    if (w.group) {
+      LAUNCH(launch(m, KC_ATTN_GROUP, 0.0, T * (3.0 * E * 4 + E * 4.0), [&] { return t0b_launch_attn_group(aa, m->stream); }));
+    } else {
+      // causal pairs per row: p(p+1)/2, each 2*hd flops for q.k and 2*hd for p.v, per head
+      const double fl = (double)R * m->H * (p * (p + 1) / 2.0) * 4.0 * 64.0;
+      LAUNCH(launch(m, KC_ATTN_TIME, fl, T * (3.0 * E * 4 + E * 4.0), [&] { return t0b_launch_attn_time(aa, m->stream); }));
+    }
 
     Epi r{};
     r.kind = EPI_RESID;
@@ -589,7 +669,8 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
 
   // decoder on the output patches only: rmsnorm(out_norm) -> residual block
   const int nout = R * hp;
-  LAUNCH(t0b_launch_dec_gather(x, m->out_g, m->xo.as<float>(), R, p, hp, E, m->stream));
+  LAUNCH(launch(m, KC_OTHER, 0.0, nout * E * 8.0,
+                [&] { return t0b_launch_dec_gather(x, m->out_g, m->xo.as<float>(), R, p, hp, E, m->stream); }));
   SgemmArgs d{};
   d.A = m->xo.as<float>();
   d.lda = E;
@@ -602,7 +683,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   d.K = E;
   d.bias = m->dec_hb;
   d.relu = 1;
-  LAUNCH(t0b_launch_sgemm(d, m->stream));
+  LAUNCH(launch(m, KC_SGEMM, 2.0 * d.M * d.N * d.K, 0.0, [&] { return t0b_launch_sgemm(d, m->stream); }));
   d.B = m->dec_rw;
   d.C = m->dout.as<float>();
   d.ldc = m->dec_out;
@@ -610,14 +691,16 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   d.bias = m->dec_rb;
   d.bias2 = m->dec_ob;
   d.relu = 0;
-  LAUNCH(t0b_launch_sgemm(d, m->stream));
+  LAUNCH(launch(m, KC_SGEMM, 2.0 * d.M * d.N * d.K, 0.0, [&] { return t0b_launch_sgemm(d, m->stream); }));
   d.A = m->dhid.as<float>();
   d.B = m->dec_ow;
   d.bias = d.bias2 = nullptr;
   d.accumulate = 1;
-  LAUNCH(t0b_launch_sgemm(d, m->stream));
-  LAUNCH(t0b_launch_dec_head(m->dout.as<float>(), m->loc.as<float>(), m->scl.as<float>(), ps.out, nullptr, R, hp,
-                             ps.horizon, m->nq, m->info.scaler_use_arcsinh, m->stream));
+  LAUNCH(launch(m, KC_SGEMM, 2.0 * d.M * d.N * d.K, 0.0, [&] { return t0b_launch_sgemm(d, m->stream); }));
+  LAUNCH(launch(m, KC_OTHER, 0.0, (double)nout * m->dec_out * 8.0, [&] {
+    return t0b_launch_dec_head(m->dout.as<float>(), m->loc.as<float>(), m->scl.as<float>(), ps.out, nullptr, R, hp,
+                               ps.horizon, m->nq, m->info.scaler_use_arcsinh, m->stream);
+  }));
   return T0B_OK;
 }
 
@@ -766,6 +849,33 @@ extern "C" t0b_status t0b_model_set_max_tokens(t0b_model *m, size_t max_tokens) 
   m->max_tokens = max_tokens;
   return T0B_OK;
 }
+
+extern "C" t0b_status t0b_model_profile_enable(t0b_model *m, int on) {
+  if (!m) return fail(T0B_ERR_INVALID, "t0b_model_profile_enable: NULL model");
+  CUDA_TRY(cudaSetDevice(m->eng->device));
+  CUDA_TRY(cudaStreamSynchronize(m->stream));
+  fold_records(m);
+  std::memset(m->stats, 0, sizeof(m->stats));
+  for (int i = 0; i < KC_N; ++i) std::snprintf(m->stats[i].name, sizeof(m->stats[i].name), "%s", kKcNames[i]);
+  m->prof = on != 0;
+  return T0B_OK;
+}
+
+extern "C" t0b_status t0b_model_profile_read(t0b_model *m, t0b_kernel_stats *out, int max_classes, int *n_classes) {
+  if (!m || !out || !n_classes) return fail(T0B_ERR_INVALID, "t0b_model_profile_read: NULL argument");
+  CUDA_TRY(cudaSetDevice(m->eng->device));
+  CUDA_TRY(cudaStreamSynchronize(m->stream));
+  fold_records(m);
+  const int n = std::min(max_classes, (int)KC_N);
+  for (int i = 0; i < n; ++i) {
+    out[i] = m->stats[i];
+    std::snprintf(out[i].name, sizeof(out[i].name), "%s", kKcNames[i]);
+  }
+  *n_classes = n;
+  return T0B_OK;
+}
+
+extern "C" uint64_t t0b_model_launch_count(const t0b_model *m) { return m ? m->launches : 0; }
 
 extern "C" t0b_status t0b_model_sync(t0b_model *m) {
   if (!m) return fail(T0B_ERR_INVALID, "t0b_model_sync: NULL model");

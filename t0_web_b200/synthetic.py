@@ -119,17 +119,22 @@ def multiseries(n_series: int, t_ctx: int, seed: int = 0, n_variates: int | tupl
     else:
         nv = np.full(n_series, int(n_variates), np.int32)
     rows = int(nv.sum())
-    t = np.arange(t_ctx, dtype=np.float64)[None, :]
+    # per-row parameters first, then the values in row chunks (bounded memory)
     k = rng.integers(2, 4, size=(rows, 1))
-    x = np.zeros((rows, t_ctx), np.float64)
-    for j in range(3):
-        period = rng.uniform(7.0, 168.0, size=(rows, 1))
-        amp = rng.uniform(0.5, 2.0, size=(rows, 1)) * (j < k)
-        phase = rng.uniform(0.0, 2.0 * np.pi, size=(rows, 1))
-        x += amp * np.sin(2.0 * np.pi * t / period + phase)
+    period = rng.uniform(7.0, 168.0, size=(3, rows, 1))
+    amp = rng.uniform(0.5, 2.0, size=(3, rows, 1)) * (np.arange(3)[:, None, None] < k[None])
+    phase = rng.uniform(0.0, 2.0 * np.pi, size=(3, rows, 1))
     slope = rng.uniform(-1.0, 1.0, size=(rows, 1))
-    x += slope * t / t_ctx + rng.uniform(-1.0, 1.0, size=(rows, 1))
-    x += 0.2 * rng.standard_normal((rows, t_ctx))
+    offset = rng.uniform(-1.0, 1.0, size=(rows, 1))
+    x = np.empty((rows, t_ctx), np.float32)
+    t = np.arange(t_ctx, dtype=np.float64)[None, :]
+    for c0 in range(0, rows, 1024):
+        c1 = min(rows, c0 + 1024)
+        acc = slope[c0:c1] * (t / t_ctx) + offset[c0:c1]
+        for j in range(3):
+            acc += amp[j, c0:c1] * np.sin((2.0 * np.pi / period[j, c0:c1]) * t + phase[j, c0:c1])
+        acc += 0.2 * rng.standard_normal((c1 - c0, t_ctx))
+        x[c0:c1] = acc
     gap = int(round(gap_frac * t_ctx))
     if gap > 0:
         r0 = 0
@@ -137,7 +142,7 @@ def multiseries(n_series: int, t_ctx: int, seed: int = 0, n_variates: int | tupl
             start = int(rng.integers(0, t_ctx - gap + 1))
             x[r0:r0 + nv[s], start:start + gap] = np.nan
             r0 += int(nv[s])
-    return x.astype(np.float32), nv
+    return x, nv
 
 
 def gemm_case(N: int, K: int, M: int, seed: int = 0) -> tuple[np.ndarray, np.ndarray]:

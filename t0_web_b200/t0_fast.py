@@ -29,7 +29,7 @@ import ctypes as C
 
 import numpy as np
 
-from ._lib import ModelInfo, T0bError, check, lib, ptr
+from ._lib import KernelStats, ModelInfo, T0bError, check, lib, ptr
 
 DEFAULT_BATCH_CHUNK = 16  # lib.rs:32
 MAX_HORIZON = 1024  # model.rs:26
@@ -96,6 +96,20 @@ class GpuModel:
 
     def sync(self) -> None:
         check(lib().t0b_model_sync(self._h))
+
+    def profile(self, on: bool = True) -> None:
+        """Bracket every kernel launch with CUDA events (resets statistics)."""
+        check(lib().t0b_model_profile_enable(self._h, int(on)))
+
+    def profile_read(self) -> dict[str, dict]:
+        arr = (KernelStats * 8)()
+        n = C.c_int(0)
+        check(lib().t0b_model_profile_read(self._h, arr, 8, C.byref(n)))
+        return {arr[i].name.decode(): dict(launches=int(arr[i].launches), total_ms=arr[i].total_ms,
+                                           flops=arr[i].flops, bytes=arr[i].bytes) for i in range(n.value)}
+
+    def launch_count(self) -> int:
+        return int(lib().t0b_model_launch_count(self._h))
 
     def close(self):
         if getattr(self, "_h", None):
