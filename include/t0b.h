@@ -146,6 +146,35 @@ t0b_status t0b_swiglu_q(t0b_engine *e, int ggml_type, const void *w0_dev, const 
                         int N2, const float *x_dev, int M, const float *b0_dev, const float *b2_dev,
                         float *z_dev, float *y_dev, void *stream);
 
+/* ---- no-allocation dequant-GEMM (no reference counterpart) ----
+ * The product of t0b_gemm_q, same arguments minus the engine, computed on
+ * the calling thread's current device without allocating any device memory:
+ * the split f16 copy of x, the weight-scale reduction word and the kernel
+ * error word live in one fixed array compiled into the library
+ * (T0B_NOALLOC_SCRATCH_BYTES per device, reserved when the library's device
+ * code is loaded on that device).  Meant for hosts that cannot allocate at
+ * call time: a process that has handed all of HBM to its own arena up front,
+ * or a serving loop that must not pay cudaMalloc/cudaFree latency and their
+ * implicit device-wide synchronisation in the middle of a request.
+ *
+ * Limits and rules:
+ *  - M * K <= T0B_NOALLOC_MAX_X_ELEMENTS, else T0B_ERR_INVALID (nothing runs);
+ *    K % 256 == 0 and N % 256 == 0 as for t0b_gemm_q.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress, with that device current) and caches it; make
+ *    that first call before capturing the stream into a graph.
+ *  - All calls on one device share the array.  Each call clears the two
+ *    control words it needs zeroed and overwrites the x copy before reading
+ *    it, so no state carries over from one call to the next; but calls that
+ *    overlap in time on one device (several host threads, or work enqueued
+ *    on other streams before this call returns) race on it and must be
+ *    serialised by the caller.  Each call synchronises `stream` before it
+ *    returns. */
+#define T0B_NOALLOC_MAX_X_ELEMENTS ((size_t)1 << 22)
+#define T0B_NOALLOC_SCRATCH_BYTES ((size_t)256 + 4 * T0B_NOALLOC_MAX_X_ELEMENTS)
+t0b_status t0b_gemm_q_noalloc(int ggml_type, const void *w_dev, int N, int K, const float *x_dev, int M,
+                              const float *bias_dev, float *y_dev, void *stream);
+
 /* ---- host codecs (gguf.rs) ---- */
 /* Parse and validate a GGUF file without a device: gguf::read_gguf
  * (gguf.rs:347-405) + config_from_gguf_metadata (weights.rs:69-112) + the

@@ -12,6 +12,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1082,6 +1083,97 @@ extern "C" t0b_status t0b_swiglu_q(t0b_engine *e, int ggml_type, const void *w0_
   CUDA_TRY(engine_qgemm(qt, e->scratch_zh.as<__half>(), e->scratch_zl.as<__half>(), M, F, (const uint8_t *)w2_dev, N2,
                         sh2, dn, e->d_err, st));
   return engine_check(e, st);
+}
+
+// ================================================ no-allocation standalone GEMM
+// t0b_gemm_q_noalloc works out of one fixed array that is part of this
+// library's device code, so a call allocates nothing.  Layout:
+//   bytes [0, 4)              absmax bits of the weight-block scales
+//   bytes [4, 8)              kernel error word
+//   bytes [256, 256 + 2X)     hi f16 half of x   (X = T0B_NOALLOC_MAX_X_ELEMENTS)
+//   bytes [256 + 2X, 256 + 4X) lo f16 half of x
+// Both control words must be zero when the kernels that use them start: the
+// absmax launcher clears its word on the stream, and the call clears the
+// error word first.  The x halves are written in full before they are read.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[T0B_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+unsigned char *g_noalloc_addr[kNoallocMaxDevices];  // per device ordinal, filled on first use
+
+// Device address of the scratch array on the current device (looked up once
+// per device, with that device current).
+t0b_status noalloc_scratch(unsigned char **out) {
+  int dev = -1;
+  CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoallocMaxDevices)
+    return fail(T0B_ERR_UNSUPPORTED, "t0b_gemm_q_noalloc: device ordinal " + std::to_string(dev) + " out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    int major = 0, minor = 0;
+    CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    CUDA_TRY(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+    if (major != 10 || minor != 0)
+      return fail(T0B_ERR_UNSUPPORTED, "t0b_gemm_q_noalloc: built for sm_100a (B200); device is sm_" +
+                                           std::to_string(major) + std::to_string(minor));
+    unsigned char *p = nullptr;
+    CUDA_TRY(cudaGetSymbolAddress((void **)&p, g_noalloc_scratch));
+    if (!p || (reinterpret_cast<uintptr_t>(p) & 255))
+      return fail(T0B_ERR_CUDA, "t0b_gemm_q_noalloc: scratch array address is not 256-byte aligned");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return T0B_OK;
+}
+}  // namespace
+
+extern "C" t0b_status t0b_gemm_q_noalloc(int ggml_type, const void *w_dev, int N, int K, const float *x_dev, int M,
+                                         const float *bias_dev, float *y_dev, void *stream) {
+  if (!w_dev || !x_dev || !y_dev) return fail(T0B_ERR_INVALID, "t0b_gemm_q_noalloc: NULL argument");
+  const int qt = qt_of(ggml_type);
+  if (!qt) return fail(T0B_ERR_UNSUPPORTED, "t0b_gemm_q_noalloc: weight type must be Q8_0 or Q4_0");
+  if (M < 1 || N < 1 || K < 1) return fail(T0B_ERR_INVALID, "t0b_gemm_q_noalloc: empty shape");
+  if (K % 256) return fail(T0B_ERR_UNSUPPORTED, "t0b_gemm_q_noalloc: K must be a multiple of 256");
+  if (N % 256) return fail(T0B_ERR_UNSUPPORTED, "t0b_gemm_q_noalloc: N must be a multiple of 256");
+  const size_t n_x = (size_t)M * (size_t)K;
+  if (n_x > T0B_NOALLOC_MAX_X_ELEMENTS)
+    return fail(T0B_ERR_INVALID, "t0b_gemm_q_noalloc: M*K = " + std::to_string(n_x) + " exceeds the fixed scratch (" +
+                                     std::to_string((size_t)T0B_NOALLOC_MAX_X_ELEMENTS) + " elements of x)");
+  unsigned char *base = nullptr;
+  t0b_status s = noalloc_scratch(&base);
+  if (s != T0B_OK) return s;
+  unsigned int *red = reinterpret_cast<unsigned int *>(base);
+  int *err = reinterpret_cast<int *>(base + 4);
+  __half *xh = reinterpret_cast<__half *>(base + 256);
+  __half *xl = xh + T0B_NOALLOC_MAX_X_ELEMENTS;
+  cudaStream_t st = (cudaStream_t)stream;
+  CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
+  CUDA_TRY(t0b_launch_split_f32(x_dev, xh, xl, n_x, st));
+  // weight prescale exponent from the largest block scale (clears `red` first)
+  CUDA_TRY(t0b_launch_absmax_scale((const uint8_t *)w_dev, (size_t)N * K / 32, qt == 8 ? 34 : 18, red, st));
+  unsigned int bits = 0;
+  CUDA_TRY(cudaMemcpyAsync(&bits, red, sizeof(bits), cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  float maxd;
+  std::memcpy(&maxd, &bits, 4);
+  const int sh = t0b_weight_shift(maxd, qt);
+  Epi ep{};
+  ep.kind = EPI_PLAIN;
+  ep.M = M;
+  ep.N = N;
+  ep.bias = bias_dev;
+  ep.y = y_dev;
+  ep.ldy = N;
+  if (M >= 128)
+    CUDA_TRY(t0b_launch_gemm_tc(qt, xh, xl, M, K, (const uint8_t *)w_dev, N, sh, ep, err, st));
+  else
+    CUDA_TRY(t0b_launch_gemm_small(qt, xh, xl, M, K, (const uint8_t *)w_dev, ep, err, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  int herr = 0;
+  CUDA_TRY(cudaMemcpy(&herr, err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (herr) return fail(T0B_ERR_DEVICE, "t0b_gemm_q_noalloc: a kernel reported device error code " + std::to_string(herr));
+  return T0B_OK;
 }
 
 // ============================================================ host codecs
