@@ -311,12 +311,28 @@ t0b_status parse_config(const t0b::GgufFile &f, t0b_model *m) {
   NEED("decoder.mlp.hidden_layer.weight", E, E, false);
   NEED("decoder.mlp.output_layer.weight", P * nq, E, false);
   NEED("decoder.residual_layer.weight", P * nq, E, false);
+  // 1-D tensors (c == 0: element count only)
+  NEED("patch_encoder.projection.mlp.hidden_layer.bias", E, 0, false);
+  NEED("patch_encoder.projection.mlp.output_layer.bias", E, 0, false);
+  NEED("patch_encoder.projection.residual_layer.bias", E, 0, false);
+  NEED("transformer.out_norm.scale", E, 0, false);
+  NEED("decoder.mlp.hidden_layer.bias", E, 0, false);
+  NEED("decoder.mlp.output_layer.bias", P * nq, 0, false);
+  NEED("decoder.residual_layer.bias", P * nq, 0, false);
   for (int l = 0; l < m->L; ++l) {
     const std::string p = "transformer.layers." + std::to_string(l);
     NEED(p + ".attention_block.attention.wQKV.weight", 3 * E, E, true);
     NEED(p + ".attention_block.attention.wO.weight", E, E, true);
     NEED(p + ".mlp.0.weight", 2 * F, E, true);
     NEED(p + ".mlp.2.weight", E, F, true);
+    NEED(p + ".attention_block.norm.scale", E, 0, false);
+    NEED(p + ".attention_block.attention.wQKV.bias", 3 * E, 0, false);
+    NEED(p + ".attention_block.attention.wO.bias", E, 0, false);
+    NEED(p + ".attention_block.attention.q_norm.scale", E / m->H, 0, false);
+    NEED(p + ".attention_block.attention.k_norm.scale", E / m->H, 0, false);
+    NEED(p + ".norm.scale", E, 0, false);
+    NEED(p + ".mlp.0.bias", 2 * F, 0, false);
+    NEED(p + ".mlp.2.bias", E, 0, false);
   }
 #undef NEED
   if (m->info.weight_type == -1) return fail(T0B_ERR_FORMAT, "gguf: model has no layers");

@@ -33,8 +33,9 @@ ALPHA = dict(
     scaler_eps_mode="variance_offset",
 )
 
-# A small model of the same family for quick CPU checks.
-TINY = dict(ALPHA, embed_dim=64, num_layers=3, num_heads=2, mlp_hidden_dim=128)
+# The smallest model of the same family the engine runs (head_dim 64,
+# embed_dim and mlp_hidden_dim multiples of 256): quick CPU checks and fixtures.
+TINY = dict(ALPHA, embed_dim=256, num_layers=3, num_heads=4, mlp_hidden_dim=256)
 
 
 def tensor_shapes(cfg: dict) -> list[tuple[str, tuple[int, ...]]]:

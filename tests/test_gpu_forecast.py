@@ -111,3 +111,20 @@ def test_model_bytes(gpu_model):
     assert m.quantizable_gpu_bytes() == 106_954_752  # 100,663,296 values x 34/32
     assert gpu_model("q4_0").quantizable_gpu_bytes() == 56_623_104
     assert m.total_weight_bytes() > m.quantizable_gpu_bytes()
+
+
+@pytest.mark.parametrize("quant", ["q8_0", "q4_0"])
+def test_tiny_model_matches_golden_fixture(engine, quant):
+    """The committed oracle outputs of tests/golden/tiny_forecast.npz (made by
+    tests/golden/make_golden.py) for the TINY model: no oracle call at run time."""
+    import os
+    from t0_web_b200 import gguf
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "tiny_forecast.npz"))
+    m = t0_fast.load_model_from_gguf(engine, gguf.export_gguf(S.random_weights(S.TINY, seed=0), S.TINY, quant))
+    try:
+        got = t0_fast.forecast(engine, m, g["sine_ctx"], 1, 77, 30)
+        assert max_abs(got, g[quant + "_sine"]) <= TOL
+        got = t0_fast.forecast_multiseries(engine, m, g["multi_ctx"], g["multi_nv"], 96, 40)
+        assert max_abs(got, g[quant + "_multi"]) <= TOL
+    finally:
+        m.close()
