@@ -85,6 +85,19 @@ T0B_DEV void tma_load_2d(void *dst, const void *tmap, uint64_t *bar, int x, int 
       "l"((uint64_t)tmap), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
+// 2-D tiled bulk tensor store shared -> global (bulk-group completion).
+// Rows or columns outside the tensor are not written.  x * element size
+// must be a multiple of 16 bytes and x, y >= 0 (callers guarantee both).
+T0B_DEV void tma_store_2d(const void *tmap, const void *src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"((uint64_t)tmap),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+T0B_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until no committed bulk store still reads shared memory.
+T0B_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until every committed bulk store has completed.
+T0B_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 T0B_DEV void prefetch_tmap(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)tmap) : "memory");
 }
@@ -127,6 +140,19 @@ T0B_DEV void tmem_ld32(uint32_t taddr, float *v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane.
+T0B_DEV void tmem_ld16(uint32_t taddr, float *v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows of 128 B

@@ -10,7 +10,7 @@
 
 #include "common.cuh"
 
-enum : int { EPI_PLAIN = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_SWIGLU = 3 };
+enum : int { EPI_PLAIN = 0, EPI_RESID = 2, EPI_SWIGLU = 3 };
 
 struct Epi {
   int kind;
@@ -20,14 +20,9 @@ struct Epi {
   // un-normalised row, ssq_in[m * ssq_in_nt + slot], over ssq_dim columns
   const float *ssq_in;
   int ssq_in_nt, ssq_dim;
-  // EPI_PLAIN: y [M, ldy]
+  // EPI_PLAIN: y [M, ldy] = acc / row denominator + bias
   float *y;
   int ldy;
-  // EPI_QKV: y = fused q|k|v buffer [M, 3E]; per-head RMSNorm with qn / kn
-  // (eps 1e-8, ops.rs:175-177), then xpos RoPE (tables [p, hd], TIME layers
-  // only: rope != 0) with the k side using 1/scale (ops.rs:132-142).
-  const float *qn, *kn, *rcos, *rsin, *rsc, *rsc_inv;
-  int p, E, rope;
   // EPI_RESID: x[m, n] += acc + bias (f32 residual stream, in place); then
   // x*gnext split into f16 (xh, xl) for the next RMSNorm-fused GEMM and the
   // sum of x^2 over this thread's columns written to ssq_out[m*nt + slot].
@@ -92,43 +87,6 @@ T0B_DEV float epi_cols32(const Epi &e, int m, int n0, float *v, float denom) {
   }
   store_split(e.xh, e.xl, (size_t)m * e.N + n0, g, 32);
   return ss;
-}
-
-// One attention head (64 columns n0..n0+63, n0 % 64 == 0) of the QKV output,
-// bias and row scale already applied: q/k get their per-head RMSNorm and,
-// on TIME layers, xpos RoPE; v is stored as is.
-T0B_DEV void epi_qkv64_nobias(const Epi &e, int m, int n0, float *v) {
-  const int seg = n0 / e.E;  // 0 = q, 1 = k, 2 = v
-  if (seg < 2) {
-    const float *g = seg == 0 ? e.qn : e.kn;
-    float s = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 64; ++i) s += v[i] * v[i];
-    const float rdn = 1.0f / sqrtf(s / 64.0f + 1e-8f);
-#pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] = v[i] * rdn * g[i];
-    if (e.rope) {
-      const int pos = m % e.p;
-      const float *c = e.rcos + pos * 64, *sn = e.rsin + pos * 64;
-      const float *sc = (seg == 0 ? e.rsc : e.rsc_inv) + pos * 64;  // k uses 1/scale
-#pragma unroll
-      for (int d = 0; d < 64; d += 2) {  // adjacent pair (x0, x1) -> (x0 c - x1 s, x1 c + x0 s) * scale
-        const float x0 = v[d], x1 = v[d + 1];
-        v[d] = x0 * c[d] * sc[d] + (-x1) * sn[d] * sc[d];
-        v[d + 1] = x1 * c[d + 1] * sc[d + 1] + x0 * sn[d + 1] * sc[d + 1];
-      }
-    }
-  }
-  float4 *dst = reinterpret_cast<float4 *>(e.y + (size_t)m * 3 * e.E + n0);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-}
-
-T0B_DEV void epi_qkv64(const Epi &e, int m, int n0, float *v, float denom) {
-  const float rinv = 1.0f / denom;
-#pragma unroll
-  for (int i = 0; i < 64; ++i) v[i] = v[i] * rinv + e.bias[n0 + i];
-  epi_qkv64_nobias(e, m, n0, v);
 }
 
 // SwiGLU pair: gate columns f0..f0+31 and the matching up columns.

@@ -166,9 +166,7 @@ __global__ void __launch_bounds__(128) gemm_q_small_kernel(const __half *__restr
     float v[64];
 #pragma unroll
     for (int r = 0; r < 64; ++r) v[r] = tile[r * LD + t];
-    if (epi.kind == EPI_QKV) {
-      epi_qkv64(epi, m, blockIdx.x * 64, v, denom);
-    } else if (epi.kind == EPI_SWIGLU) {
+    if (epi.kind == EPI_SWIGLU) {
       epi_swiglu32(epi, m, blockIdx.x * 32, v, v + 32, denom);
     } else {
       float ss = epi_cols32(epi, m, blockIdx.x * 64, v, denom);

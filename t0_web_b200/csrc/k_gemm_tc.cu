@@ -15,22 +15,27 @@
 // activation tiles in L2).  One 32-value block column of K per pipeline
 // stage; separate rings for the activation tiles (TMA, 64-byte swizzle), the
 // raw weight blocks (TMA) and the dequantized weight tiles.  The two
-// accumulators fill all 512 TMEM columns, so the epilogue drains them into
-// registers first and hands TMEM back to the MMA warp before doing its math
-// and stores, which then overlap the next tile's MMAs.
+// accumulators fill all 512 TMEM columns; the epilogue reads them chunk by
+// chunk and releases TMEM to the next tile's MMAs when done.  Its only
+// global load is the row's RMSNorm sum of squares, fetched before the
+// accumulator is ready (the bias is staged in shared memory), and its
+// global writes are asynchronous TMA stores of swizzled 32-row chunks, so its
+// cost is a short burst of TMEM loads, math and shared-memory stores.
+// Residual adds, QK-norm and RoPE run in the row kernels that consume these
+// outputs.
 //
-// Warp roles (512 threads, four warpgroups, registers rebalanced with
-// setmaxnreg):
+// Warp roles (640 threads):
 //   warp 0      TMA producer: Ah/Al tiles and the raw blocks of the tile's
 //               weight rows (16-byte aligned superset window of the 34/18-byte
 //               block), with mbarrier completion.
 //   warp 1      allocates 512 TMEM columns; lane 0 issues tcgen05.mma and
 //               tcgen05.commit.
-//   warps 4-7   dequantize raw blocks -> Wh/Wl tiles in the canonical K-major
-//               SW64 layout (generic stores + proxy fence).
-//   warps 8-15  epilogue, two warps per TMEM lane quadrant (128 columns
-//               each): fused bias / RMSNorm row scale / QK-norm + RoPE /
-//               residual / SwiGLU, 16-byte stores.
+//   warps 4-11  dequantize raw blocks (one weight row per thread per stage)
+//               -> Wh/Wl tiles in the canonical K-major SW64 layout (generic
+//               stores + proxy fence).
+//   warps 12-19 epilogue, two warps per TMEM lane quadrant (128 columns
+//               each): bias + RMSNorm row scale (PLAIN) or SwiGLU, staged
+//               in shared memory and written by TMA stores.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -39,15 +44,16 @@
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 32;  // BK: one Q8_0/Q4_0 block column of K per stage
-constexpr int XS = 5, WS = 3, RS = 3;
-constexpr int NTHREADS = 512;
+constexpr int XS = 4, WS = 3, RS = 3;       // ring depths: activation, dequantized weight, raw weight
+constexpr int NTHREADS = 640;
 constexpr uint32_t X_TILE = BM * BK * 2;  // 8 KB, one of hi / lo
 constexpr uint32_t W_TILE = BN * BK * 2;  // 16 KB, one of hi / lo
 constexpr uint32_t OFF_XH = 0;
 constexpr uint32_t OFF_XL = OFF_XH + XS * X_TILE;
 constexpr uint32_t OFF_WH = OFF_XL + XS * X_TILE;
 constexpr uint32_t OFF_WL = OFF_WH + WS * W_TILE;
-constexpr uint32_t OFF_RAW = OFF_WL + WS * W_TILE;  // 176 KB
+constexpr uint32_t OFF_RAW = OFF_WL + WS * W_TILE;  // 160 KB
+constexpr uint32_t STG_BYTES = 2048;                // per epilogue warp: one 32-row output chunk
 
 template <int QT>
 struct TQ;
@@ -63,9 +69,12 @@ struct TQ<4> {
 template <int QT>
 struct Cfg {
   static constexpr uint32_t RAW_SLOT = (uint32_t)TQ<QT>::rawb * BN;
-  static constexpr uint32_t OFF_EPI = OFF_RAW + RS * RAW_SLOT;  // tile bias + gains for the epilogue
-  static constexpr uint32_t OFF_BAR = OFF_EPI + 2 * BN * 4;
-  static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;       // barriers + alignment slack
+  static constexpr uint32_t OFF_EPI = OFF_RAW + RS * RAW_SLOT;  // tile bias for the epilogue
+  // output staging for the TMA stores, 1024-aligned (swizzle pattern period)
+  static constexpr uint32_t OFF_STG = (OFF_EPI + BN * 4 + 1023u) & ~1023u;
+  static constexpr uint32_t OFF_BAR = OFF_STG + 8 * STG_BYTES;
+  static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;  // barriers + alignment slack
+  static_assert(SMEM <= 232448, "shared memory over the 227 KB per-block limit");
 };
 
 struct TcParams {
@@ -79,19 +88,19 @@ struct TcParams {
   int *err;
 };
 
-// 32 columns of (main + correction) accumulator for this thread's row.
-T0B_DEV void tmem_ld_pair(uint32_t taddr, float *v, float scale) {
-  float c[32];
-  tmem_ld32(taddr, v);
-  tmem_ld32(taddr + BN, c);
+// 16 columns of (main + correction) accumulator for this thread's row.
+T0B_DEV void tmem_ld_pair16(uint32_t taddr, float *v, float scale) {
+  float c[16];
+  tmem_ld16(taddr, v);
+  tmem_ld16(taddr + BN, c);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = (v[i] + c[i]) * scale;
+  for (int i = 0; i < 16; ++i) v[i] = (v[i] + c[i]) * scale;
 }
 
-// 32 values as f16 hi/lo pairs, 8 per 16-byte store.
-T0B_DEV void store_split32(__half *hi, __half *lo, size_t off, const float *v) {
+// 16 values as f16 hi/lo pairs, 8 per 16-byte store.
+T0B_DEV void store_split16(__half *hi, __half *lo, size_t off, const float *v) {
 #pragma unroll
-  for (int i = 0; i < 32; i += 8) {
+  for (int i = 0; i < 16; i += 8) {
     uint32_t h[4], l[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -107,10 +116,10 @@ T0B_DEV void store_split32(__half *hi, __half *lo, size_t off, const float *v) {
   }
 }
 
-T0B_DEV void store_f32x32(float *dst, const float *v) {
+T0B_DEV void store_f32x16(float *dst, const float *v) {
   float4 *d = reinterpret_cast<float4 *>(dst);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  for (int i = 0; i < 4; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 }
 
 // Dequantize one 32-value block of one weight row (raw window `src`, block
@@ -119,6 +128,7 @@ T0B_DEV void store_f32x32(float *dst, const float *v) {
 template <int QT>
 T0B_DEV void dequant_block(const uint8_t *src, int off, float wscale, uint32_t *hv, uint32_t *lv) {
   constexpr int RAWB = TQ<QT>::rawb;
+  constexpr int NW = QT == 8 ? 8 : 4;  // 32-bit words of quants in a block
   uint32_t wv[RAWB / 4 + 1];
 #pragma unroll
   for (int i = 0; i < RAWB / 16; ++i) {
@@ -129,11 +139,23 @@ T0B_DEV void dequant_block(const uint8_t *src, int off, float wscale, uint32_t *
     wv[4 * i + 3] = q4.w;
   }
   wv[RAWB / 4] = 0u;
-  auto word_at = [&](int byte) -> uint32_t {  // 4 bytes starting at `byte`
-    int w = byte >> 2, sh = (byte & 3) * 8;
-    return sh ? __funnelshift_r(wv[w], wv[w + 1], sh) : wv[w];
+  // `off` is even (34 s mod 16 or 18 s mod 16), so every 2-byte field sits in
+  // one word and the quants start at a word offset of 0 or 16 bits.  The
+  // word index is picked with selects so wv stays in registers.
+  auto pick = [&](int base, int k) -> uint32_t {  // wv[base + k], base in [0, 4]
+    uint32_t v = wv[k];
+    v = base == 1 ? wv[k + 1] : v;
+    v = base == 2 ? wv[k + 2] : v;
+    v = base == 3 ? wv[k + 3] : v;
+    v = base == 4 ? wv[k + 4] : v;
+    return v;
   };
-  const uint32_t dbits = word_at(off) & 0xFFFFu;
+  const uint32_t dbits = (pick(off >> 2, 0) >> ((off & 3) * 8)) & 0xFFFFu;
+  const int qb = off + 2, w0 = qb >> 2, sh = (qb & 3) * 8;
+  uint32_t qa[NW + 1];
+#pragma unroll
+  for (int k = 0; k <= NW; ++k) qa[k] = pick(w0, k);
+  auto word_q = [&](int i) -> uint32_t { return __funnelshift_r(qa[i], qa[i + 1], sh); };  // quant bytes 4i..4i+3
   const __half dh = __float2half_rn(__half2float(__ushort_as_half((unsigned short)dbits)) * wscale);  // exact
   const __half2 d2 = __halves2half2(dh, dh);
   auto emit = [&](uint32_t qv, int pair) {
@@ -146,7 +168,7 @@ T0B_DEV void dequant_block(const uint8_t *src, int off, float wscale, uint32_t *
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       uint32_t a, b;
-      i8x4_to_h2x2(word_at(off + 2 + 4 * i), a, b);  // int8 values 4i..4i+3
+      i8x4_to_h2x2(word_q(i), a, b);  // int8 values 4i..4i+3
       emit(a, 2 * i);
       emit(b, 2 * i + 1);
     }
@@ -155,7 +177,7 @@ T0B_DEV void dequant_block(const uint8_t *src, int off, float wscale, uint32_t *
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint32_t r[4];
-      nib8_to_h2x4(word_at(off + 2 + 4 * i), r);
+      nib8_to_h2x4(word_q(i), r);
       emit(r[0], 2 * i);          // values 4i, 4i+1
       emit(r[1], 2 * i + 1);      // values 4i+2, 4i+3
       emit(r[2], 8 + 2 * i);      // values 16+4i, 16+4i+1
@@ -169,7 +191,9 @@ T0B_DEV void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }  // th
 template <int QT>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_q_tc_kernel(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
-                     const __grid_constant__ CUtensorMap tm_w, TcParams prm) {
+                     const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_y,
+                     const __grid_constant__ CUtensorMap tm_zh, const __grid_constant__ CUtensorMap tm_zl,
+                     TcParams prm) {
   using C = Cfg<QT>;
   constexpr int BPB = TQ<QT>::bpb, RAWB = TQ<QT>::rawb;
   extern __shared__ uint8_t smem_raw[];
@@ -201,10 +225,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int i = 0; i < RS; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], 128);
+      mbar_init(&raw_empty[i], 256);
     }
     for (int i = 0; i < WS; ++i) {
-      mbar_init(&w_full[i], 128);
+      mbar_init(&w_full[i], 256);
       mbar_init(&w_empty[i], 1);
     }
     mbar_init(acc_full, 1);
@@ -217,6 +241,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     prefetch_tmap(&tm_xh);
     prefetch_tmap(&tm_xl);
     prefetch_tmap(&tm_w);
+    if (swiglu) {
+      prefetch_tmap(&tm_zh);
+      prefetch_tmap(&tm_zl);
+    } else {
+      prefetch_tmap(&tm_y);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -240,9 +270,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   };
 
-  const int wg = warp >> 2;
-  if (wg == 0) {
-    regs_dealloc<40>();
+  if (warp < 4) {
     if (warp == 0 && lane == 0) {
       // ---------------------------------------------------------- producer
       uint32_t g = 0;  // global stage counter across tiles
@@ -295,9 +323,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         umma_commit(acc_full);
       }
     }
-  } else if (wg == 1) {
+  } else if (warp < 12) {
     // ------------------------------------------------------------ dequant
-    const int t = threadIdx.x - 128;  // 0..127
+    const int r = threadIdx.x - 128;  // tile row 0..255
     uint32_t g = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < prm.n_tiles && ok && !*abort_flag; tile += gridDim.x) {
@@ -312,9 +340,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         uint8_t *wls = smem + OFF_WL + ws * W_TILE;
         const int off = (s * BPB) & 15;  // block start inside the aligned window
         const uint8_t *slot = smem + OFF_RAW + rs * C::RAW_SLOT;
-#pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          const int r = t + 128 * rr;  // tile row 0..255
+        {
           uint32_t hv[16], lv[16];
           dequant_block<QT>(slot + r * RAWB, off, prm.wscale, hv, lv);
 #pragma unroll
@@ -331,114 +357,111 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    regs_alloc<168>();
-    const int q = warp & 3;              // TMEM lane quadrant this warp may access
-    const int half = (warp - 8) >> 2;    // which 128 of the tile's 256 columns
-    const int et = threadIdx.x - 256;    // 0..255
+    // Each warp owns 32 rows (its TMEM lane quadrant) x half the columns.  A
+    // chunk of 16 columns goes TMEM -> registers (bias, row scale, SwiGLU)
+    // -> this warp's swizzled staging buffer -> one TMA store by lane 0, so
+    // global writes are whole rows, asynchronous and clipped at row M.
+    const int q = warp & 3;             // TMEM lane quadrant this warp may access
+    const int half = (warp - 12) >> 2;  // which half of the tile's columns
+    const int et = threadIdx.x - 384;   // 0..255
     const Epi &e = prm.epi;
-    float *sb = epi_s;       // tile bias  [BN]
-    float *sg = epi_s + BN;  // tile gains [BN] (RESID: next norm gain)
+    float *sb = epi_s;  // tile bias [BN] (SWIGLU: 128 gate then 128 up)
+    uint8_t *stg = smem + C::OFF_STG + (warp - 12) * STG_BYTES;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < prm.n_tiles; tile += gridDim.x, ++it) {
       int m0, wr0, wr1, nt;
       tile_rows(tile, m0, wr0, wr1, nt);
-      epi_bar();  // every epilogue thread is done with the previous tile's constants
+      epi_bar();  // every epilogue thread is done with the previous tile's bias
       {
         const int c = et;  // 256 threads, 256 columns
-        if (swiglu) {
-          const int f = c < 128 ? nt * 128 + c : e.F + nt * 128 + (c - 128);
-          sb[c] = e.bias ? e.bias[f] : 0.0f;
-        } else {
-          sb[c] = e.bias ? e.bias[nt * BN + c] : 0.0f;
-          if (e.kind == EPI_RESID) sg[c] = e.gnext[nt * BN + c];
-        }
+        const int f = swiglu ? (c < 128 ? nt * 128 + c : e.F + nt * 128 + (c - 128)) : nt * BN + c;
+        sb[c] = e.bias ? e.bias[f] : 0.0f;
       }
       epi_bar();
-      const int m = m0 + 32 * q + lane;
+      const int row0 = m0 + 32 * q;
+      const int m = row0 + lane;
       const bool live = m < M;
       const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
+      // the row scale is fetched while the tile's MMAs are still running
+      const float sc = prm.acc_scale * (live ? 1.0f / epi_row_denom(e, m) : 1.0f);
       const bool have = mbar_wait(acc_full, it & 1, prm.err, T0B_DEVERR_WAIT_ACC, abort_flag) && !*abort_flag;
       tc_fence_after();
-      // drain: this thread's 128 accumulator columns into registers
-      // (SWIGLU: gate columns 64*half.. and the matching up columns)
-      float v[128];
-      const float rinv = (have && live) ? 1.0f / epi_row_denom(e, m) : 1.0f;
-      const float sc = prm.acc_scale * rinv;
-      const int c0 = swiglu ? 64 * half : 128 * half;
+      // no early exit: every epilogue thread runs every iteration so the
+      // named barrier above always sees all 256 of them (after an abort the
+      // waits return at once and no work is done)
       if (have) {
         if (swiglu) {
-          tmem_ld_pair(trow + c0, v, sc);
-          tmem_ld_pair(trow + c0 + 32, v + 32, sc);
-          tmem_ld_pair(trow + 128 + c0, v + 64, sc);
-          tmem_ld_pair(trow + 128 + c0 + 32, v + 96, sc);
-        } else {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {  // gate columns 64*half + 16c and the matching up columns
+            const int g0 = 64 * half + 16 * c;
+            float gv[16], uv[16];
+            tmem_ld_pair16(trow + g0, gv, sc);
+            tmem_ld_pair16(trow + 128 + g0, uv, sc);
+            uint32_t h[8], l[8];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) tmem_ld_pair(trow + c0 + 32 * c, v + 32 * c, sc);
+            for (int i = 0; i < 16; i += 2) {
+              float z[2];
+#pragma unroll
+              for (int k = 0; k < 2; ++k) {
+                const float gg = gv[i + k] + sb[g0 + i + k];
+                const float uu = uv[i + k] + sb[128 + g0 + i + k];
+                z[k] = gg / (1.0f + expf(-gg)) * uu;
+                gv[i + k] = z[k];
+              }
+              __half h0, l0, h1, l1;
+              split_f16(z[0], h0, l0);
+              split_f16(z[1], h1, l1);
+              __half2 hh = __halves2half2(h0, h1), ll = __halves2half2(l0, l1);
+              h[i / 2] = *reinterpret_cast<uint32_t *>(&hh);
+              l[i / 2] = *reinterpret_cast<uint32_t *>(&ll);
+            }
+            if (lane == 0) bulk_wait_read0();  // the previous chunk has left the staging buffer
+            __syncwarp();
+            // 32 rows x 32 bytes per half, 32-byte swizzle: 16-byte unit j of row r at r*32 + 16*(j ^ (r>>2 & 1))
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const uint32_t o = lane * 32 + ((j ^ ((lane >> 2) & 1)) << 4);
+              *reinterpret_cast<uint4 *>(stg + o) = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+              *reinterpret_cast<uint4 *>(stg + 1024 + o) =
+                  make_uint4(l[4 * j], l[4 * j + 1], l[4 * j + 2], l[4 * j + 3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tm_zh, stg, nt * 128 + g0, row0);
+              tma_store_2d(&tm_zl, stg + 1024, nt * 128 + g0, row0);
+              bulk_commit();
+            }
+            if (e.z32 && live) store_f32x16(e.z32 + (size_t)m * e.F + (size_t)nt * 128 + g0, gv);
+          }
+        } else {  // EPI_PLAIN
+#pragma unroll 1
+          for (int c = 0; c < 8; ++c) {
+            const int c0 = 128 * half + 16 * c;
+            float v[16];
+            tmem_ld_pair16(trow + c0, v, sc);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] += sb[c0 + i];
+            if (lane == 0) bulk_wait_read0();  // the previous chunk has left the staging buffer
+            __syncwarp();
+            // 32 rows x 64 bytes, 64-byte swizzle: 16-byte unit j of row r at r*64 + 16*(j ^ (r>>1 & 3))
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              *reinterpret_cast<float4 *>(stg + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                  make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tm_y, stg, nt * BN + c0, row0);
+              bulk_commit();
+            }
+          }
         }
       }
       tc_fence_before();
       mbar_arrive(acc_empty);  // TMEM is free for the next tile's MMAs
-      // no early exit: every epilogue thread runs every iteration so the
-      // named barrier above always sees all 256 of them (after an abort the
-      // waits return at once and no work is done)
-      if (!have || !live) continue;
-      if (e.kind == EPI_QKV) {
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float *vh = v + 64 * hh;
-#pragma unroll
-          for (int i = 0; i < 64; ++i) vh[i] += sb[c0 + 64 * hh + i];
-          epi_qkv64_nobias(e, m, nt * BN + c0 + 64 * hh, vh);
-        }
-      } else if (e.kind == EPI_SWIGLU) {
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float z[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float gg = v[32 * c + i] + sb[c0 + 32 * c + i];
-            const float uu = v[64 + 32 * c + i] + sb[128 + c0 + 32 * c + i];
-            z[i] = gg / (1.0f + expf(-gg)) * uu;
-          }
-          const size_t f0 = (size_t)nt * 128 + c0 + 32 * c;
-          if (e.zh) store_split32(e.zh, e.zl, (size_t)m * e.F + f0, z);
-          if (e.z32) store_f32x32(e.z32 + (size_t)m * e.F + f0, z);
-        }
-      } else if (e.kind == EPI_PLAIN) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[32 * c + i] += sb[c0 + 32 * c + i];
-          store_f32x32(e.y + (size_t)m * e.ldy + nt * BN + c0 + 32 * c, v + 32 * c);
-        }
-      } else {  // EPI_RESID: x += acc + bias; (x * gnext) split; sum of x^2
-        const int n0 = nt * BN + c0;
-        const float4 *xr = reinterpret_cast<const float4 *>(e.x + (size_t)m * e.N + n0);
-        float ss = 0.0f;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float4 xa[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) xa[i] = xr[8 * c + i];
-          float gx[32];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float xs4[4] = {xa[i].x, xa[i].y, xa[i].z, xa[i].w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int col = c0 + 32 * c + 4 * i + j;
-              const float xn = xs4[j] + (v[32 * c + 4 * i + j] + sb[col]);
-              v[32 * c + 4 * i + j] = xn;
-              ss += xn * xn;
-              gx[4 * i + j] = xn * sg[col];
-            }
-          }
-          store_f32x32(e.x + (size_t)m * e.N + n0 + 32 * c, v + 32 * c);
-          store_split32(e.xh, e.xl, (size_t)m * e.N + n0 + 32 * c, gx);
-        }
-        e.ssq_out[(size_t)m * e.ssq_out_nt + 2 * nt + half] = ss;
-      }
     }
+    if (lane == 0) bulk_wait_all();  // stores complete before the CTA exits
   }
 
   tc_fence_before();
@@ -503,6 +526,25 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
       !make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, rb, (uint64_t)wrows, rb, TQ<QT>::rawb, 128,
                     CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
+  if (epi.kind != EPI_PLAIN && epi.kind != EPI_SWIGLU) return cudaErrorInvalidValue;
+  // output maps for the epilogue's TMA stores (the unused kind's maps repeat
+  // a valid one; the kernel never touches them)
+  CUtensorMap ty, tzh, tzl;
+  if (epi.kind == EPI_PLAIN) {
+    if (!epi.y || epi.ldy < epi.N || epi.ldy % 4 ||
+        !make_tmap_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, epi.y, (uint64_t)epi.N, (uint64_t)M,
+                      (uint64_t)epi.ldy * 4, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return cudaErrorInvalidValue;
+    tzh = tzl = ty;
+  } else {
+    if (!epi.zh || !epi.zl ||
+        !make_tmap_2d(&tzh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, epi.zh, (uint64_t)epi.F, (uint64_t)M,
+                      (uint64_t)epi.F * 2, 16, 32, CU_TENSOR_MAP_SWIZZLE_32B) ||
+        !make_tmap_2d(&tzl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, epi.zl, (uint64_t)epi.F, (uint64_t)M,
+                      (uint64_t)epi.F * 2, 16, 32, CU_TENSOR_MAP_SWIZZLE_32B))
+      return cudaErrorInvalidValue;
+    ty = tzh;
+  }
   TcParams prm;
   prm.M = M;
   prm.N = epi.N;
@@ -518,7 +560,7 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
   if (e != cudaSuccess) return e;
   const int grid = prm.n_tiles < sm_count() ? prm.n_tiles : sm_count();  // persistent: one CTA per SM
-  kfn<<<grid, NTHREADS, C::SMEM, st>>>(txh, txl, tw, prm);
+  kfn<<<grid, NTHREADS, C::SMEM, st>>>(txh, txl, tw, ty, tzh, tzl, prm);
   return cudaGetLastError();
 }
 
@@ -527,16 +569,13 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
 // Host entry.  qt: 8 = Q8_0, 4 = Q4_0.  Requires K % 256 == 0, N % 256 == 0
 // (SWIGLU: F % 128 == 0), M >= 1, 16-byte aligned A rows.  `wrows` is the
 // number of rows of W (N, or 2F for SWIGLU); `wshift` the weight prescale
-// exponent from t0b_weight_shift.  RESID writes two partial sums of squares
-// per 256-column tile (one per 128-column half).
+// exponent from t0b_weight_shift.  Epilogue kinds: PLAIN (bias + optional
+// RMSNorm row scale) and SWIGLU; others are rejected (cudaErrorInvalidValue).
 cudaError_t t0b_launch_gemm_tc(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
                                int wshift, const Epi &epi, int *err, cudaStream_t st) {
   if (qt == 8) return launch_tc_t<8>(ah, al, M, K, W, wrows, wshift, epi, err, st);
   return launch_tc_t<4>(ah, al, M, K, W, wrows, wshift, epi, err, st);
 }
-
-// Columns per RESID partial sum of squares in the tensor-core path.
-int t0b_tc_tile_width() { return 128; }
 
 // Largest |scale| of a Q8_0 / Q4_0 matrix (device), as the f32 bit pattern of
 // a non-negative float (so an integer max is a float max).

@@ -149,42 +149,105 @@ __global__ void rownorm_split_kernel(const float *x, const float *g, __half *xh,
 }
 
 // ============================================================== attention
+T0B_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Sum over the 16 lanes of an aligned half-warp.
+T0B_DEV float half_warp_sum(float v) {
+#pragma unroll
+  for (int o = 8; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Four consecutive head dims d..d+3 (d % 4 == 0) of one q or k vector whose
+// sum of squares over the head is ss: RMSNorm with gains g (ops.rs:175-177),
+// then, if tab != NULL, xpos RoPE at position pos on the adjacent pairs
+// (d, d+1), (d+2, d+3): (x0, x1) -> (x0 c - x1 s, x1 c + x0 s) * scale
+// (ops.rs:132-142); tab = cos table, sc = the scale table to use.
+T0B_DEV float4 qk_norm_rope4(float4 v, float ss, const float *g, int d, const float *tab, const float *sc, int p,
+                             int pos) {
+  const float rdn = 1.0f / sqrtf(ss / 64.0f + 1e-8f);
+  float x[4] = {v.x * rdn * g[d], v.y * rdn * g[d + 1], v.z * rdn * g[d + 2], v.w * rdn * g[d + 3]};
+  if (tab) {
+    const float *c = tab + pos * 64 + d, *sn = tab + (size_t)p * 64 + pos * 64 + d, *s = sc + pos * 64 + d;
+#pragma unroll
+    for (int k = 0; k < 4; k += 2) {
+      const float x0 = x[k], x1 = x[k + 1];
+      x[k] = x0 * c[k] * s[k] + (-x1) * sn[k] * s[k];
+      x[k + 1] = x1 * c[k + 1] * s[k + 1] + x0 * sn[k + 1] * s[k + 1];
+    }
+  }
+  return make_float4(x[0], x[1], x[2], x[3]);
+}
+
 // Time attention for one (variate row, head): causal over the row's p
 // patches, keys restricted to non-padding patches (mask.rs:49-65).  A query
 // in a whole-padding patch has every key blocked; the reference's softmax
 // then averages V over all p patches (scores all equal -1e9), reproduced
-// here.  K/V staged in shared memory with a 65-float pitch.
+// here.  q, k and v of the row's head are staged once in shared memory
+// (16-byte loads), q and k normalised and rotated on the way in; K keeps a
+// 65-float pitch so the lane-per-key score loop is bank-conflict free.
 __global__ void __launch_bounds__(128) attn_time_kernel(AttnArgs a) {
   extern __shared__ float sm[];
   const int r = blockIdx.x, h = blockIdx.y;
   const int p = a.p, E = a.E;
   const int LD = 65;
-  float *Ks = sm;
-  float *Vs = sm + p * LD;
-  float *Ps = sm + 2 * p * LD;  // [4 warps][p] probabilities
+  // Qs and Vs first: their rows take 16-byte accesses, so their offsets
+  // stay multiples of 64 floats whatever p is; Ks (65-float pitch, scalar
+  // accesses only) and Ps follow
+  float *Qs = sm;                // [p][64]
+  float *Vs = Qs + p * 64;       // [p][64]
+  float *Ks = Vs + p * 64;       // [p][65]
+  float *Ps = Ks + p * LD;       // [4 warps][p] probabilities
   const size_t tok0 = (size_t)r * p;
-  for (int i = threadIdx.x; i < p * 64; i += blockDim.x) {
-    int j = i >> 6, d = i & 63;
-    const float *row = a.qkv + (tok0 + j) * 3 * E;
-    Ks[j * LD + d] = row[E + h * 64 + d];
-    Vs[j * LD + d] = row[2 * E + h * 64 + d];
+  const float *rope_c = a.use_rope ? a.rope : nullptr;
+  const float *rsc = a.rope + (size_t)2 * p * 64, *rsc_inv = a.rope + (size_t)3 * p * 64;
+  // 16 threads per token, 4 dims each; every thread runs every iteration so
+  // the half-warp reductions see all 16 lanes
+  for (int base = 0; base < p * 16; base += 128) {
+    const int i = base + threadIdx.x;
+    const bool ok = i < p * 16;
+    const int j = ok ? i >> 4 : 0, d = (i & 15) * 4;
+    const float *row = a.qkv + (tok0 + j) * 3 * E + h * 64 + d;
+    float4 qv = ok ? *reinterpret_cast<const float4 *>(row) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 kv = ok ? *reinterpret_cast<const float4 *>(row + E) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float sq = half_warp_sum(qv.x * qv.x + qv.y * qv.y + qv.z * qv.z + qv.w * qv.w);
+    const float sk = half_warp_sum(kv.x * kv.x + kv.y * kv.y + kv.z * kv.z + kv.w * kv.w);
+    if (ok) {
+      qv = qk_norm_rope4(qv, sq, a.qn, d, rope_c, rsc, p, j);
+      kv = qk_norm_rope4(kv, sk, a.kn, d, rope_c, rsc_inv, p, j);
+      *reinterpret_cast<float4 *>(Qs + j * 64 + d) = qv;
+      float *kd = Ks + j * LD + d;
+      kd[0] = kv.x;
+      kd[1] = kv.y;
+      kd[2] = kv.z;
+      kd[3] = kv.w;
+      *reinterpret_cast<float4 *>(Vs + j * 64 + d) = *reinterpret_cast<const float4 *>(row + 2 * E);
+    }
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int lo = a.row_first_valid[r];
   float *pw = Ps + warp * p;
   for (int i = warp; i < p; i += 4) {
-    const float *qrow = a.qkv + (tok0 + i) * 3 * E + h * 64;
-    float q[64];
-#pragma unroll
-    for (int d = 0; d < 64; ++d) q[d] = qrow[d];
+    const float *qi = Qs + i * 64;
     const bool masked = i < lo;
     const int j0 = masked ? 0 : lo, j1 = masked ? p - 1 : i;
     float mx = -INFINITY;
     for (int j = j0 + lane; j <= j1; j += 32) {
-      float s = 0.0f;
+      const float *kj = Ks + j * LD;
+      float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
 #pragma unroll
-      for (int d = 0; d < 64; ++d) s = fmaf(q[d], Ks[j * LD + d], s);
+      for (int d = 0; d < 64; d += 4) {
+        s0 = fmaf(qi[d], kj[d], s0);
+        s1 = fmaf(qi[d + 1], kj[d + 1], s1);
+        s2 = fmaf(qi[d + 2], kj[d + 2], s2);
+        s3 = fmaf(qi[d + 3], kj[d + 3], s3);
+      }
+      float s = (s0 + s1) + (s2 + s3);
       s = masked ? -1.0e9f : s * 0.125f;
       pw[j] = s;
       mx = fmaxf(mx, s);
@@ -197,15 +260,25 @@ __global__ void __launch_bounds__(128) attn_time_kernel(AttnArgs a) {
       pw[j] = e;
       sum += e;
     }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    sum = warp_sum(sum);
     __syncwarp();
-    float o0 = 0.0f, o1 = 0.0f;
-    for (int j = j0; j <= j1; ++j) {
-      float pj = pw[j] / sum;
-      o0 = fmaf(pj, Vs[j * LD + lane], o0);
-      o1 = fmaf(pj, Vs[j * LD + lane + 32], o1);
+    float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
+    int j = j0;
+    for (; j + 1 <= j1; j += 2) {
+      const float p0 = pw[j], p1 = pw[j + 1];
+      o0 = fmaf(p0, Vs[j * 64 + lane], o0);
+      o1 = fmaf(p0, Vs[j * 64 + lane + 32], o1);
+      o2 = fmaf(p1, Vs[(j + 1) * 64 + lane], o2);
+      o3 = fmaf(p1, Vs[(j + 1) * 64 + lane + 32], o3);
     }
+    if (j <= j1) {
+      const float p0 = pw[j];
+      o0 = fmaf(p0, Vs[j * 64 + lane], o0);
+      o1 = fmaf(p0, Vs[j * 64 + lane + 32], o1);
+    }
+    const float inv = 1.0f / sum;
+    o0 = (o0 + o2) * inv;
+    o1 = (o1 + o3) * inv;
     __syncwarp();
     const size_t oo = (tok0 + i) * E + h * 64;
     __half hh, ll;
@@ -225,17 +298,24 @@ __global__ void __launch_bounds__(128) attn_time_kernel(AttnArgs a) {
 // Group attention for one (series, patch): every head (one warp each) over
 // the series' variate rows at that patch (mask.rs:69-82).  Rows whose patch
 // is whole padding are blocked keys; such a query averages V over the
-// series' rows.
+// series' rows.  q and k get their per-head RMSNorm as they are read (no
+// RoPE on GROUP layers).
 __global__ void __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
   const int s = blockIdx.x, patch = blockIdx.y;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (h >= a.H) return;
   const int r0 = a.series_row0[s], nv = a.series_nrows[s];
   const int p = a.p, E = a.E;
+  const float qg0 = a.qn[lane], qg1 = a.qn[lane + 32], kg0 = a.kn[lane], kg1 = a.kn[lane + 32];
   for (int qa = 0; qa < nv; ++qa) {
     const size_t tq = (size_t)(r0 + qa) * p + patch;
     const float *qrow = a.qkv + tq * 3 * E + h * 64;
-    const float q0 = qrow[lane], q1 = qrow[lane + 32];
+    float q0 = qrow[lane], q1 = qrow[lane + 32];
+    {
+      const float rdn = 1.0f / sqrtf(warp_sum(q0 * q0 + q1 * q1) / 64.0f + 1e-8f);
+      q0 = q0 * rdn * qg0;
+      q1 = q1 * rdn * qg1;
+    }
     const bool qmasked = patch < a.row_first_valid[r0 + qa];
     // two passes over keys: max, then exp-sum and output (nv is small)
     float mx = -INFINITY;
@@ -243,9 +323,9 @@ __global__ void __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
       const bool kvalid = patch >= a.row_first_valid[r0 + kb];
       const size_t tk = (size_t)(r0 + kb) * p + patch;
       const float *krow = a.qkv + tk * 3 * E + E + h * 64;
-      float d = q0 * krow[lane] + q1 * krow[lane + 32];
-#pragma unroll
-      for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      const float k0 = krow[lane], k1 = krow[lane + 32];
+      const float rdn = 1.0f / sqrtf(warp_sum(k0 * k0 + k1 * k1) / 64.0f + 1e-8f);
+      const float d = warp_sum(q0 * (k0 * rdn * kg0) + q1 * (k1 * rdn * kg1));
       float sc = qmasked ? -1.0e9f : (kvalid ? d * 0.125f : -INFINITY);
       mx = fmaxf(mx, sc);
     }
@@ -254,9 +334,9 @@ __global__ void __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
       const bool kvalid = patch >= a.row_first_valid[r0 + kb];
       const size_t tk = (size_t)(r0 + kb) * p + patch;
       const float *krow = a.qkv + tk * 3 * E + E + h * 64;
-      float d = q0 * krow[lane] + q1 * krow[lane + 32];
-#pragma unroll
-      for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      const float k0 = krow[lane], k1 = krow[lane + 32];
+      const float rdn = 1.0f / sqrtf(warp_sum(k0 * k0 + k1 * k1) / 64.0f + 1e-8f);
+      const float d = warp_sum(q0 * (k0 * rdn * kg0) + q1 * (k1 * rdn * kg1));
       float sc = qmasked ? -1.0e9f : (kvalid ? d * 0.125f : -INFINITY);
       float e = expf(sc - mx);
       sum += e;
@@ -279,6 +359,40 @@ __global__ void __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
       a.o32[oo + lane + 32] = o1;
     }
   }
+}
+
+// ============================================================== residual
+// One warp per row: x += y (the bias-added output of the wO / mlp.2 GEMM),
+// then xh/xl = split(x * g) for the next RMSNorm-fused GEMM and ssq[row] =
+// sum x^2 (single slot).  E % 128 == 0; 16-byte accesses.
+__global__ void resid_split_kernel(float *x, const float *y, const float *g, __half *xh, __half *xl, float *ssq,
+                                   int M, int E) {
+  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  float4 *xr = reinterpret_cast<float4 *>(x + (size_t)row * E);
+  const float4 *yr = reinterpret_cast<const float4 *>(y + (size_t)row * E);
+  const float4 *g4 = reinterpret_cast<const float4 *>(g);
+  uint2 *hr = reinterpret_cast<uint2 *>(xh + (size_t)row * E);
+  uint2 *lr = reinterpret_cast<uint2 *>(xl + (size_t)row * E);
+  float s = 0.0f;
+  for (int c = lane; c < E / 4; c += 32) {
+    const float4 a = xr[c], b = yr[c], gg = g4[c];
+    const float4 v = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+    xr[c] = v;
+    s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    __half h0, l0, h1, l1, h2, l2, h3, l3;
+    split_f16(v.x * gg.x, h0, l0);
+    split_f16(v.y * gg.y, h1, l1);
+    split_f16(v.z * gg.z, h2, l2);
+    split_f16(v.w * gg.w, h3, l3);
+    __half2 ha = __halves2half2(h0, h1), hb = __halves2half2(h2, h3);
+    __half2 la = __halves2half2(l0, l1), lb = __halves2half2(l2, l3);
+    hr[c] = make_uint2(*reinterpret_cast<uint32_t *>(&ha), *reinterpret_cast<uint32_t *>(&hb));
+    lr[c] = make_uint2(*reinterpret_cast<uint32_t *>(&la), *reinterpret_cast<uint32_t *>(&lb));
+  }
+  s = warp_sum(s);
+  if (lane == 0) ssq[row] = s;
 }
 
 // ============================================================== decoder
@@ -334,8 +448,14 @@ cudaError_t t0b_launch_rownorm_split(const float *x, const float *g, __half *xh,
   rownorm_split_kernel<<<(M + 7) / 8, 256, 0, st>>>(x, g, xh, xl, ssq, M, E);
   return cudaGetLastError();
 }
+cudaError_t t0b_launch_resid_split(float *x, const float *y, const float *g, __half *xh, __half *xl, float *ssq,
+                                   int M, int E, cudaStream_t st) {
+  if (E % 128) return cudaErrorInvalidValue;
+  resid_split_kernel<<<(M + 7) / 8, 256, 0, st>>>(x, y, g, xh, xl, ssq, M, E);
+  return cudaGetLastError();
+}
 cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
-  size_t smem = (size_t)(2 * a.p * 65 + 4 * a.p) * sizeof(float);
+  size_t smem = (size_t)(a.p * (65 + 64 + 64) + 4 * a.p) * sizeof(float);
   cudaError_t e = cudaFuncSetAttribute(attn_time_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.R, a.H);

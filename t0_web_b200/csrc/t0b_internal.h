@@ -38,6 +38,11 @@ struct AttnArgs {
   float *o32;        // optional f32 output
   const int *row_first_valid;  // whole-padding patches at the start of each row
   const int *series_row0, *series_nrows;
+  // per-head QK RMSNorm gains [64] (eps 1e-8, ops.rs:175-177), applied to q
+  // and k as they are read; on TIME layers (use_rope) then xpos RoPE with the
+  // tables rope = [4][p][64]: cos, sin, scale, 1/scale (k uses 1/scale).
+  const float *qn, *kn, *rope;
+  int use_rope;
   int R, p, E, H, n_series;
 };
 
@@ -45,7 +50,6 @@ cudaError_t t0b_launch_gemm_small(int qt, const __half *ah, const __half *al, in
                                   const Epi &epi, int *err, cudaStream_t st);
 cudaError_t t0b_launch_gemm_tc(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
                                int wshift, const Epi &epi, int *err, cudaStream_t st);
-int t0b_tc_tile_width();
 cudaError_t t0b_launch_absmax_scale(const uint8_t *W, size_t nblocks, int bpb, unsigned int *out, cudaStream_t st);
 
 // Exponent s of the power-of-two weight prescale for the split-f16 tensor-core
@@ -60,6 +64,9 @@ inline int t0b_weight_shift(float max_d, int qt) {
 }
 cudaError_t t0b_launch_prep(const PrepArgs &a, cudaStream_t st);
 cudaError_t t0b_launch_sgemm(const SgemmArgs &a, cudaStream_t st);
+// x[m, :] += y[m, :]; xh/xl = split(x * g); ssq[m] = sum x^2 (one slot).
+cudaError_t t0b_launch_resid_split(float *x, const float *y, const float *g, __half *xh, __half *xl, float *ssq,
+                                   int M, int E, cudaStream_t st);
 cudaError_t t0b_launch_rownorm_split(const float *x, const float *g, __half *xh, __half *xl, float *ssq, int M, int E,
                                      cudaStream_t st);
 cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st);

@@ -482,7 +482,6 @@ cudaError_t qgemm(t0b_model *m, const __half *ah, const __half *al, int M, int K
   const double flops = 2.0 * M * (double)wrows * K;
   const double bytes = wbytes + 4.0 * M * K + 4.0 * M * outc * (epi.kind == EPI_RESID ? 2.0 : 1.0);
   if (use_tc(m, M)) {
-    if (epi.kind == EPI_RESID) epi.ssq_out_nt = epi.N / t0b_tc_tile_width();
     return launch(m, KC_GEMM_TC, flops, bytes, [&] {
       return t0b_launch_gemm_tc(m->qt, ah, al, M, K, W, wrows, wshift, epi, m->d_err, m->stream);
     });
@@ -490,6 +489,40 @@ cudaError_t qgemm(t0b_model *m, const __half *ah, const __half *al, int M, int K
   if (epi.kind == EPI_RESID) epi.ssq_out_nt = epi.N / 64;
   return launch(m, KC_GEMM_SMALL, flops, bytes,
                 [&] { return t0b_launch_gemm_small(m->qt, ah, al, M, K, W, epi, m->d_err, m->stream); });
+}
+
+// Residual branch output GEMM (wO or mlp.2): x += A . W^T + bias, then the
+// split of x * gnext and its sum of squares for the next RMSNorm-fused GEMM.
+// The tensor-core path writes the branch output to `ybuf` and a row kernel
+// does the rest; the small-M path fuses it into the GEMM epilogue.  Sets
+// *ssq_nt to the number of partial sums of squares per row it leaves.
+cudaError_t resid_gemm(t0b_model *m, const __half *ah, const __half *al, int M, int K, const uint8_t *W,
+                       int wshift, const float *bias, float *x, const float *gnext, float *ybuf, int *ssq_nt) {
+  const int E = m->E;
+  Epi r{};
+  r.M = M;
+  r.N = E;
+  r.bias = bias;
+  if (use_tc(m, M)) {
+    r.kind = EPI_PLAIN;
+    r.y = ybuf;
+    r.ldy = E;
+    cudaError_t e = qgemm(m, ah, al, M, K, W, E, wshift, r);
+    if (e != cudaSuccess) return e;
+    *ssq_nt = 1;
+    return launch(m, KC_OTHER, 0.0, (double)M * E * 16.0, [&] {
+      return t0b_launch_resid_split(x, ybuf, gnext, m->xh.as<__half>(), m->xl.as<__half>(), m->ssq.as<float>(), M,
+                                    E, m->stream);
+    });
+  }
+  r.kind = EPI_RESID;
+  r.x = x;
+  r.gnext = gnext;
+  r.xh = m->xh.as<__half>();
+  r.xl = m->xl.as<__half>();
+  r.ssq_out = m->ssq.as<float>();
+  *ssq_nt = E / 64;
+  return qgemm(m, ah, al, M, K, W, E, wshift, r);
 }
 
 t0b_status ensure_ws(t0b_model *m, size_t T, size_t R, size_t nout) {
@@ -621,12 +654,14 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   aa.H = m->H;
   aa.n_series = ns;
   const int M = (int)T;
-  const int resid_nt = use_tc(m, M) ? E / t0b_tc_tile_width() : E / 64;
+  aa.rope = rope;
 
   for (int l = 0; l < m->L; ++l) {
     const LayerW &w = m->layers[l];
+    // q | k | v = rmsnorm(x) . wQKV^T + b; QK-norm and RoPE happen in the
+    // attention kernels as q and k are read
     Epi e{};
-    e.kind = EPI_QKV;
+    e.kind = EPI_PLAIN;
     e.M = M;
     e.N = 3 * E;
     e.bias = w.bqkv;
@@ -634,16 +669,11 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
     e.ssq_in_nt = ssq_nt;
     e.ssq_dim = E;
     e.y = m->qkv.as<float>();
-    e.qn = w.qn;
-    e.kn = w.kn;
-    e.rcos = rope;
-    e.rsin = rope + (size_t)p * 64;
-    e.rsc = rope + (size_t)2 * p * 64;
-    e.rsc_inv = rope + (size_t)3 * p * 64;
-    e.p = p;
-    e.E = E;
-    e.rope = w.group ? 0 : 1;
+    e.ldy = 3 * E;
     LAUNCH(qgemm(m, m->xh.as<__half>(), m->xl.as<__half>(), M, E, w.wqkv, 3 * E, w.sh_qkv, e));
+    aa.qn = w.qn;
+    aa.kn = w.kn;
+    aa.use_rope = w.group ? 0 : 1;
     if (w.group) {
       LAUNCH(launch(m, KC_ATTN_GROUP, 0.0, T * (3.0 * E * 4 + E * 4.0), [&] { return t0b_launch_attn_group(aa, m->stream); }));
     } else {
@@ -651,19 +681,10 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
       const double fl = (double)R * m->H * (p * (p + 1) / 2.0) * 4.0 * 64.0;
       LAUNCH(launch(m, KC_ATTN_TIME, fl, T * (3.0 * E * 4 + E * 4.0), [&] { return t0b_launch_attn_time(aa, m->stream); }));
     }
-
-    Epi r{};
-    r.kind = EPI_RESID;
-    r.M = M;
-    r.N = E;
-    r.bias = w.bo;
-    r.x = x;
-    r.gnext = w.g_mlp;
-    r.xh = m->xh.as<__half>();
-    r.xl = m->xl.as<__half>();
-    r.ssq_out = m->ssq.as<float>();
-    LAUNCH(qgemm(m, m->ah.as<__half>(), m->al.as<__half>(), M, E, w.wo, E, w.sh_o, r));
-    ssq_nt = resid_nt;
+    // the q|k|v buffer is free again: it holds the residual branch outputs
+    float *ybuf = m->qkv.as<float>();
+    LAUNCH(resid_gemm(m, m->ah.as<__half>(), m->al.as<__half>(), M, E, w.wo, w.sh_o, w.bo, x, w.g_mlp, ybuf,
+                      &ssq_nt));
 
     Epi sg{};
     sg.kind = EPI_SWIGLU;
@@ -678,10 +699,9 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
     sg.zl = m->hl.as<__half>();
     LAUNCH(qgemm(m, m->xh.as<__half>(), m->xl.as<__half>(), M, E, w.w0, 2 * F, w.sh_0, sg));
 
-    Epi r2 = r;
-    r2.bias = w.b2;
-    r2.gnext = (l + 1 < m->L) ? m->layers[l + 1].g_attn : m->out_g;
-    LAUNCH(qgemm(m, m->hh.as<__half>(), m->hl.as<__half>(), M, F, w.w2, E, w.sh_2, r2));
+    const float *gnext = (l + 1 < m->L) ? m->layers[l + 1].g_attn : m->out_g;
+    LAUNCH(resid_gemm(m, m->hh.as<__half>(), m->hl.as<__half>(), M, F, w.w2, w.sh_2, w.b2, x, gnext, ybuf,
+                      &ssq_nt));
   }
 
   // decoder on the output patches only: rmsnorm(out_norm) -> residual block
