@@ -123,10 +123,13 @@ T0B_DEV void store_f32x16(float *dst, const float *v) {
 }
 
 // Dequantize one 32-value block of one weight row (raw window `src`, block
-// starting `off` bytes in) into 16 f16x2 hi words and 16 lo words:
-// hi = f16(2^s d q), lo = f16(2^s d q - hi).
-template <int QT>
-T0B_DEV void dequant_block(const uint8_t *src, int off, float wscale, uint32_t *hv, uint32_t *lv) {
+// starting OFF bytes in) into 16 f16x2 hi words and 16 lo words:
+// hi = f16(2^s d q), lo = f16(2^s d q - hi).  OFF is a compile-time
+// constant (the block start inside the 16-byte aligned window is 34 s mod 16
+// or 18 s mod 16, always even), so every word index and shift is static and
+// the window stays in registers.
+template <int QT, int OFF>
+T0B_DEV void dequant_block(const uint8_t *src, float wscale, uint32_t *hv, uint32_t *lv) {
   constexpr int RAWB = TQ<QT>::rawb;
   constexpr int NW = QT == 8 ? 8 : 4;  // 32-bit words of quants in a block
   uint32_t wv[RAWB / 4 + 1];
@@ -139,23 +142,12 @@ T0B_DEV void dequant_block(const uint8_t *src, int off, float wscale, uint32_t *
     wv[4 * i + 3] = q4.w;
   }
   wv[RAWB / 4] = 0u;
-  // `off` is even (34 s mod 16 or 18 s mod 16), so every 2-byte field sits in
-  // one word and the quants start at a word offset of 0 or 16 bits.  The
-  // word index is picked with selects so wv stays in registers.
-  auto pick = [&](int base, int k) -> uint32_t {  // wv[base + k], base in [0, 4]
-    uint32_t v = wv[k];
-    v = base == 1 ? wv[k + 1] : v;
-    v = base == 2 ? wv[k + 2] : v;
-    v = base == 3 ? wv[k + 3] : v;
-    v = base == 4 ? wv[k + 4] : v;
-    return v;
+  const uint32_t dbits = (wv[OFF >> 2] >> ((OFF & 3) * 8)) & 0xFFFFu;
+  constexpr int QB = OFF + 2, W0 = QB >> 2, SH = (QB & 3) * 8;
+  static_assert(W0 + NW < RAWB / 4 + 1, "block overruns the raw window");
+  auto word_q = [&](int i) -> uint32_t {  // quant bytes 4i..4i+3
+    return SH ? __funnelshift_r(wv[W0 + i], wv[W0 + i + 1], SH) : wv[W0 + i];
   };
-  const uint32_t dbits = (pick(off >> 2, 0) >> ((off & 3) * 8)) & 0xFFFFu;
-  const int qb = off + 2, w0 = qb >> 2, sh = (qb & 3) * 8;
-  uint32_t qa[NW + 1];
-#pragma unroll
-  for (int k = 0; k <= NW; ++k) qa[k] = pick(w0, k);
-  auto word_q = [&](int i) -> uint32_t { return __funnelshift_r(qa[i], qa[i + 1], sh); };  // quant bytes 4i..4i+3
   const __half dh = __float2half_rn(__half2float(__ushort_as_half((unsigned short)dbits)) * wscale);  // exact
   const __half2 d2 = __halves2half2(dh, dh);
   auto emit = [&](uint32_t qv, int pair) {
@@ -183,6 +175,34 @@ T0B_DEV void dequant_block(const uint8_t *src, int off, float wscale, uint32_t *
       emit(r[2], 8 + 2 * i);      // values 16+4i, 16+4i+1
       emit(r[3], 8 + 2 * i + 1);  // values 16+4i+2, 16+4i+3
     }
+  }
+}
+
+// Dequantize tile row r of one stage into the Wh / Wl tiles (canonical
+// K-major SW64 layout: 16-byte unit c of row r at sw64_offset(r, 8c)).
+template <int QT, int OFF>
+T0B_DEV void dequant_row(const uint8_t *src, float wscale, uint8_t *whs, uint8_t *wls, int r) {
+  uint32_t hv[16], lv[16];
+  dequant_block<QT, OFF>(src, wscale, hv, lv);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint32_t o = sw64_offset(r, 8 * c);
+    *reinterpret_cast<uint4 *>(whs + o) = make_uint4(hv[4 * c], hv[4 * c + 1], hv[4 * c + 2], hv[4 * c + 3]);
+    *reinterpret_cast<uint4 *>(wls + o) = make_uint4(lv[4 * c], lv[4 * c + 1], lv[4 * c + 2], lv[4 * c + 3]);
+  }
+}
+
+template <int QT>
+T0B_DEV void dequant_row_at(int off, const uint8_t *src, float wscale, uint8_t *whs, uint8_t *wls, int r) {
+  switch (off) {  // uniform across the CTA: the stage's block offset
+    case 0: dequant_row<QT, 0>(src, wscale, whs, wls, r); break;
+    case 2: dequant_row<QT, 2>(src, wscale, whs, wls, r); break;
+    case 4: dequant_row<QT, 4>(src, wscale, whs, wls, r); break;
+    case 6: dequant_row<QT, 6>(src, wscale, whs, wls, r); break;
+    case 8: dequant_row<QT, 8>(src, wscale, whs, wls, r); break;
+    case 10: dequant_row<QT, 10>(src, wscale, whs, wls, r); break;
+    case 12: dequant_row<QT, 12>(src, wscale, whs, wls, r); break;
+    default: dequant_row<QT, 14>(src, wscale, whs, wls, r); break;
   }
 }
 
@@ -340,16 +360,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         uint8_t *wls = smem + OFF_WL + ws * W_TILE;
         const int off = (s * BPB) & 15;  // block start inside the aligned window
         const uint8_t *slot = smem + OFF_RAW + rs * C::RAW_SLOT;
-        {
-          uint32_t hv[16], lv[16];
-          dequant_block<QT>(slot + r * RAWB, off, prm.wscale, hv, lv);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint32_t o = sw64_offset(r, 8 * c);
-            *reinterpret_cast<uint4 *>(whs + o) = make_uint4(hv[4 * c], hv[4 * c + 1], hv[4 * c + 2], hv[4 * c + 3]);
-            *reinterpret_cast<uint4 *>(wls + o) = make_uint4(lv[4 * c], lv[4 * c + 1], lv[4 * c + 2], lv[4 * c + 3]);
-          }
-        }
+        dequant_row_at<QT>(off, slot + r * RAWB, prm.wscale, whs, wls, r);
         mbar_arrive(&raw_empty[rs]);
         fence_proxy_async_smem();
         mbar_arrive(&w_full[ws]);
@@ -405,7 +416,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               for (int k = 0; k < 2; ++k) {
                 const float gg = gv[i + k] + sb[g0 + i + k];
                 const float uu = uv[i + k] + sb[128 + g0 + i + k];
-                z[k] = gg / (1.0f + expf(-gg)) * uu;
+                z[k] = gg * __frcp_rn(1.0f + __expf(-gg)) * uu;
                 gv[i + k] = z[k];
               }
               __half h0, l0, h1, l1;
