@@ -295,6 +295,177 @@ __global__ void __launch_bounds__(128) attn_time_kernel(AttnArgs a) {
   }
 }
 
+// Register-tiled time attention for one (variate row, head), for p <= 131
+// (same semantics as attn_time_kernel).  q, k, v of the row's head are staged
+// in shared memory (q and k normalised and rotated on the way in; q and k
+// rows with their 16-byte units swizzled by row/4 so the tile loads below
+// are bank-conflict free), then
+//   1. S = q k^T / 8 on the causal lower-triangular 4x4 tiles, 16 FMAs per
+//      pair of 16-byte loads;
+//   2. row softmax over the attendable keys [first valid patch, i] (a
+//      whole-padding query row gets 1/p everywhere), probabilities in place;
+//   3. O = P v on 4-query x 4-dim tiles, written as the f16 hi/lo split.
+constexpr int kAttnTiledMaxP = 131;
+
+__global__ void __launch_bounds__(128) attn_time_tiled_kernel(AttnArgs a) {
+  extern __shared__ float4 sm4[];
+  float *sm = reinterpret_cast<float *>(sm4);
+  const int r = blockIdx.x, h = blockIdx.y;
+  const int p = a.p, E = a.E;
+  const int PP = (p + 3) & ~3;  // rows padded to whole 4-row tiles
+  const int T = PP / 4;
+  float *Qs = sm;             // [PP][64] swizzled
+  float *Ks = Qs + PP * 64;   // [PP][64] swizzled
+  float *Vs = Ks + PP * 64;   // [PP][64]
+  float *Ss = Vs + PP * 64;   // [PP][PP] scores, then probabilities
+  const size_t tok0 = (size_t)r * p;
+  const float *rope_c = a.use_rope ? a.rope : nullptr;
+  const float *rsc = a.rope + (size_t)2 * p * 64, *rsc_inv = a.rope + (size_t)3 * p * 64;
+  // ---- stage q, k, v: every 16-byte copy issued at once (cp.async), rows
+  // p..PP-1 zero, then QK-norm + RoPE in place (16 threads per token)
+  for (int i = threadIdx.x; i < PP * 16; i += blockDim.x) {
+    const int j = i >> 4, c = i & 15;
+    const int qo = j * 64 + ((((c ^ (j >> 2)) & 7) | (c & 8)) << 2);
+    if (j < p) {
+      const float *row = a.qkv + (tok0 + j) * 3 * E + h * 64 + c * 4;
+      cp_async16(Qs + qo, row);
+      cp_async16(Ks + qo, row + E);
+      cp_async16(Vs + j * 64 + c * 4, row + 2 * E);
+    } else {
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4 *>(Qs + qo) = z;
+      *reinterpret_cast<float4 *>(Ks + qo) = z;
+      *reinterpret_cast<float4 *>(Vs + j * 64 + c * 4) = z;
+    }
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  for (int base = 0; base < p * 16; base += 128) {
+    const int i = base + threadIdx.x;
+    const bool ok = i < p * 16;  // all lanes run every iteration for the half-warp sums
+    const int j = ok ? i >> 4 : 0, c = i & 15, d = c * 4;
+    const int qo = j * 64 + ((((c ^ (j >> 2)) & 7) | (c & 8)) << 2);
+    float4 qv = *reinterpret_cast<const float4 *>(Qs + qo);
+    float4 kv = *reinterpret_cast<const float4 *>(Ks + qo);
+    const float sq = half_warp_sum(qv.x * qv.x + qv.y * qv.y + qv.z * qv.z + qv.w * qv.w);
+    const float sk = half_warp_sum(kv.x * kv.x + kv.y * kv.y + kv.z * kv.z + kv.w * kv.w);
+    if (ok) {
+      *reinterpret_cast<float4 *>(Qs + qo) = qk_norm_rope4(qv, sq, a.qn, d, rope_c, rsc, p, j);
+      *reinterpret_cast<float4 *>(Ks + qo) = qk_norm_rope4(kv, sk, a.kn, d, rope_c, rsc_inv, p, j);
+    }
+  }
+  __syncthreads();
+  const int lo = a.row_first_valid[r];
+  // ---- 1. scores on the lower-triangular 4x4 tiles (qt >= kt)
+  const int n1 = T * (T + 1) / 2;
+  for (int t = threadIdx.x; t < n1; t += blockDim.x) {
+    int qt = (int)((sqrtf(8.0f * t + 1.0f) - 1.0f) * 0.5f);
+    while (qt * (qt + 1) / 2 > t) --qt;
+    while ((qt + 1) * (qt + 2) / 2 <= t) ++qt;
+    const int kt = t - qt * (qt + 1) / 2;
+    float acc[4][4];
+#pragma unroll
+    for (int x = 0; x < 4; ++x)
+#pragma unroll
+      for (int y = 0; y < 4; ++y) acc[x][y] = 0.0f;
+    const float *qb = Qs + qt * 256, *kb = Ks + kt * 256;
+    const int qs = qt & 7, ks = kt & 7;
+#pragma unroll 4
+    for (int c = 0; c < 16; ++c) {
+      const int qc = ((c ^ qs) & 7) | (c & 8), kc = ((c ^ ks) & 7) | (c & 8);
+      float4 q4[4], k4[4];
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        q4[x] = *reinterpret_cast<const float4 *>(qb + x * 64 + qc * 4);
+        k4[x] = *reinterpret_cast<const float4 *>(kb + x * 64 + kc * 4);
+      }
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) {
+          acc[x][y] = fmaf(q4[x].x, k4[y].x, acc[x][y]);
+          acc[x][y] = fmaf(q4[x].y, k4[y].y, acc[x][y]);
+          acc[x][y] = fmaf(q4[x].z, k4[y].z, acc[x][y]);
+          acc[x][y] = fmaf(q4[x].w, k4[y].w, acc[x][y]);
+        }
+    }
+#pragma unroll
+    for (int x = 0; x < 4; ++x)
+      *reinterpret_cast<float4 *>(Ss + (qt * 4 + x) * PP + kt * 4) =
+          make_float4(acc[x][0] * 0.125f, acc[x][1] * 0.125f, acc[x][2] * 0.125f, acc[x][3] * 0.125f);
+  }
+  __syncthreads();
+  // ---- 2. softmax per query row, probabilities in place (zero elsewhere)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = warp; i < PP; i += 4) {
+    float *srow = Ss + i * PP;
+    if (i >= p) {
+      for (int j = lane; j < PP; j += 32) srow[j] = 0.0f;
+    } else if (i < lo) {  // whole-padding query: every key blocked -> uniform over all p
+      const float u = 1.0f / (float)p;
+      for (int j = lane; j < PP; j += 32) srow[j] = j < p ? u : 0.0f;
+    } else {
+      float mx = -INFINITY;
+      for (int j = lo + lane; j <= i; j += 32) mx = fmaxf(mx, srow[j]);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float sum = 0.0f;
+      for (int j = lo + lane; j <= i; j += 32) {
+        const float e = expf(srow[j] - mx);
+        srow[j] = e;
+        sum += e;
+      }
+      sum = warp_sum(sum);
+      __syncwarp();
+      for (int j = lane; j < PP; j += 32) srow[j] = (j >= lo && j <= i) ? srow[j] / sum : 0.0f;
+    }
+  }
+  __syncthreads();
+  // ---- 3. O = P v on 4-query x 4-dim tiles
+  const int n3 = T * 16;
+  for (int t = threadIdx.x; t < n3; t += blockDim.x) {
+    const int qt = t >> 4, dt = t & 15;
+    const int i0 = qt * 4;
+    const bool any_masked = i0 < lo;
+    const int j0 = any_masked ? 0 : lo;
+    const int j1 = any_masked ? p : min(i0 + 4, p);  // exclusive
+    float acc[4][4];
+#pragma unroll
+    for (int x = 0; x < 4; ++x)
+#pragma unroll
+      for (int y = 0; y < 4; ++y) acc[x][y] = 0.0f;
+    const float *pb = Ss + i0 * PP;
+    for (int j = j0; j < j1; ++j) {
+      const float4 v = *reinterpret_cast<const float4 *>(Vs + j * 64 + dt * 4);
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const float pj = pb[x * PP + j];
+        acc[x][0] = fmaf(pj, v.x, acc[x][0]);
+        acc[x][1] = fmaf(pj, v.y, acc[x][1]);
+        acc[x][2] = fmaf(pj, v.z, acc[x][2]);
+        acc[x][3] = fmaf(pj, v.w, acc[x][3]);
+      }
+    }
+#pragma unroll
+    for (int x = 0; x < 4; ++x) {
+      const int i = i0 + x;
+      if (i >= p) break;
+      const size_t oo = (tok0 + i) * E + h * 64 + dt * 4;
+      __half hh[4], ll[4];
+#pragma unroll
+      for (int y = 0; y < 4; ++y) split_f16(acc[x][y], hh[y], ll[y]);
+      __half2 h01 = __halves2half2(hh[0], hh[1]), h23 = __halves2half2(hh[2], hh[3]);
+      __half2 l01 = __halves2half2(ll[0], ll[1]), l23 = __halves2half2(ll[2], ll[3]);
+      *reinterpret_cast<uint2 *>(a.oh + oo) =
+          make_uint2(*reinterpret_cast<uint32_t *>(&h01), *reinterpret_cast<uint32_t *>(&h23));
+      *reinterpret_cast<uint2 *>(a.ol + oo) =
+          make_uint2(*reinterpret_cast<uint32_t *>(&l01), *reinterpret_cast<uint32_t *>(&l23));
+      if (a.o32) *reinterpret_cast<float4 *>(a.o32 + oo) = make_float4(acc[x][0], acc[x][1], acc[x][2], acc[x][3]);
+    }
+  }
+}
+
 // Group attention for one (series, patch): every head (one warp each) over
 // the series' variate rows at that patch (mask.rs:69-82).  Rows whose patch
 // is whole padding are blocked keys; such a query averages V over the
@@ -347,6 +518,87 @@ __global__ void __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
     o0 = o0 / sum;
     o1 = o1 / sum;
     const size_t oo = tq * E + h * 64;
+    __half hh, ll;
+    split_f16(o0, hh, ll);
+    a.oh[oo + lane] = hh;
+    a.ol[oo + lane] = ll;
+    split_f16(o1, hh, ll);
+    a.oh[oo + lane + 32] = hh;
+    a.ol[oo + lane + 32] = ll;
+    if (a.o32) {
+      a.o32[oo + lane] = o0;
+      a.o32[oo + lane + 32] = o1;
+    }
+  }
+}
+
+// Group attention with the series' keys and values held in registers: one
+// warp per head loads k and v of all NV (>= the series' row count) variate
+// rows at this patch with independent loads, normalises the keys once, then
+// answers every query row (same semantics as attn_group_kernel).
+template <int NV>
+__global__ void __launch_bounds__(256) attn_group_reg_kernel(AttnArgs a) {
+  const int s = blockIdx.x, patch = blockIdx.y;
+  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (h >= a.H) return;
+  const int r0 = a.series_row0[s], nv = a.series_nrows[s];
+  const int p = a.p, E = a.E;
+  float q0[NV], q1[NV], k0[NV], k1[NV], v0[NV], v1[NV];
+  uint32_t kvalid = 0;
+#pragma unroll
+  for (int b = 0; b < NV; ++b) {
+    q0[b] = q1[b] = k0[b] = k1[b] = v0[b] = v1[b] = 0.0f;
+    if (b < nv) {
+      const float *row = a.qkv + ((size_t)(r0 + b) * p + patch) * 3 * E + h * 64;
+      q0[b] = row[lane];
+      q1[b] = row[lane + 32];
+      k0[b] = row[E + lane];
+      k1[b] = row[E + lane + 32];
+      v0[b] = row[2 * E + lane];
+      v1[b] = row[2 * E + lane + 32];
+      if (patch >= a.row_first_valid[r0 + b]) kvalid |= 1u << b;
+    }
+  }
+  const float qg0 = a.qn[lane], qg1 = a.qn[lane + 32], kg0 = a.kn[lane], kg1 = a.kn[lane + 32];
+#pragma unroll
+  for (int b = 0; b < NV; ++b) {
+    if (b < nv) {
+      const float rk = 1.0f / sqrtf(warp_sum(k0[b] * k0[b] + k1[b] * k1[b]) / 64.0f + 1e-8f);
+      k0[b] = k0[b] * rk * kg0;
+      k1[b] = k1[b] * rk * kg1;
+      const float rq = 1.0f / sqrtf(warp_sum(q0[b] * q0[b] + q1[b] * q1[b]) / 64.0f + 1e-8f);
+      q0[b] = q0[b] * rq * qg0;
+      q1[b] = q1[b] * rq * qg1;
+    }
+  }
+#pragma unroll
+  for (int qa = 0; qa < NV; ++qa) {
+    if (qa >= nv) break;
+    const bool qmasked = !((kvalid >> qa) & 1u);  // a row's query and key share its first valid patch
+    float sc[NV];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int b = 0; b < NV; ++b) {
+      sc[b] = -INFINITY;
+      if (b < nv) {
+        const float d = warp_sum(q0[qa] * k0[b] + q1[qa] * k1[b]);
+        sc[b] = qmasked ? -1.0e9f : (((kvalid >> b) & 1u) ? d * 0.125f : -INFINITY);
+        mx = fmaxf(mx, sc[b]);
+      }
+    }
+    float sum = 0.0f, o0 = 0.0f, o1 = 0.0f;
+#pragma unroll
+    for (int b = 0; b < NV; ++b) {
+      if (b < nv) {
+        const float e = expf(sc[b] - mx);
+        sum += e;
+        o0 = fmaf(e, v0[b], o0);
+        o1 = fmaf(e, v1[b], o1);
+      }
+    }
+    o0 = o0 / sum;
+    o1 = o1 / sum;
+    const size_t oo = ((size_t)(r0 + qa) * p + patch) * E + h * 64;
     __half hh, ll;
     split_f16(o0, hh, ll);
     a.oh[oo + lane] = hh;
@@ -455,6 +707,15 @@ cudaError_t t0b_launch_resid_split(float *x, const float *y, const float *g, __h
   return cudaGetLastError();
 }
 cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
+  if (a.p <= kAttnTiledMaxP) {
+    const int PP = (a.p + 3) & ~3;
+    const size_t smem = (size_t)(PP * 64 * 3 + PP * PP) * sizeof(float);
+    cudaError_t e =
+        cudaFuncSetAttribute(attn_time_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attn_time_tiled_kernel<<<dim3(a.R, a.H), 128, smem, st>>>(a);
+    return cudaGetLastError();
+  }
   size_t smem = (size_t)(a.p * (65 + 64 + 64) + 4 * a.p) * sizeof(float);
   cudaError_t e = cudaFuncSetAttribute(attn_time_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -464,6 +725,14 @@ cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
 }
 cudaError_t t0b_launch_attn_group(const AttnArgs &a, cudaStream_t st) {
   dim3 grid(a.n_series, a.p);
+  if (a.max_nrows <= 8) {
+    attn_group_reg_kernel<8><<<grid, 32 * a.H, 0, st>>>(a);
+    return cudaGetLastError();
+  }
+  if (a.max_nrows <= 16) {
+    attn_group_reg_kernel<16><<<grid, 32 * a.H, 0, st>>>(a);
+    return cudaGetLastError();
+  }
   attn_group_kernel<<<grid, 32 * a.H, 0, st>>>(a);
   return cudaGetLastError();
 }

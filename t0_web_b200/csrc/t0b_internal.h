@@ -44,6 +44,7 @@ struct AttnArgs {
   const float *qn, *kn, *rope;
   int use_rope;
   int R, p, E, H, n_series;
+  int max_nrows;  // largest series_nrows entry (host-side bound for the group kernel)
 };
 
 cudaError_t t0b_launch_gemm_small(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W,

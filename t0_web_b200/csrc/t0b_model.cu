@@ -653,6 +653,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   aa.E = E;
   aa.H = m->H;
   aa.n_series = ns;
+  aa.max_nrows = ps.s_nrows.empty() ? 0 : *std::max_element(ps.s_nrows.begin(), ps.s_nrows.end());
   const int M = (int)T;
   aa.rope = rope;
 
