@@ -1,17 +1,20 @@
 #!/usr/bin/env python
 """Throughput benchmark: series-forecasts/sec of the t0-alpha-shape quantized
-forecast path on B200, sharded over N GPUs.
+forecast path on B200, N GPUs.
 
 Workload (the box-wide sweep configuration, one context length per run):
-8192 independent multivariate series, v ~ U{1..8} variates (seed 0), each
-variate a sum of 2-3 sinusoids + trend + N(0,0.2) noise with a 5% NaN gap,
-context 2048 (p = 67 patches), horizon 96, random-init t0-alpha weights
-exported to Q8_0 GGUF.  Total work is fixed (strong scaling): each rank takes
-a contiguous, token-balanced shard of the series; the quantile outputs are
-all-gathered over NCCL.  A step = one forecast of all 8192 series.
+8192 independent multivariate series per GPU, v ~ U{1..8} variates (seed 0
++ rank), each variate a sum of 2-3 sinusoids + trend + N(0,0.2) noise with a
+5% NaN gap, context 2048 (p = 67 patches), horizon 96, random-init t0-alpha
+weights exported to Q8_0 GGUF.  Series are independent, so every rank
+forecasts its own series with no collective on the data path (weak scaling:
+per-GPU work is fixed as N grows); the process group only carries the
+barriers and the max-over-ranks timing.  A step = one forecast of every
+rank's 8192 series.  `--strong` instead splits one fixed set of series across
+the ranks (token-balanced shards, NCCL all-gather of the quantiles).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--quant q8_0|q4_0]
-                    [--ctx 2048] [--impl ours|reference]
+                    [--ctx 2048] [--impl ours|reference] [--strong]
 
 Under torchrun each rank drives one GPU; rank 0 prints one JSON line.
 """
@@ -46,24 +49,30 @@ def parse():
     ap.add_argument("--cpu-sample", type=int, default=0, help="series per CPU-baseline step (0 = one per thread)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--strong", action="store_true", help="split one fixed set of series across the ranks")
     return ap.parse_args()
 
 
-def workload(args):
+def workload(args, seed):
     from t0_web_b200 import synthetic as S
-    ctx, nv = S.multiseries(args.series, args.ctx, seed=args.seed, n_variates=(1, 8))
+    ctx, nv = S.multiseries(args.series, args.ctx, seed=seed, n_variates=(1, 8))
     return ctx, nv
 
 
 def config_block(args, nv, world):
     p = (args.ctx + (32 - args.ctx % 32) % 32 + (args.horizon + 31) // 32 * 32) // 32
     rows = int(nv.sum())
+    per = "in total" if args.strong else "per GPU"
+    par = ("series-sharded, weights replicated, NCCL all-gather of quantiles" if args.strong else
+           "independent series per GPU, weights replicated, no data-path collective")
     return {
-        "workload": (f"{args.series} multivariate series (v~U{{1..8}}, seed {args.seed}), ctx {args.ctx}, "
-                     f"horizon {args.horizon}, t0-alpha shape random-init weights as {args.quant.upper()} GGUF"),
-        "series": args.series, "rows": rows, "patches_per_row": p, "tokens": rows * p,
+        "workload": (f"{args.series} multivariate series {per} (v~U{{1..8}}, seed {args.seed}"
+                     f"{'' if args.strong else ' + rank'}), ctx {args.ctx}, horizon {args.horizon}, "
+                     f"t0-alpha shape random-init weights as {args.quant.upper()} GGUF"),
+        "series": args.series, "series_total": args.series * (1 if args.strong else world),
+        "rows": rows, "patches_per_row": p, "tokens": rows * p,
         "ctx": args.ctx, "horizon": args.horizon, "quant": args.quant,
-        "parallelism": f"dp{world} (series-sharded, weights replicated, NCCL all-gather of quantiles)",
+        "parallelism": f"dp{world} ({par})",
         "l2": "inputs larger than L2 (>=38 MB contexts + GBs of activations per step) and a 256 MB "
               "buffer write between timed steps",
     }
@@ -178,7 +187,8 @@ def run_ours(args):
     weights = S.random_weights(S.ALPHA, seed=0)
     gbytes = gguf.export_gguf(weights, S.ALPHA, args.quant)
     del weights
-    ctx, nv = workload(args)
+    # weak scaling: every rank its own series; strong: one set split across ranks
+    ctx, nv = workload(args, args.seed if args.strong else args.seed + rank)
     engine = t0_fast.Engine(local)
     model = t0_fast.load_model_from_gguf(engine, gbytes)
     # one explicit stream for the library, the timing events and the collective
@@ -186,8 +196,12 @@ def run_ours(args):
     torch.cuda.set_stream(stream)
     model.set_stream(stream.cuda_stream)
 
-    row_ranges = sharded.shard_rows(nv, world)
-    ser_ranges = sharded.balanced_split(nv, world)
+    if args.strong:
+        row_ranges = sharded.shard_rows(nv, world)
+        ser_ranges = sharded.balanced_split(nv, world)
+    else:
+        row_ranges = [(0, int(nv.sum()))] * world
+        ser_ranges = [(0, len(nv))] * world
     r0, r1 = row_ranges[rank]
     s0, s1 = ser_ranges[rank]
     rows_per_rank = [b - a for a, b in row_ranges]
@@ -197,11 +211,12 @@ def run_ours(args):
     ctx_dev = torch.from_numpy(ctx_shard).cuda()
     out_dev = torch.empty((r1 - r0, args.horizon, nq), device="cuda")
     flush = torch.empty(L2_FLUSH_BYTES // 4, device="cuda")
+    gather = args.strong and world > 1
 
     def step():
         if s1 > s0:
             t0_fast.forecast_multiseries_device(model, ctx_dev, nv_shard, args.ctx, args.horizon, out_dev)
-        if world > 1:
+        if gather:
             return sharded.gather_outputs(out_dev, rows_per_rank)
         return out_dev
 
@@ -233,6 +248,7 @@ def run_ours(args):
     launches = model.launch_count() - launches0
     model.profile(False)
     clocks = sampler.stop() if sampler else None
+    series_total = args.series * (1 if args.strong else world)
     t = torch.tensor([total_ms, float(launches)], dtype=torch.float64, device="cuda")
     if world > 1:
         tm = t[:1].clone()
@@ -241,8 +257,8 @@ def run_ours(args):
         dist.all_reduce(tl, op=dist.ReduceOp.SUM)
         total_ms, launches = float(tm.item()), int(tl.item())
     ms_per_step = total_ms / args.steps
-    value = args.series / (ms_per_step / 1e3)
-    assert full.shape[0] == int(nv.sum())
+    value = series_total / (ms_per_step / 1e3)
+    assert full.shape[0] == (int(nv.sum()) if (gather or world == 1 or not args.strong) else r1 - r0)
 
     # ---- end to end through the public host API (H2D and D2H inside) ----
     e2e = None
@@ -250,7 +266,7 @@ def run_ours(args):
         def e2e_step():
             out = t0_fast.forecast_multiseries(engine, model, ctx_shard, nv_shard, args.ctx, args.horizon) \
                 if s1 > s0 else np.zeros((0, args.horizon, nq), np.float32)
-            if world > 1:
+            if gather:
                 g = sharded.gather_outputs(torch.from_numpy(out).cuda(), rows_per_rank)
                 return g.cpu().numpy()
             return out
@@ -262,13 +278,18 @@ def run_ours(args):
             t0 = time.perf_counter()
             e2e_step()
             times.append(time.perf_counter() - t0)
-        et = torch.tensor([sum(times)], dtype=torch.float64, device="cuda")
+        et = torch.tensor([sum(times), float(ctx_shard.nbytes), float(ctx_shard.shape[0] * args.horizon * nq * 4)],
+                          dtype=torch.float64, device="cuda")
         if world > 1:
-            dist.all_reduce(et, op=dist.ReduceOp.MAX)
-        e_ms = float(et.item()) * 1e3 / args.steps
-        h2d = int(ctx.nbytes)  # whole job: every rank copies its shard's contexts
-        d2h = int(ctx.shape[0] * args.horizon * nq * 4) * (world if world > 1 else 1)
-        e2e = {"value": args.series / (e_ms / 1e3), "unit": "series/s", "ms_per_step": e_ms,
+            e_max = et[:1].clone()
+            dist.all_reduce(e_max, op=dist.ReduceOp.MAX)
+            e_sum = et[1:].clone()
+            dist.all_reduce(e_sum, op=dist.ReduceOp.SUM)
+            et = torch.cat([e_max, e_sum])
+        e_ms = float(et[0].item()) * 1e3 / args.steps
+        h2d = int(et[1].item())  # every rank copies its own contexts in
+        d2h = int(et[2].item()) * (world if gather else 1)  # and its (or, gathered, all) quantiles out
+        e2e = {"value": series_total / (e_ms / 1e3), "unit": "series/s", "ms_per_step": e_ms,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
     # ---- roofline of the dominant kernel (tcgen05 dequant GEMM) ----
@@ -279,6 +300,11 @@ def run_ours(args):
         per_launch_ms = g["total_ms"] / g["launches"]
         achieved = g["flops"] / (g["total_ms"] / 1e3) / 1e12
         tr = committed_traffic(args.quant)
+        if tr:  # per-token DRAM bytes of one launch (ncu) x this run's tokens per launch
+            n_gemm = 4 * model.info.num_layers
+            tok_per_launch = (int(nv_shard.sum()) * config_block(args, nv, world)["patches_per_row"] * n_gemm
+                              * args.steps / g["launches"])
+            tr = tr["dram_bytes_per_token_per_launch"] * tok_per_launch
         roofline = {"kernel": "gemm_q_tc_kernel", "bound": "tensor", "achieved": achieved, "peak": peak_tf,
                     "unit": "TFLOP/s", "frac": achieved / peak_tf,
                     "peak_kind": f"{peak_kind} bf16 sustained (dense cuBLAS)",
@@ -299,8 +325,8 @@ def run_ours(args):
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "series/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": config_block(args, nv, world), "e2e": e2e, "roofline": roofline,
+                "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": config_block(args, nv, world), "e2e": e2e, "roofline": roofline,
                 "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": launches, "kernels": breakdown,
                 "arith": "GEMMs: split-f16 (3 MMAs, exact weight split) on tcgen05 with f32 TMEM accumulation; "
                          "attention, norms, scaler in f32"}
@@ -320,14 +346,14 @@ def run_reference(args):
     weights = S.random_weights(S.ALPHA, seed=0)
     gbytes = gguf.export_gguf(weights, S.ALPHA, args.quant)
     del weights
-    ctx, nv = workload(args)
+    ctx, nv = workload(args, args.seed)
     th = cpu_threads()
     n = args.cpu_sample or th
     rate, times = oracle_sample_rate(gbytes, ctx, nv, args, n, th, steps=args.steps, warmup=args.warmup)
     ms = 1e3 * sum(times) / len(times)
     line = {"metric": METRIC, "value": rate, "unit": "series/s", "n_gpus": int(os.environ.get("WORLD_SIZE", 1)),
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
             "config": config_block(args, nv, 1),
             "cpu_baseline": {"value": rate, "unit": "series/s", "cores": th, "kind": "port",
                              "sample": f"first {n} series of the workload per step, one series per thread; the "

@@ -7,8 +7,8 @@
  * Each entry point names the reference (idle-intelligence/t0-web) interface
  * it replaces.  The reference boundary is the Rust crate API of `t0-fast`
  * (crates/t0-fast/src/lib.rs) plus the GGUF codec of `t0-core`
- * (crates/t0-core/src/gguf.rs); a Rust engine crate would bind these symbols
- * through `extern "C"`.
+ * (crates/t0-core/src/gguf.rs); a Rust engine crate binds these symbols
+ * through an `extern "C"` block.
  *
  * Threading: an engine may be shared by several models; a model is not
  * thread-safe (mirrors `GpuModel`/`Pool` being !Sync, pool.rs:9-16).  All
