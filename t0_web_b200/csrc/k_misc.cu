@@ -466,6 +466,324 @@ __global__ void __launch_bounds__(128) attn_time_tiled_kernel(AttnArgs a) {
   }
 }
 
+// ---------------------------------------------------------- tensor-core time attention
+// Time attention for one (variate row, head) on mma.sync tensor cores, for
+// p <= 128 (same semantics as attn_time_kernel).  f32-class products from f16
+// MMAs: every operand is split into hi + lo f16 terms and a product is
+// hi.hi + hi.lo + lo.hi with f32 accumulation.
+//   - staging: one thread per key token and tensor loads its k or v row,
+//     applies QK-norm and RoPE to k, and stores k (row-major) and v
+//     (transposed) as f16 hi/lo in shared memory;
+//   - one warp per block of 16 queries keeps its q rows in registers (normed,
+//     rotated, split into mma fragments), walks the key blocks up to the
+//     diagonal with an online softmax on the score fragments, and accumulates
+//     P.V with P re-split from the score registers (FlashAttention-2 style).
+constexpr int kAttnMmaMaxP = 128;
+
+// RoPE of the adjacent pair (x0, x1) = dims (2i, 2i+1) from a compact table
+// row (cos[32], sin[32] per pair, scale[32], 1/scale[32] per dim mod 32):
+// (x0, x1) -> (x0 c - x1 s, x1 c + x0 s) * scale, k uses 1/scale.
+T0B_DEV void rope_pair(float &x0, float &x1, const float *tab, int i, bool kside) {
+  const float c = tab[i], sn = tab[32 + i];
+  const float *sc = tab + (kside ? 96 : 64);
+  const float s0 = sc[(2 * i) & 31], s1 = sc[(2 * i + 1) & 31];
+  const float a0 = x0, a1 = x1;
+  x0 = a0 * c * s0 + (-a1) * sn * s0;
+  x1 = a1 * c * s1 + a0 * sn * s1;
+}
+
+T0B_DEV uint32_t pack_h2(__half lo_elem, __half hi_elem) {
+  __half2 v = __halves2half2(lo_elem, hi_elem);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// (x0, x1) -> f16x2 hi word and f16x2 lo word (the same values as split_f16
+// element by element, with packed conversions)
+T0B_DEV void split2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const float2 hf = __half22float2(h);
+  const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+  hi = *reinterpret_cast<const uint32_t *>(&h);
+  lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+// Four 8x8 b16 matrices from shared memory (rows addressed by lanes 8m..8m+7
+// for matrix m), plain or transposed: the mma.sync B-fragment loaders.
+T0B_DEV void ldsm_x4(const void *row_addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(row_addr)));
+}
+T0B_DEV void ldsm_x4_trans(const void *row_addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(row_addr)));
+}
+
+// RoPE on 16 consecutive dims 16cg..16cg+15 (8 pairs) with 16-byte table
+// loads; same arithmetic as rope_pair.
+T0B_DEV void rope16(float *x, const float *tab, int cg, bool kside) {
+  const float4 *t4 = reinterpret_cast<const float4 *>(tab);
+  const float4 c0 = t4[2 * cg], c1 = t4[2 * cg + 1], n0 = t4[8 + 2 * cg], n1 = t4[8 + 2 * cg + 1];
+  const float4 *sp = t4 + (kside ? 24 : 16) + ((16 * cg) & 31) / 4;
+  const float4 s0 = sp[0], s1 = sp[1], s2 = sp[2], s3 = sp[3];
+  const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  const float sn[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+  const float sv[16] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w,
+                        s2.x, s2.y, s2.z, s2.w, s3.x, s3.y, s3.z, s3.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float a0 = x[2 * i], a1 = x[2 * i + 1];
+    x[2 * i] = a0 * cs[i] * sv[2 * i] + (-a1) * sn[i] * sv[2 * i];
+    x[2 * i + 1] = a1 * cs[i] * sv[2 * i + 1] + a0 * sn[i] * sv[2 * i + 1];
+  }
+}
+
+__global__ void __launch_bounds__(256, 2) attn_time_mma_kernel(AttnArgs a) {
+  extern __shared__ uint4 smem_u4[];
+  const int r = blockIdx.x, h = blockIdx.y;
+  const int p = a.p, E = a.E;
+  const int QB = (p + 15) >> 4;  // blocks of 16 queries (= keys)
+  const int PK = QB * 16;
+  // k and v row-major [PK][72] f16 (72-half pitch: conflict-free ldmatrix rows)
+  __half *Kh = reinterpret_cast<__half *>(smem_u4);
+  __half *Kl = Kh + PK * 72;
+  __half *Vh = Kl + PK * 72;
+  __half *Vl = Vh + PK * 72;
+  const size_t tok0 = (size_t)r * p;
+  const bool rope = a.use_rope != 0;
+  const int lo = a.row_first_valid[r];
+
+  // ---- staging (blockDim = 32 QB = 2 PK): threads [0, PK) take the v row of
+  // token j, threads [PK, 2 PK) the k row; every load of a row is issued
+  // before any conversion
+  {
+    const bool is_k = threadIdx.x >= PK;
+    const int j = is_k ? threadIdx.x - PK : threadIdx.x;
+    const float *src = a.qkv + (tok0 + (j < p ? j : 0)) * 3 * E + h * 64 + (is_k ? E : 2 * E);
+    float xv[64];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const float4 x4 = j < p ? *reinterpret_cast<const float4 *>(src + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      xv[4 * c] = x4.x, xv[4 * c + 1] = x4.y, xv[4 * c + 2] = x4.z, xv[4 * c + 3] = x4.w;
+    }
+    if (is_k && j < p) {  // QK-norm over the whole row, then RoPE
+      float ss = 0.0f;
+#pragma unroll
+      for (int d = 0; d < 64; ++d) ss += xv[d] * xv[d];
+      const float rdn = 1.0f / sqrtf(ss / 64.0f + 1e-8f);
+      const float4 *g4 = reinterpret_cast<const float4 *>(a.kn);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const float4 gg = g4[c];
+        xv[4 * c] = xv[4 * c] * rdn * gg.x;
+        xv[4 * c + 1] = xv[4 * c + 1] * rdn * gg.y;
+        xv[4 * c + 2] = xv[4 * c + 2] * rdn * gg.z;
+        xv[4 * c + 3] = xv[4 * c + 3] * rdn * gg.w;
+      }
+      if (rope) {
+        const float *tab = a.rope_c + (size_t)j * 128;
+#pragma unroll
+        for (int cg = 0; cg < 4; ++cg) rope16(xv + 16 * cg, tab, cg, true);
+      }
+    }
+    __half *dh = (is_k ? Kh : Vh) + j * 72, *dl = (is_k ? Kl : Vl) + j * 72;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {  // 8 dims per 16-byte unit
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) split2(xv[8 * u + 2 * e], xv[8 * u + 2 * e + 1], hw[e], lw[e]);
+      *reinterpret_cast<uint4 *>(dh + 8 * u) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4 *>(dl + 8 * u) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+  }
+
+  // ---- this warp's query rows
+  const int qb = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int ia = qb * 16 + g, ib = ia + 8;  // this thread's two query rows
+  float qa[16], qbv[16];                    // dims 16kc + {2t, 2t+1, 2t+8, 2t+9}
+  {
+    const float *ra = a.qkv + (tok0 + min(ia, p - 1)) * 3 * E + h * 64;
+    const float *rb = a.qkv + (tok0 + min(ib, p - 1)) * 3 * E + h * 64;
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {
+      const float2 u0 = *reinterpret_cast<const float2 *>(ra + 16 * kc + 2 * t);
+      const float2 u1 = *reinterpret_cast<const float2 *>(ra + 16 * kc + 2 * t + 8);
+      const float2 w0 = *reinterpret_cast<const float2 *>(rb + 16 * kc + 2 * t);
+      const float2 w1 = *reinterpret_cast<const float2 *>(rb + 16 * kc + 2 * t + 8);
+      qa[4 * kc] = u0.x, qa[4 * kc + 1] = u0.y, qa[4 * kc + 2] = u1.x, qa[4 * kc + 3] = u1.y;
+      qbv[4 * kc] = w0.x, qbv[4 * kc + 1] = w0.y, qbv[4 * kc + 2] = w1.x, qbv[4 * kc + 3] = w1.y;
+    }
+  }
+
+  // ---- q: QK-norm, RoPE, split into mma fragments (rows >= p are zero)
+  uint32_t qh[4][4], ql[4][4];
+  {
+    if (ia >= p)
+#pragma unroll
+      for (int x = 0; x < 16; ++x) qa[x] = 0.0f;
+    if (ib >= p)
+#pragma unroll
+      for (int x = 0; x < 16; ++x) qbv[x] = 0.0f;
+    float sa = 0.0f, sb = 0.0f;
+#pragma unroll
+    for (int x = 0; x < 16; ++x) {
+      sa += qa[x] * qa[x];
+      sb += qbv[x] * qbv[x];
+    }
+    sa += __shfl_xor_sync(0xffffffffu, sa, 1);
+    sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+    sb += __shfl_xor_sync(0xffffffffu, sb, 1);
+    sb += __shfl_xor_sync(0xffffffffu, sb, 2);
+    const float ra_n = 1.0f / sqrtf(sa / 64.0f + 1e-8f), rb_n = 1.0f / sqrtf(sb / 64.0f + 1e-8f);
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {
+      const float2 g0 = *reinterpret_cast<const float2 *>(a.qn + 16 * kc + 2 * t);
+      const float2 g1 = *reinterpret_cast<const float2 *>(a.qn + 16 * kc + 2 * t + 8);
+      const float gg[4] = {g0.x, g0.y, g1.x, g1.y};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        qa[4 * kc + e] = qa[4 * kc + e] * ra_n * gg[e];
+        qbv[4 * kc + e] = qbv[4 * kc + e] * rb_n * gg[e];
+      }
+    }
+    if (rope) {
+      const float *ta = a.rope_c + (size_t)min(ia, p - 1) * 128, *tb = a.rope_c + (size_t)min(ib, p - 1) * 128;
+#pragma unroll
+      for (int kc = 0; kc < 4; ++kc)
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          const int pi = 8 * kc + t + (e >> 1) * 4;  // pair index of dims (2pi, 2pi+1)
+          rope_pair(qa[4 * kc + e], qa[4 * kc + e + 1], ta, pi, false);
+          rope_pair(qbv[4 * kc + e], qbv[4 * kc + e + 1], tb, pi, false);
+        }
+    }
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {
+      split2(qa[4 * kc], qa[4 * kc + 1], qh[kc][0], ql[kc][0]);
+      split2(qbv[4 * kc], qbv[4 * kc + 1], qh[kc][1], ql[kc][1]);
+      split2(qa[4 * kc + 2], qa[4 * kc + 3], qh[kc][2], ql[kc][2]);
+      split2(qbv[4 * kc + 2], qbv[4 * kc + 3], qh[kc][3], ql[kc][3]);
+    }
+  }
+  __syncthreads();  // k and v staged
+
+  const bool any_masked = qb * 16 < lo;  // a whole-padding query in this block
+  const int kb0 = any_masked ? 0 : (lo >> 4), kb1 = any_masked ? QB - 1 : qb;
+  float o[8][4];
+#pragma unroll
+  for (int nd = 0; nd < 8; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.0f;
+  float ma = -INFINITY, mb = -INFINITY, la = 0.0f, lb = 0.0f;
+  for (int kb = kb0; kb <= kb1; ++kb) {
+    float sc[2][4];
+#pragma unroll
+    for (int nh = 0; nh < 2; ++nh) sc[nh][0] = sc[nh][1] = sc[nh][2] = sc[nh][3] = 0.0f;
+    // ldmatrix rows: matrix m = lane / 8 -> keys (m / 2) * 8 + (lane % 8), dims (m % 2) * 8
+    const int koff = (kb * 16 + ((lane >> 4) << 3) + (lane & 7)) * 72 + ((lane >> 3) & 1) * 8;
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {
+      uint32_t h00, h01, h10, h11, l00, l01, l10, l11;  // [key half][dim half]
+      ldsm_x4(Kh + koff + 16 * kc, h00, h01, h10, h11);
+      ldsm_x4(Kl + koff + 16 * kc, l00, l01, l10, l11);
+      mma16816(sc[0][0], sc[0][1], sc[0][2], sc[0][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], h00, h01);
+      mma16816(sc[1][0], sc[1][1], sc[1][2], sc[1][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], h10, h11);
+      mma16816(sc[0][0], sc[0][1], sc[0][2], sc[0][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], l00, l01);
+      mma16816(sc[1][0], sc[1][1], sc[1][2], sc[1][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], l10, l11);
+      mma16816(sc[0][0], sc[0][1], sc[0][2], sc[0][3], ql[kc][0], ql[kc][1], ql[kc][2], ql[kc][3], h00, h01);
+      mma16816(sc[1][0], sc[1][1], sc[1][2], sc[1][3], ql[kc][0], ql[kc][1], ql[kc][2], ql[kc][3], h10, h11);
+    }
+    // scale + masks; e = 0,1: row ia, e = 2,3: row ib
+    float bma = -INFINITY, bmb = -INFINITY;
+#pragma unroll
+    for (int nh = 0; nh < 2; ++nh)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = e < 2 ? ia : ib;
+        const int key = kb * 16 + nh * 8 + 2 * t + (e & 1);
+        float s = sc[nh][e] * 0.125f;
+        if (row >= p || row < lo)  // padding row / whole-padding query: uniform over the p keys
+          s = key < p ? -1.0e9f : -INFINITY;
+        else if (key < lo || key > row)
+          s = -INFINITY;
+        sc[nh][e] = s;
+        if (e < 2) bma = fmaxf(bma, s); else bmb = fmaxf(bmb, s);
+      }
+    bma = fmaxf(bma, __shfl_xor_sync(0xffffffffu, bma, 1));
+    bma = fmaxf(bma, __shfl_xor_sync(0xffffffffu, bma, 2));
+    bmb = fmaxf(bmb, __shfl_xor_sync(0xffffffffu, bmb, 1));
+    bmb = fmaxf(bmb, __shfl_xor_sync(0xffffffffu, bmb, 2));
+    const float na = fmaxf(ma, bma), nb = fmaxf(mb, bmb);
+    const float ua = na == -INFINITY ? 0.0f : na, ub = nb == -INFINITY ? 0.0f : nb;
+    const float ca = expf(ma - ua), cb = expf(mb - ub);  // rescale of what came before (0 at the start)
+    ma = na;
+    mb = nb;
+    la *= ca;
+    lb *= cb;
+#pragma unroll
+    for (int nd = 0; nd < 8; ++nd) {
+      o[nd][0] *= ca, o[nd][1] *= ca;
+      o[nd][2] *= cb, o[nd][3] *= cb;
+    }
+#pragma unroll
+    for (int nh = 0; nh < 2; ++nh)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float pe = expf(sc[nh][e] - (e < 2 ? ua : ub));
+        sc[nh][e] = pe;
+        if (e < 2) la += pe; else lb += pe;
+      }
+    // P as the A operand (16 queries x 16 keys of this block), split hi/lo
+    uint32_t ph[4], pl[4];
+    split2(sc[0][0], sc[0][1], ph[0], pl[0]);
+    split2(sc[0][2], sc[0][3], ph[1], pl[1]);
+    split2(sc[1][0], sc[1][1], ph[2], pl[2]);
+    split2(sc[1][2], sc[1][3], ph[3], pl[3]);
+    // transposed ldmatrix rows: matrix m -> keys (m % 2) * 8 + (lane % 8), dims (m / 2) * 8
+    const int voff = (kb * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * 72 + ((lane >> 4) << 3);
+#pragma unroll
+    for (int n2 = 0; n2 < 4; ++n2) {  // dims 16 n2 .. 16 n2 + 15 = n8 blocks 2 n2, 2 n2 + 1
+      uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+      ldsm_x4_trans(Vh + voff + 16 * n2, h0, h1, h2, h3);
+      ldsm_x4_trans(Vl + voff + 16 * n2, l0, l1, l2, l3);
+      float *oa = o[2 * n2], *ob = o[2 * n2 + 1];
+      mma16816(oa[0], oa[1], oa[2], oa[3], ph[0], ph[1], ph[2], ph[3], h0, h1);
+      mma16816(ob[0], ob[1], ob[2], ob[3], ph[0], ph[1], ph[2], ph[3], h2, h3);
+      mma16816(oa[0], oa[1], oa[2], oa[3], ph[0], ph[1], ph[2], ph[3], l0, l1);
+      mma16816(ob[0], ob[1], ob[2], ob[3], ph[0], ph[1], ph[2], ph[3], l2, l3);
+      mma16816(oa[0], oa[1], oa[2], oa[3], pl[0], pl[1], pl[2], pl[3], h0, h1);
+      mma16816(ob[0], ob[1], ob[2], ob[3], pl[0], pl[1], pl[2], pl[3], h2, h3);
+    }
+  }
+  la += __shfl_xor_sync(0xffffffffu, la, 1);
+  la += __shfl_xor_sync(0xffffffffu, la, 2);
+  lb += __shfl_xor_sync(0xffffffffu, lb, 1);
+  lb += __shfl_xor_sync(0xffffffffu, lb, 2);
+  const float inva = 1.0f / la, invb = 1.0f / lb;
+#pragma unroll
+  for (int nd = 0; nd < 8; ++nd) {
+    const int d = nd * 8 + 2 * t;
+    if (ia < p) {
+      const float x0 = o[nd][0] * inva, x1 = o[nd][1] * inva;
+      const size_t oo = (tok0 + ia) * E + h * 64 + d;
+      uint32_t hw, lw;
+      split2(x0, x1, hw, lw);
+      *reinterpret_cast<uint32_t *>(a.oh + oo) = hw;
+      *reinterpret_cast<uint32_t *>(a.ol + oo) = lw;
+      if (a.o32) *reinterpret_cast<float2 *>(a.o32 + oo) = make_float2(x0, x1);
+    }
+    if (ib < p) {
+      const float x0 = o[nd][2] * invb, x1 = o[nd][3] * invb;
+      const size_t oo = (tok0 + ib) * E + h * 64 + d;
+      uint32_t hw, lw;
+      split2(x0, x1, hw, lw);
+      *reinterpret_cast<uint32_t *>(a.oh + oo) = hw;
+      *reinterpret_cast<uint32_t *>(a.ol + oo) = lw;
+      if (a.o32) *reinterpret_cast<float2 *>(a.o32 + oo) = make_float2(x0, x1);
+    }
+  }
+}
+
 // Group attention for one (series, patch): every head (one warp each) over
 // the series' variate rows at that patch (mask.rs:69-82).  Rows whose patch
 // is whole padding are blocked keys; such a query averages V over the
@@ -707,6 +1025,14 @@ cudaError_t t0b_launch_resid_split(float *x, const float *y, const float *g, __h
   return cudaGetLastError();
 }
 cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
+  if (a.p <= kAttnMmaMaxP) {
+    const int QB = (a.p + 15) / 16, PK = 16 * QB;
+    const size_t smem = (size_t)(4 * PK * 72) * sizeof(__half);
+    cudaError_t e = cudaFuncSetAttribute(attn_time_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attn_time_mma_kernel<<<dim3(a.R, a.H), 32 * QB, smem, st>>>(a);
+    return cudaGetLastError();
+  }
   if (a.p <= kAttnTiledMaxP) {
     const int PP = (a.p + 3) & ~3;
     const size_t smem = (size_t)(PP * 64 * 3 + PP * PP) * sizeof(float);

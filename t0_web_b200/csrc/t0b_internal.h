@@ -42,6 +42,9 @@ struct AttnArgs {
   // and k as they are read; on TIME layers (use_rope) then xpos RoPE with the
   // tables rope = [4][p][64]: cos, sin, scale, 1/scale (k uses 1/scale).
   const float *qn, *kn, *rope;
+  // the same tables without duplicates, [p][128]: cos[32], sin[32] per
+  // rotated pair, scale[32], 1/scale[32] per dim mod 32
+  const float *rope_c;
   int use_rope;
   int R, p, E, H, n_series;
   int max_nrows;  // largest series_nrows entry (host-side bound for the group kernel)

@@ -393,7 +393,8 @@ t0b_status rope_tables(t0b_model *m, int p, const float **out) {
     return T0B_OK;
   }
   const int hd = 64, half = 32;
-  std::vector<float> h((size_t)4 * p * hd);
+  // [4][p][hd] full tables, then the [p][128] compact copy
+  std::vector<float> h((size_t)4 * p * hd + (size_t)p * 128);
   float *cs = h.data(), *sn = cs + (size_t)p * hd, *sc = sn + (size_t)p * hd, *si = sc + (size_t)p * hd;
   const double theta = 10000.0, base512 = 512.0;
   const double max_half = std::floor((double)(p - 1) / 2.0);
@@ -410,6 +411,14 @@ t0b_status rope_tables(t0b_model *m, int p, const float **out) {
       si[pos * hd + j] = si[pos * hd + half + j] = 1.0f / s;  // k side (ops.rs:135-136 recip)
     }
   }
+  float *cc = si + (size_t)p * hd;
+  for (int pos = 0; pos < p; ++pos)
+    for (int j = 0; j < half; ++j) {
+      cc[pos * 128 + j] = cs[pos * hd + 2 * j];
+      cc[pos * 128 + 32 + j] = sn[pos * hd + 2 * j];
+      cc[pos * 128 + 64 + j] = sc[pos * hd + j];
+      cc[pos * 128 + 96 + j] = si[pos * hd + j];
+    }
   float *d = nullptr;
   if (cudaMalloc(&d, h.size() * 4) != cudaSuccess) return fail(T0B_ERR_OOM, "t0b: out of device memory");
   CUDA_TRY(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
@@ -656,6 +665,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   aa.max_nrows = ps.s_nrows.empty() ? 0 : *std::max_element(ps.s_nrows.begin(), ps.s_nrows.end());
   const int M = (int)T;
   aa.rope = rope;
+  aa.rope_c = rope + (size_t)4 * p * 64;
 
   for (int l = 0; l < m->L; ++l) {
     const LayerW &w = m->layers[l];
