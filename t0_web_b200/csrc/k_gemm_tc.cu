@@ -24,7 +24,7 @@
 // Residual adds, QK-norm and RoPE run in the row kernels that consume these
 // outputs.
 //
-// Warp roles (640 threads):
+// Warp roles (896 threads):
 //   warp 0      TMA producer: Ah/Al tiles and the raw blocks of the tile's
 //               weight rows (16-byte aligned superset window of the 34/18-byte
 //               block), with mbarrier completion.
@@ -33,7 +33,7 @@
 //   warps 4-11  dequantize raw blocks (one weight row per thread per stage)
 //               -> Wh/Wl tiles in the canonical K-major SW64 layout (generic
 //               stores + proxy fence).
-//   warps 12-19 epilogue, two warps per TMEM lane quadrant (128 columns
+//   warps 12-27 epilogue, four warps per TMEM lane quadrant (64 columns
 //               each): bias + RMSNorm row scale (PLAIN) or SwiGLU, staged
 //               in shared memory and written by TMA stores.
 #include <cuda.h>
@@ -44,8 +44,9 @@
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 32;  // BK: one Q8_0/Q4_0 block column of K per stage
-constexpr int XS = 4, WS = 3, RS = 3;       // ring depths: activation, dequantized weight, raw weight
-constexpr int NTHREADS = 640;
+constexpr int XS = 3, WS = 3, RS = 3;       // ring depths: activation, dequantized weight, raw weight
+constexpr int NTHREADS = 896;
+constexpr int EPI_WARPS = 16;  // warps 12-27, four per TMEM lane quadrant
 constexpr uint32_t X_TILE = BM * BK * 2;  // 8 KB, one of hi / lo
 constexpr uint32_t W_TILE = BN * BK * 2;  // 16 KB, one of hi / lo
 constexpr uint32_t OFF_XH = 0;
@@ -72,7 +73,7 @@ struct Cfg {
   static constexpr uint32_t OFF_EPI = OFF_RAW + RS * RAW_SLOT;  // tile bias for the epilogue
   // output staging for the TMA stores, 1024-aligned (swizzle pattern period)
   static constexpr uint32_t OFF_STG = (OFF_EPI + BN * 4 + 1023u) & ~1023u;
-  static constexpr uint32_t OFF_BAR = OFF_STG + 8 * STG_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_STG + EPI_WARPS * STG_BYTES;
   static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;  // barriers + alignment slack
   static_assert(SMEM <= 232448, "shared memory over the 227 KB per-block limit");
 };
@@ -206,7 +207,7 @@ T0B_DEV void dequant_row_at(int off, const uint8_t *src, float wscale, uint8_t *
   }
 }
 
-T0B_DEV void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }  // the 8 epilogue warps only
+T0B_DEV void epi_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }  // the 16 epilogue warps only
 
 template <int QT>
 __global__ void __launch_bounds__(NTHREADS, 1)
@@ -252,7 +253,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&w_empty[i], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 256);
+    mbar_init(acc_empty, 32 * EPI_WARPS);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -368,13 +369,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Each warp owns 32 rows (its TMEM lane quadrant) x half the columns.  A
+    // Each warp owns 32 rows (its TMEM lane quadrant) x a quarter of the columns.  A
     // chunk of 16 columns goes TMEM -> registers (bias, row scale, SwiGLU)
     // -> this warp's swizzled staging buffer -> one TMA store by lane 0, so
     // global writes are whole rows, asynchronous and clipped at row M.
     const int q = warp & 3;             // TMEM lane quadrant this warp may access
-    const int half = (warp - 12) >> 2;  // which half of the tile's columns
-    const int et = threadIdx.x - 384;   // 0..255
+    const int quarter = (warp - 12) >> 2;  // which quarter of the tile's columns
+    const int et = threadIdx.x - 384;      // 0..511
     const Epi &e = prm.epi;
     float *sb = epi_s;  // tile bias [BN] (SWIGLU: 128 gate then 128 up)
     uint8_t *stg = smem + C::OFF_STG + (warp - 12) * STG_BYTES;
@@ -383,8 +384,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       int m0, wr0, wr1, nt;
       tile_rows(tile, m0, wr0, wr1, nt);
       epi_bar();  // every epilogue thread is done with the previous tile's bias
-      {
-        const int c = et;  // 256 threads, 256 columns
+      if (et < BN) {
+        const int c = et;
         const int f = swiglu ? (c < 128 ? nt * 128 + c : e.F + nt * 128 + (c - 128)) : nt * BN + c;
         sb[c] = e.bias ? e.bias[f] : 0.0f;
       }
@@ -398,13 +399,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const bool have = mbar_wait(acc_full, it & 1, prm.err, T0B_DEVERR_WAIT_ACC, abort_flag) && !*abort_flag;
       tc_fence_after();
       // no early exit: every epilogue thread runs every iteration so the
-      // named barrier above always sees all 256 of them (after an abort the
+      // named barrier above always sees all 512 of them (after an abort the
       // waits return at once and no work is done)
       if (have) {
         if (swiglu) {
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {  // gate columns 64*half + 16c and the matching up columns
-            const int g0 = 64 * half + 16 * c;
+          for (int c = 0; c < 2; ++c) {  // gate columns 32*quarter + 16c and the matching up columns
+            const int g0 = 32 * quarter + 16 * c;
             float gv[16], uv[16];
             tmem_ld_pair16(trow + g0, gv, sc);
             tmem_ld_pair16(trow + 128 + g0, uv, sc);
@@ -447,8 +448,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         } else {  // EPI_PLAIN
 #pragma unroll 1
-          for (int c = 0; c < 8; ++c) {
-            const int c0 = 128 * half + 16 * c;
+          for (int c = 0; c < 4; ++c) {
+            const int c0 = 64 * quarter + 16 * c;
             float v[16];
             tmem_ld_pair16(trow + c0, v, sc);
 #pragma unroll
