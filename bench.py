@@ -50,6 +50,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--strong", action="store_true", help="split one fixed set of series across the ranks")
+    ap.add_argument("--workload", default="forecast", choices=["forecast", "single", "gemm", "swiglu"],
+                    help="forecast: the multi-series headline (default); single: one-series latency (cfg 1); "
+                         "gemm: standalone Q8_0 dequant-GEMM N=3072 K=1024 (cfg 2); swiglu: standalone Q4_0 "
+                         "SwiGLU F=4096 K=1024 N2=1024 (cfg 3).  The extra workloads print one line per case.")
     return ap.parse_args()
 
 
@@ -337,6 +341,131 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+
+# ----------------------------------------------------- secondary workloads
+def run_single(args):
+    """cfg 1: one univariate series, ctx 512, horizon 96 (M = 19 tokens per
+    GEMM: the small-M kernel).  value = median ms per forecast through the
+    host API; roofline = that kernel's weight bytes per launch / its mean
+    device time (HBM bound)."""
+    import numpy as np
+    import torch
+
+    from t0_web_b200 import gguf, synthetic as S, t0_fast
+    quant = args.quant
+    weights = S.random_weights(S.ALPHA, seed=0)
+    gbytes = gguf.export_gguf(weights, S.ALPHA, quant)
+    del weights
+    engine = t0_fast.Engine(0)
+    model = t0_fast.load_model_from_gguf(engine, gbytes)
+    ctx = S.sine_context(512, seed=0)
+    def timed(n):
+        for _ in range(max(args.warmup, 3)):
+            t0_fast.forecast(engine, model, ctx, 1, 512, 96)
+        out = []
+        for _ in range(n):
+            t0 = time.perf_counter()
+            t0_fast.forecast(engine, model, ctx, 1, 512, 96)
+            out.append((time.perf_counter() - t0) * 1e3)
+        return out
+
+    nsteps = max(args.steps, 20)
+    times = timed(nsteps)                 # default: passes replayed from CUDA graphs
+    model.use_graphs(False)
+    eager = timed(nsteps)                 # one host launch per kernel
+    model.use_graphs(True)
+    model.profile(True)                   # per-kernel device times (events, no graphs)
+    timed(nsteps)
+    prof = model.profile_read()
+    model.profile(False)
+    peak_tf, peak_gbs, kind = measured_peaks()
+    g = prof.get("gemm_small", {})
+    roof = None
+    if g.get("launches"):
+        gbs = g["bytes"] / (g["total_ms"] / 1e3) / 1e9
+        roof = {"kernel": "gemm_q_small_kernel", "bound": "hbm", "achieved": gbs, "peak": peak_gbs, "unit": "GB/s",
+                "frac": gbs / peak_gbs, "peak_kind": f"{kind} HBM copy", "avg_launch_us": 1e3 * g["total_ms"] / g["launches"],
+                "bytes_per_launch": g["bytes"] / g["launches"]}
+    n = nsteps
+    print(json.dumps({"metric": "single forecast latency (ctx 512, h 96, univariate)", "value": float(np.median(times)),
+                      "unit": "ms", "higher_is_better": False, "n_gpus": 1, "steps": n, "dtype": "f32",
+                      "data": "synthetic", "config": {"workload": f"cfg1 sine context, t0-alpha random-init {quant}",
+                                                      "tokens_per_gemm": 19},
+                      "eager_launch_ms": float(np.median(eager)),
+                      "device_ms_per_forecast": sum(v["total_ms"] for v in prof.values()) / n,
+                      "kernels": {k: {"launches": v["launches"] // n, "ms": round(v["total_ms"] / n, 4)}
+                                  for k, v in prof.items() if v["launches"]},
+                      "roofline": roof}), flush=True)
+    model.close()
+    engine.close()
+
+
+def run_standalone(args):
+    """cfg 2 / cfg 3 through the C ABI (t0b_gemm_q / t0b_swiglu_q), device
+    buffers, timed with CUDA events around each call (the call includes the
+    split of x into f16 planes and the weight-scale reduction + readback)."""
+    import numpy as np
+    import torch
+
+    from t0_web_b200 import gguf, synthetic as S, t0_fast
+    from t0_web_b200._lib import Q4_0, Q8_0, check, lib, ptr
+    engine = t0_fast.Engine(0)
+    dev = torch.device("cuda:0")
+    st = torch.cuda.Stream()
+    torch.cuda.set_stream(st)
+    peak_tf, peak_gbs, kind = measured_peaks()
+    rng = np.random.default_rng(0)
+    if args.workload == "gemm":
+        N, K, qt = 3072, 1024, Q8_0
+        w = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
+        wd = torch.from_numpy(gguf.quantize(w, qt)).to(dev)
+        cases = [16, 256, 4096, 65536]
+    else:
+        F, K, N2, qt = 4096, 1024, 1024, Q4_0
+        w0 = (rng.standard_normal((2 * F, K), dtype=np.float32) * np.float32(0.02))
+        w2 = (rng.standard_normal((N2, F), dtype=np.float32) * np.float32(0.02))
+        w0d = torch.from_numpy(gguf.quantize(w0, qt)).to(dev)
+        w2d = torch.from_numpy(gguf.quantize(w2, qt)).to(dev)
+        cases = [16, 1024, 65536]
+    for M in cases:
+        x = torch.randn((M, K), device=dev)
+        if args.workload == "gemm":
+            y = torch.empty((M, N), device=dev)
+            flops = 2.0 * M * N * K
+
+            def call():
+                check(lib().t0b_gemm_q(engine.handle, qt, ptr(wd), N, K, ptr(x), M, None, ptr(y), st.cuda_stream))
+        else:
+            y = torch.empty((M, N2), device=dev)
+            flops = 2.0 * M * 2 * F * K + 2.0 * M * N2 * F
+
+            def call():
+                check(lib().t0b_swiglu_q(engine.handle, qt, ptr(w0d), ptr(w2d), F, K, N2, ptr(x), M, None, None,
+                                         None, ptr(y), st.cuda_stream))
+        for _ in range(3):
+            call()
+        reps = 20 if M <= 4096 else 5
+        evs = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            call()
+            b.record(st)
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        ms = float(np.median([a.elapsed_time(b) for a, b in evs]))
+        tf = flops / (ms / 1e3) / 1e12
+        name = "Q8_0 dequant-GEMM N=3072 K=1024" if args.workload == "gemm" else \
+            "Q4_0 SwiGLU MLP F=4096 K=1024 N2=1024 (gate/up + fused SiLU, down)"
+        print(json.dumps({"metric": f"{name}, M={M}", "value": tf, "unit": "TFLOP/s (useful)", "ms_per_call": ms,
+                          "higher_is_better": True, "n_gpus": 1, "dtype": "f32-class (split-f16 x3)",
+                          "data": "synthetic N(0,0.02) weights, N(0,1) activations",
+                          "frac_of_peak": tf / peak_tf, "peak": peak_tf, "peak_kind": f"{kind} bf16 sustained",
+                          "path": "tcgen05" if M >= 128 else "mma.sync small-M",
+                          "note": "per call: x split + weight-scale reduction and readback + GEMM(s) + sync"}),
+              flush=True)
+    engine.close()
+
 # ----------------------------------------------------------- reference arm
 def run_reference(args):
     rank = int(os.environ.get("RANK", 0))
@@ -367,5 +496,9 @@ if __name__ == "__main__":
     a = parse()
     if a.impl == "reference":
         run_reference(a)
+    elif a.workload == "single":
+        run_single(a)
+    elif a.workload in ("gemm", "swiglu"):
+        run_standalone(a)
     else:
         run_ours(a)

@@ -75,6 +75,13 @@ void *t0b_model_stream(const t0b_model *m);
 /* Upper bound on tokens (rows x patches) per device pass; larger requests are
  * split into passes.  Default 262144. */
 t0b_status t0b_model_set_max_tokens(t0b_model *m, size_t max_tokens);
+/* Replay each forecast pass from a CUDA graph (default on).  A pass's launch
+ * sequence is captured the first time its shape, input/output pointers and
+ * workspace are seen, and replayed afterwards, so per-kernel host launch
+ * overhead is paid once per shape; graphs are not used while profiling is on.
+ * No reference counterpart (t0-fast records one wgpu command buffer per
+ * forward, model.rs:755-786). */
+t0b_status t0b_model_use_graphs(t0b_model *m, int on);
 
 /* ---- forecasts (host buffers; synchronous) ----
  * Output layout [rows, horizon, n_quantiles] row-major, quantile-minor.

@@ -17,7 +17,7 @@ F32, F16, Q4_0, Q8_0 = 0, 1, 2, 8
 # every symbol include/t0b.h declares
 EXPORTED = [
     "t0b_last_error", "t0b_engine_create", "t0b_engine_destroy", "t0b_model_load_gguf", "t0b_model_destroy",
-    "t0b_model_info_get", "t0b_model_set_stream", "t0b_model_stream", "t0b_model_set_max_tokens",
+    "t0b_model_info_get", "t0b_model_set_stream", "t0b_model_stream", "t0b_model_set_max_tokens", "t0b_model_use_graphs",
     "t0b_forecast", "t0b_forecast_batch", "t0b_forecast_batch_rows", "t0b_forecast_multiseries",
     "t0b_forecast_multiseries_device", "t0b_model_sync", "t0b_gemm_q", "t0b_swiglu_q", "t0b_gemm_q_noalloc", "t0b_gguf_validate",
     "t0b_quantize", "t0b_dequantize", "t0b_row_bytes", "t0b_export_gguf", "t0b_model_profile_enable",
@@ -69,6 +69,7 @@ def lib() -> C.CDLL:
     L.t0b_model_stream.argtypes = [vp]
     L.t0b_model_stream.restype = vp
     L.t0b_model_set_max_tokens.argtypes = [vp, sz]
+    L.t0b_model_use_graphs.argtypes = [vp, st]
     L.t0b_forecast.argtypes = [vp, vp, sz, sz, sz, vp]
     L.t0b_forecast_batch.argtypes = [vp, vp, sz, sz, sz, sz, vp]
     L.t0b_forecast_batch_rows.argtypes = [vp, vp, vp, sz, sz, sz, vp]

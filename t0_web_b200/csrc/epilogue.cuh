@@ -89,19 +89,21 @@ T0B_DEV float epi_cols32(const Epi &e, int m, int n0, float *v, float denom) {
   return ss;
 }
 
-// SwiGLU pair: gate columns f0..f0+31 and the matching up columns.
-T0B_DEV void epi_swiglu32(const Epi &e, int m, int f0, const float *gacc, const float *uacc, float denom) {
-  float z[32];
+// SwiGLU on NF features: gate columns f0..f0+NF-1 and the matching up
+// columns (ops.rs:49-62).
+template <int NF>
+T0B_DEV void epi_swiglu(const Epi &e, int m, int f0, const float *gacc, const float *uacc, float denom) {
+  float z[NF];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
+  for (int i = 0; i < NF; ++i) {
     float g = gacc[i] / denom + (e.bias ? e.bias[f0 + i] : 0.0f);
     float u = uacc[i] / denom + (e.bias ? e.bias[e.F + f0 + i] : 0.0f);
     z[i] = g / (1.0f + expf(-g)) * u;
   }
-  if (e.zh) store_split(e.zh, e.zl, (size_t)m * e.F + f0, z, 32);
+  if (e.zh) store_split(e.zh, e.zl, (size_t)m * e.F + f0, z, NF);
   if (e.z32) {
     float4 *dst = reinterpret_cast<float4 *>(e.z32 + (size_t)m * e.F + f0);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) dst[i] = make_float4(z[4 * i], z[4 * i + 1], z[4 * i + 2], z[4 * i + 3]);
+    for (int i = 0; i < NF / 4; ++i) dst[i] = make_float4(z[4 * i], z[4 * i + 1], z[4 * i + 2], z[4 * i + 3]);
   }
 }

@@ -84,12 +84,26 @@ struct LayerW {
   bool group;
 };
 
+// Grows the small-M GEMM's split-K workspace to at least (part_floats,
+// cnt_ints); newly allocated counters are zeroed on `st` (the kernels leave
+// them at zero).  Only call it while no kernel of `st` uses the buffers.
+cudaError_t reserve_small_ws(DBuf &part, DBuf &cnt, size_t part_floats, size_t cnt_ints, cudaStream_t st) {
+  cudaError_t e = part.reserve(part_floats * 4);
+  if (e != cudaSuccess) return e;
+  if (cnt_ints * 4 > cnt.bytes) {
+    if ((e = cnt.reserve(cnt_ints * 4)) != cudaSuccess) return e;
+    return cudaMemsetAsync(cnt.p, 0, cnt.bytes, st);
+  }
+  return cudaSuccess;
+}
+
 }  // namespace
 
 struct t0b_engine {
   int device = 0;
   int *d_err = nullptr;
   DBuf scratch_xh, scratch_xl, scratch_zh, scratch_zl, scratch_red;
+  DBuf small_part, small_cnt;  // split-K workspace of the small-M GEMM
 };
 
 struct t0b_model {
@@ -110,6 +124,7 @@ struct t0b_model {
   // workspace
   DBuf x, qkv, feat, ssq, xo, dhid, dout, loc, scl;
   DBuf xh, xl, ah, al, hh, hl;
+  DBuf small_part, small_cnt;  // split-K workspace of the small-M GEMM
   DBuf meta;  // row/series metadata
   HBuf hmeta;
   DBuf ctx_stage, out_stage;
@@ -124,7 +139,21 @@ struct t0b_model {
   std::vector<Rec> recs;
   std::vector<cudaEvent_t> ev_pool;
   t0b_kernel_stats stats[7];
+  // CUDA graphs of whole passes, keyed by everything the captured launch
+  // sequence depends on (shape, input/output and workspace pointers)
+  bool use_graphs = true;
+  struct GraphEntry {
+    cudaGraphExec_t exec;
+    uint64_t launches, last_use;
+  };
+  std::map<std::vector<uint64_t>, GraphEntry> graphs;
+  uint64_t graph_clock = 0;
+  void drop_graphs() {
+    for (auto &kv : graphs) cudaGraphExecDestroy(kv.second.exec);
+    graphs.clear();
+  }
   ~t0b_model() {
+    drop_graphs();
     for (auto &r : recs) {
       cudaEventDestroy(r.a);
       cudaEventDestroy(r.b);
@@ -495,9 +524,15 @@ cudaError_t qgemm(t0b_model *m, const __half *ah, const __half *al, int M, int K
       return t0b_launch_gemm_tc(m->qt, ah, al, M, K, W, wrows, wshift, epi, m->d_err, m->stream);
     });
   }
-  if (epi.kind == EPI_RESID) epi.ssq_out_nt = epi.N / 64;
-  return launch(m, KC_GEMM_SMALL, flops, bytes,
-                [&] { return t0b_launch_gemm_small(m->qt, ah, al, M, K, W, epi, m->d_err, m->stream); });
+  if (epi.kind == EPI_RESID) epi.ssq_out_nt = epi.N / 32;
+  size_t pf = 0, ci = 0;
+  t0b_small_workspace(M, K, epi, &pf, &ci);
+  const bool split = pf && m->small_part.bytes >= pf * 4 && m->small_cnt.bytes >= ci * 4;
+  float *part = split ? m->small_part.as<float>() : nullptr;
+  int *cnt = split ? m->small_cnt.as<int>() : nullptr;
+  return launch(m, KC_GEMM_SMALL, flops, bytes, [&] {
+    return t0b_launch_gemm_small(m->qt, ah, al, M, K, W, epi, m->d_err, m->stream, part, cnt);
+  });
 }
 
 // Residual branch output GEMM (wO or mlp.2): x += A . W^T + bias, then the
@@ -530,7 +565,7 @@ cudaError_t resid_gemm(t0b_model *m, const __half *ah, const __half *al, int M, 
   r.xh = m->xh.as<__half>();
   r.xl = m->xl.as<__half>();
   r.ssq_out = m->ssq.as<float>();
-  *ssq_nt = E / 64;
+  *ssq_nt = E / 32;
   return qgemm(m, ah, al, M, K, W, E, wshift, r);
 }
 
@@ -539,7 +574,23 @@ t0b_status ensure_ws(t0b_model *m, size_t T, size_t R, size_t nout) {
   CUDA_TRY(m->x.reserve(T * E * 4));
   CUDA_TRY(m->qkv.reserve(T * 3 * E * 4));
   CUDA_TRY(m->feat.reserve(T * 96 * 4));
-  CUDA_TRY(m->ssq.reserve(T * 16 * 4));
+  CUDA_TRY(m->ssq.reserve(T * std::max<size_t>(16, E / 32) * 4));
+  if ((int)T < m->tc_min_tokens) {  // small-M GEMMs: split-K workspace for the layer's four shapes
+    size_t pf = 0, ci = 0;
+    Epi sh[4]{};
+    sh[0].kind = EPI_PLAIN, sh[0].N = 3 * (int)E;
+    sh[1].kind = EPI_RESID, sh[1].N = (int)E;
+    sh[2].kind = EPI_SWIGLU, sh[2].N = 2 * (int)F, sh[2].F = (int)F;
+    sh[3].kind = EPI_RESID, sh[3].N = (int)E;
+    const int Ks[4] = {(int)E, (int)E, (int)E, (int)F};
+    for (int i = 0; i < 4; ++i) {
+      size_t a = 0, b = 0;
+      t0b_small_workspace((int)T, Ks[i], sh[i], &a, &b);
+      pf = std::max(pf, a);
+      ci = std::max(ci, b);
+    }
+    if (pf) CUDA_TRY(reserve_small_ws(m->small_part, m->small_cnt, pf, ci, m->stream));
+  }
   CUDA_TRY(m->xh.reserve(T * E * 2));
   CUDA_TRY(m->xl.reserve(T * E * 2));
   CUDA_TRY(m->ah.reserve(T * E * 2));
@@ -590,11 +641,34 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   const size_t o_fv = put(ps.row_fv.data(), (size_t)R * 4);
   const size_t o_s0 = put(ps.s_row0.data(), (size_t)ns * 4);
   const size_t o_sn = put(ps.s_nrows.data(), (size_t)ns * 4);
-  CUDA_TRY(cudaMemcpyAsync(m->meta.p, hb, o, cudaMemcpyHostToDevice, m->stream));
   uint8_t *db = (uint8_t *)m->meta.p;
-
   const float *rope = nullptr;
   if ((st = rope_tables(m, p, &rope)) != T0B_OK) return st;
+
+  // Everything from here on is stream work only (the metadata copy from the
+  // pinned staging buffer and the kernels), so without profiling it is
+  // captured once per pass shape into a CUDA graph and replayed.
+  const bool graph = m->use_graphs && !m->prof && m->stream != nullptr;
+  std::vector<uint64_t> key;
+  if (graph) {
+    key = {(uint64_t)R, (uint64_t)p, (uint64_t)hp, (uint64_t)ns, (uint64_t)ps.horizon, (uint64_t)o,
+           (uint64_t)(uintptr_t)ps.ctx, (uint64_t)(uintptr_t)ps.out, (uint64_t)(uintptr_t)hb,
+           (uint64_t)(uintptr_t)rope, (uint64_t)m->tc_min_tokens,
+           // the group-attention kernel variant depends on the largest series
+           (uint64_t)(ps.s_nrows.empty() ? 0 : *std::max_element(ps.s_nrows.begin(), ps.s_nrows.end()))};
+    for (const DBuf *b : {&m->x, &m->qkv, &m->feat, &m->ssq, &m->xo, &m->dhid, &m->dout, &m->loc, &m->scl, &m->xh,
+                          &m->xl, &m->ah, &m->al, &m->hh, &m->hl, &m->small_part, &m->small_cnt, &m->meta})
+      key.push_back((uint64_t)(uintptr_t)b->p);
+    auto it = m->graphs.find(key);
+    if (it != m->graphs.end()) {
+      it->second.last_use = ++m->graph_clock;
+      m->launches += it->second.launches;
+      CUDA_TRY(cudaGraphLaunch(it->second.exec, m->stream));
+      return T0B_OK;
+    }
+  }
+  auto body = [&]() -> t0b_status {
+  CUDA_TRY(cudaMemcpyAsync(m->meta.p, hb, o, cudaMemcpyHostToDevice, m->stream));
 
   // 1. pad + causal scaler + patch features
   PrepArgs pa{};
@@ -750,6 +824,32 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
                                ps.horizon, m->nq, m->info.scaler_use_arcsinh, m->stream);
   }));
   return T0B_OK;
+  };
+  if (!graph) return body();
+  const uint64_t launches0 = m->launches;
+  CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeRelaxed));
+  const t0b_status bs = body();
+  cudaGraph_t g = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(m->stream, &g);
+  if (bs != T0B_OK) {
+    if (g) cudaGraphDestroy(g);
+    return bs;
+  }
+  if (ce != cudaSuccess) return fail(T0B_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+  cudaGraphExec_t ex = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&ex, g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) return fail(T0B_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ie));
+  if (m->graphs.size() >= 32) {  // keep the 32 most recently used pass shapes
+    auto lru = m->graphs.begin();
+    for (auto it = m->graphs.begin(); it != m->graphs.end(); ++it)
+      if (it->second.last_use < lru->second.last_use) lru = it;
+    cudaGraphExecDestroy(lru->second.exec);
+    m->graphs.erase(lru);
+  }
+  m->graphs[key] = {ex, m->launches - launches0, ++m->graph_clock};
+  CUDA_TRY(cudaGraphLaunch(ex, m->stream));
+  return T0B_OK;
 }
 
 t0b_status check_horizon(size_t horizon) {
@@ -895,6 +995,15 @@ extern "C" void *t0b_model_stream(const t0b_model *m) { return m ? (void *)m->st
 extern "C" t0b_status t0b_model_set_max_tokens(t0b_model *m, size_t max_tokens) {
   if (!m || max_tokens < 64) return fail(T0B_ERR_INVALID, "t0b_model_set_max_tokens: need >= 64");
   m->max_tokens = max_tokens;
+  return T0B_OK;
+}
+
+extern "C" t0b_status t0b_model_use_graphs(t0b_model *m, int on) {
+  if (!m) return fail(T0B_ERR_INVALID, "t0b_model_use_graphs: NULL model");
+  CUDA_TRY(cudaSetDevice(m->eng->device));
+  CUDA_TRY(cudaStreamSynchronize(m->stream));
+  m->use_graphs = on != 0;
+  if (!on) m->drop_graphs();
   return T0B_OK;
 }
 
@@ -1046,11 +1155,22 @@ t0b_status device_weight_shift(t0b_engine *e, int qt, const uint8_t *W, size_t n
   return T0B_OK;
 }
 
-cudaError_t engine_qgemm(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
-                         int wshift, Epi &epi, int *err, cudaStream_t st) {
+cudaError_t engine_qgemm(t0b_engine *e, int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W,
+                         int wrows, int wshift, Epi &epi, int *err, cudaStream_t st) {
   const bool tc = M >= 128;
   if (tc) return t0b_launch_gemm_tc(qt, ah, al, M, K, W, wrows, wshift, epi, err, st);
-  return t0b_launch_gemm_small(qt, ah, al, M, K, W, epi, err, st);
+  size_t pf = 0, ci = 0;
+  t0b_small_workspace(M, K, epi, &pf, &ci);
+  if (!pf) return t0b_launch_gemm_small(qt, ah, al, M, K, W, epi, err, st);
+  // a launch earlier in the same call may still use the workspace: let it
+  // finish before the workspace grows
+  if (pf * 4 > e->small_part.bytes || ci * 4 > e->small_cnt.bytes) {
+    cudaError_t w = cudaStreamSynchronize(st);
+    if (w != cudaSuccess) return w;
+  }
+  cudaError_t r = reserve_small_ws(e->small_part, e->small_cnt, pf, ci, st);
+  if (r != cudaSuccess) return r;
+  return t0b_launch_gemm_small(qt, ah, al, M, K, W, epi, err, st, e->small_part.as<float>(), e->small_cnt.as<int>());
 }
 
 t0b_status engine_check(t0b_engine *e, cudaStream_t st) {
@@ -1086,7 +1206,7 @@ extern "C" t0b_status t0b_gemm_q(t0b_engine *e, int ggml_type, const void *w_dev
   ep.bias = bias_dev;
   ep.y = y_dev;
   ep.ldy = N;
-  CUDA_TRY(engine_qgemm(qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, (const uint8_t *)w_dev, N,
+  CUDA_TRY(engine_qgemm(e, qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, (const uint8_t *)w_dev, N,
                         sh, ep, e->d_err, st));
   return engine_check(e, st);
 }
@@ -1118,7 +1238,7 @@ extern "C" t0b_status t0b_swiglu_q(t0b_engine *e, int ggml_type, const void *w0_
   sg.zh = e->scratch_zh.as<__half>();
   sg.zl = e->scratch_zl.as<__half>();
   sg.z32 = z_dev;
-  CUDA_TRY(engine_qgemm(qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, (const uint8_t *)w0_dev,
+  CUDA_TRY(engine_qgemm(e, qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, (const uint8_t *)w0_dev,
                         2 * F, sh0, sg, e->d_err, st));
   Epi dn{};
   dn.kind = EPI_PLAIN;
@@ -1127,7 +1247,7 @@ extern "C" t0b_status t0b_swiglu_q(t0b_engine *e, int ggml_type, const void *w0_
   dn.bias = b2_dev;
   dn.y = y_dev;
   dn.ldy = N2;
-  CUDA_TRY(engine_qgemm(qt, e->scratch_zh.as<__half>(), e->scratch_zl.as<__half>(), M, F, (const uint8_t *)w2_dev, N2,
+  CUDA_TRY(engine_qgemm(e, qt, e->scratch_zh.as<__half>(), e->scratch_zl.as<__half>(), M, F, (const uint8_t *)w2_dev, N2,
                         sh2, dn, e->d_err, st));
   return engine_check(e, st);
 }

@@ -94,6 +94,10 @@ class GpuModel:
     def set_max_tokens(self, n: int) -> None:
         check(lib().t0b_model_set_max_tokens(self._h, int(n)))
 
+    def use_graphs(self, on: bool = True) -> None:
+        """Replay forecast passes from cached CUDA graphs (default on)."""
+        check(lib().t0b_model_use_graphs(self._h, int(on)))
+
     def sync(self) -> None:
         check(lib().t0b_model_sync(self._h))
 

@@ -101,6 +101,36 @@ def test_chunking_is_invisible(engine, gpu_model):
     assert max_abs(one, many) <= TOL
 
 
+def test_graph_replay_matches_eager_launches(engine, gpu_model):
+    """Passes replayed from cached CUDA graphs give the eager launches' outputs
+    bit for bit.  The two multiseries cases share every shape and buffer but
+    not the largest series (8 vs 12 rows), which selects a different
+    group-attention kernel, so a replay keyed too coarsely would show here."""
+    m = gpu_model("q8_0")
+    ctx16, _ = S.multiseries(2, 512, seed=11, n_variates=8)
+    cases = [
+        lambda: t0_fast.forecast_multiseries(engine, m, ctx16, np.array([8, 8], np.int32), 512, 96),
+        lambda: t0_fast.forecast_multiseries(engine, m, ctx16, np.array([4, 12], np.int32), 512, 96),
+        lambda: t0_fast.forecast(engine, m, S.sine_context(512, seed=0), 1, 512, 96),
+        lambda: t0_fast.forecast_multiseries(engine, m, *S.multiseries(6, 2048, seed=2, n_variates=3), 2048, 96),
+    ]
+    m.use_graphs(False)
+    try:
+        eager = [c() for c in cases]
+        n0 = m.launch_count()
+        for c in cases:
+            c()
+        eager_launches = m.launch_count() - n0
+    finally:
+        m.use_graphs(True)
+    for rep in range(2):  # capture, then replay
+        n0 = m.launch_count()
+        for i, c in enumerate(cases):
+            got = c()
+            assert np.array_equal(got, eager[i]), (rep, i, max_abs(got, eager[i]))
+        assert m.launch_count() - n0 == eager_launches
+
+
 def test_horizon_limit_is_an_error(engine, gpu_model):
     with pytest.raises(T0bError):
         t0_fast.forecast(engine, gpu_model("q8_0"), S.sine_context(64), 1, 64, 1025)
