@@ -202,6 +202,27 @@ T0B_DEV void mma16816(float &d0, float &d1, float &d2, float &d3, uint32_t a0, u
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Four 8x8 b16 matrices from shared memory (rows addressed by lanes 8m..8m+7
+// for matrix m), plain or transposed: the mma.sync B-fragment loaders.
+T0B_DEV void ldsm_x4(const void *row_addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(row_addr)));
+}
+T0B_DEV void ldsm_x4_trans(const void *row_addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(row_addr)));
+}
+
+// ------------------------------------------- programmatic dependent launch
+// pdl_wait: block until the previous kernel on the stream has completed and
+// its writes are visible (a no-op when this kernel was launched normally).
+// pdl_launch_dependents: let the next kernel, if it was launched as a
+// programmatic dependent, start its independent prologue now.
+T0B_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+T0B_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- cp.async
 T0B_DEV void cp_async16(void *dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");

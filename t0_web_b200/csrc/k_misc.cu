@@ -14,29 +14,60 @@
 #include "t0b_internal.h"
 
 // ============================================================== prep
-// One thread per variate row: a sequential Welford scan over the padded
-// row, exactly the reference recurrence in f32.
-__global__ void prep_kernel(PrepArgs a) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= a.R) return;
-  const int P = 32;
+// One warp per variate row.  The causal scaler is the reference's Welford
+// recurrence in f32 (scaler.rs:44-118), inherently sequential: lane 0 runs it
+// over a chunk of kPrepChunk steps and records (count, mean, m2) after every
+// step in shared memory; then all 32 lanes turn those states into the
+// per-step loc / scale, the scaled value and the patch features in parallel
+// (lane = step within the patch, so feature rows are written coalesced).
+constexpr int kPrepChunk = 256;  // steps per chunk (a multiple of the patch size 32)
+constexpr int kPrepWarps = 4;
+
+__global__ void __launch_bounds__(32 * kPrepWarps) prep_kernel(PrepArgs a) {
+  __shared__ float s_x[kPrepWarps][kPrepChunk], s_cnt[kPrepWarps][kPrepChunk];
+  __shared__ float s_mean[kPrepWarps][kPrepChunk], s_m2[kPrepWarps][kPrepChunk];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kPrepWarps + w;
+  if (r >= a.R) return;  // whole warp
   const int lead = a.row_lead[r];
   const int len = a.row_len[r];
   const float *src = a.ctx + a.row_off[r];
-  float count = 0.0f, mean = 0.0f, m2 = 0.0f;
-  float feat_v[32];
+  const int steps = a.p * 32;
   const int hp0 = a.p - a.hp - 1;  // first output patch
-  for (int patch = 0; patch < a.p; ++patch) {
-    float *f = a.feat + ((size_t)r * a.p + patch) * 96;
-    float lo = 0.0f, sc = 1.0f;
-    for (int k = 0; k < P; ++k) {
-      const int t = patch * P + k;
+  float count = 0.0f, mean = 0.0f, m2 = 0.0f;  // lane 0's recurrence state
+  for (int c0 = 0; c0 < steps; c0 += kPrepChunk) {
+    const int n = min(kPrepChunk, steps - c0);
+    // raw values of the chunk (0 outside the context), coalesced
+    for (int i = lane; i < n; i += 32) {
+      const int t = c0 + i;
+      s_x[w][i] = (t >= lead && t < lead + len) ? src[t - lead] : 0.0f;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      for (int i = 0; i < n; ++i) {
+        const int t = c0 + i;
+        const float x = s_x[w][i];
+        if (t >= lead && t < lead + len && !isnan(x)) {
+          count = __fadd_rn(count, 1.0f);
+          const float delta = __fsub_rn(x, mean);
+          mean = __fadd_rn(mean, __fdiv_rn(delta, count));
+          const float delta2 = __fsub_rn(x, mean);
+          m2 = __fadd_rn(m2, __fmul_rn(delta, delta2));
+        }
+        s_cnt[w][i] = count;
+        s_mean[w][i] = mean;
+        s_m2[w][i] = m2;
+      }
+    }
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+      const int t = c0 + i, patch = t >> 5, k = t & 31;
       int mask;  // 0 valid, 1 pad, 2 missing, 4 withheld
       float x = 0.0f;
       if (t < lead) {
         mask = 1;
       } else if (t < lead + len) {
-        x = src[t - lead];
+        x = s_x[w][i];
         if (isnan(x)) {
           mask = 2;
           x = 0.0f;
@@ -46,33 +77,25 @@ __global__ void prep_kernel(PrepArgs a) {
       } else {
         mask = 4;
       }
-      if (mask == 0) {
-        count = __fadd_rn(count, 1.0f);
-        float delta = __fsub_rn(x, mean);
-        mean = __fadd_rn(mean, __fdiv_rn(delta, count));
-        float delta2 = __fsub_rn(x, mean);
-        m2 = __fadd_rn(m2, __fmul_rn(delta, delta2));
-      }
-      if (mask == 1) {  // padding sentinel: group id < 0
-        lo = 0.0f;
-        sc = 1.0f;
-      } else {
-        lo = mean;
-        float var = count > 1.0f ? fmaxf(__fdiv_rn(m2, __fsub_rn(count, 1.0f)), 0.0f) : 0.0f;
+      float lo = 0.0f, sc = 1.0f;
+      if (mask != 1) {  // padding sentinel (group id < 0) keeps loc 0 / scale 1
+        const float cnt = s_cnt[w][i];
+        lo = s_mean[w][i];
+        const float var = cnt > 1.0f ? fmaxf(__fdiv_rn(s_m2[w][i], __fsub_rn(cnt, 1.0f)), 0.0f) : 0.0f;
         sc = a.variance_offset ? __fsqrt_rn(__fadd_rn(var, a.eps)) : fmaxf(__fsqrt_rn(var), a.eps);
       }
-      float z = __fdiv_rn(__fsub_rn(x, lo), sc);
-      feat_v[k] = a.use_arcsinh ? asinhf(z) : z;
+      const float zv = __fdiv_rn(__fsub_rn(x, lo), sc);
+      float *f = a.feat + ((size_t)r * a.p + patch) * 96;
+      f[k] = a.use_arcsinh ? asinhf(zv) : zv;
       f[32 + k] = (float)k / 32.0f;
       f[64 + k] = mask == 0 ? 1.0f : 0.0f;
+      if (k == 31 && patch >= hp0 && patch < hp0 + a.hp) {  // stats at the patch's last step
+        const size_t o = (size_t)r * a.hp + (patch - hp0);
+        a.out_loc[o] = lo;
+        a.out_scale[o] = sc;
+      }
     }
-#pragma unroll 8
-    for (int k = 0; k < 32; ++k) f[k] = feat_v[k];
-    if (patch >= hp0 && patch < hp0 + a.hp) {  // stats at the patch's last step
-      const size_t o = (size_t)r * a.hp + (patch - hp0);
-      a.out_loc[o] = lo;
-      a.out_scale[o] = sc;
-    }
+    __syncwarp();
   }
 }
 
@@ -126,10 +149,76 @@ __global__ void __launch_bounds__(256) sgemm_nt_kernel(SgemmArgs a) {
   }
 }
 
+// Few rows (M <= 32 per CTA): a CTA owns 32 output columns and MT rows,
+// stages its whole A [MT, K] and B [32, K] slices in shared memory with one
+// round of 16-byte cp.async copies, and its 8 warps split K: lane n
+// accumulates column n for every row (A values broadcast from shared
+// memory), then the warps' partials are added in warp order.
+constexpr int kSgemmSmallWarps = 8;
+
+template <int MT>
+__global__ void __launch_bounds__(32 * kSgemmSmallWarps) sgemm_small_kernel(SgemmArgs a) {
+  extern __shared__ __align__(16) float sg_smem[];
+  const int KP = a.K + 4;  // row pitch (floats): 16-byte pad keeps 128-bit row reads conflict-free
+  float *As = sg_smem;                      // [MT][KP]
+  float *Bs = As + (size_t)MT * KP;         // [32][KP]
+  float *red = sg_smem;                     // [warps][MT][32], reuses A/B after the main loop
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * MT, n0 = blockIdx.x * 32;
+  const int g4 = a.K / 4;  // 16-byte granules per row
+  for (int i = threadIdx.x; i < (MT + 32) * g4; i += blockDim.x) {
+    const int row = i / g4, q = i - row * g4;
+    if (row < MT) {
+      const int m = min(m0 + row, a.M - 1);  // rows past M duplicate a valid row; outputs dropped
+      cp_async16(As + (size_t)row * KP + 4 * q, a.A + (size_t)m * a.lda + 4 * q);
+    } else {
+      const int n = min(n0 + row - MT, a.N - 1);
+      cp_async16(Bs + (size_t)(row - MT) * KP + 4 * q, a.B + (size_t)n * a.ldb + 4 * q);
+    }
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  float acc[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+  const int kw = a.K / kSgemmSmallWarps;  // a multiple of 4
+  const float *brow = Bs + (size_t)lane * KP + w * kw;
+  for (int k = 0; k < kw; k += 4) {
+    const float4 b = *reinterpret_cast<const float4 *>(brow + k);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const float4 x = *reinterpret_cast<const float4 *>(As + (size_t)m * KP + w * kw + k);
+      acc[m] = fmaf(x.x, b.x, acc[m]);
+      acc[m] = fmaf(x.y, b.y, acc[m]);
+      acc[m] = fmaf(x.z, b.z, acc[m]);
+      acc[m] = fmaf(x.w, b.w, acc[m]);
+    }
+  }
+  __syncthreads();  // A/B no longer read: reuse as the partial tiles
+#pragma unroll
+  for (int m = 0; m < MT; ++m) red[((size_t)w * MT + m) * 32 + lane] = acc[m];
+  __syncthreads();
+  for (int i = threadIdx.x; i < MT * 32; i += blockDim.x) {
+    const int m = m0 + i / 32, n = n0 + (i & 31);
+    float v = red[i];
+#pragma unroll
+    for (int q = 1; q < kSgemmSmallWarps; ++q) v += red[(size_t)q * MT * 32 + i];
+    if (m >= a.M || n >= a.N) continue;
+    if (a.bias) v = v + a.bias[n];
+    if (a.bias2) v = v + a.bias2[n];
+    if (a.bias3) v = v + a.bias3[n];
+    if (a.relu) v = fmaxf(v, 0.0f);
+    float *c = a.C + (size_t)m * a.ldc + n;
+    *c = a.accumulate ? (*c + v) : v;
+  }
+}
+
 // ============================================================== rownorm_split
 // One warp per row: xh/xl = split(x * g), ssq[r] = sum x^2 (single slot).
 __global__ void rownorm_split_kernel(const float *x, const float *g, __half *xh, __half *xl, float *ssq, int M,
                                      int E) {
+  pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
@@ -191,6 +280,7 @@ T0B_DEV float4 qk_norm_rope4(float4 v, float ss, const float *g, int d, const fl
 // (16-byte loads), q and k normalised and rotated on the way in; K keeps a
 // 65-float pitch so the lane-per-key score loop is bank-conflict free.
 __global__ void __launch_bounds__(128) attn_time_kernel(AttnArgs a) {
+  pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
   extern __shared__ float sm[];
   const int r = blockIdx.x, h = blockIdx.y;
   const int p = a.p, E = a.E;
@@ -308,6 +398,7 @@ __global__ void __launch_bounds__(128) attn_time_kernel(AttnArgs a) {
 constexpr int kAttnTiledMaxP = 131;
 
 __global__ void __launch_bounds__(128) attn_time_tiled_kernel(AttnArgs a) {
+  pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
   extern __shared__ float4 sm4[];
   float *sm = reinterpret_cast<float *>(sm4);
   const int r = blockIdx.x, h = blockIdx.y;
@@ -507,19 +598,6 @@ T0B_DEV void split2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
   lo = *reinterpret_cast<const uint32_t *>(&l);
 }
 
-// Four 8x8 b16 matrices from shared memory (rows addressed by lanes 8m..8m+7
-// for matrix m), plain or transposed: the mma.sync B-fragment loaders.
-T0B_DEV void ldsm_x4(const void *row_addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(smem_u32(row_addr)));
-}
-T0B_DEV void ldsm_x4_trans(const void *row_addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(smem_u32(row_addr)));
-}
-
 // RoPE on 16 consecutive dims 16cg..16cg+15 (8 pairs) with 16-byte table
 // loads; same arithmetic as rope_pair.
 T0B_DEV void rope16(float *x, const float *tab, int cg, bool kside) {
@@ -540,6 +618,7 @@ T0B_DEV void rope16(float *x, const float *tab, int cg, bool kside) {
 }
 
 __global__ void __launch_bounds__(256, 2) attn_time_mma_kernel(AttnArgs a) {
+  pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
   extern __shared__ uint4 smem_u4[];
   const int r = blockIdx.x, h = blockIdx.y;
   const int p = a.p, E = a.E;
@@ -790,6 +869,7 @@ __global__ void __launch_bounds__(256, 2) attn_time_mma_kernel(AttnArgs a) {
 // series' rows.  q and k get their per-head RMSNorm as they are read (no
 // RoPE on GROUP layers).
 __global__ void __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
+  pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
   const int s = blockIdx.x, patch = blockIdx.y;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (h >= a.H) return;
@@ -856,6 +936,7 @@ __global__ void __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
 // answers every query row (same semantics as attn_group_kernel).
 template <int NV>
 __global__ void __launch_bounds__(256) attn_group_reg_kernel(AttnArgs a) {
+  pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
   const int s = blockIdx.x, patch = blockIdx.y;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (h >= a.H) return;
@@ -1005,10 +1086,27 @@ __global__ void dec_head_kernel(const float *dec, const float *loc, const float 
 
 // ============================================================== launchers
 cudaError_t t0b_launch_prep(const PrepArgs &a, cudaStream_t st) {
-  prep_kernel<<<(a.R + 127) / 128, 128, 0, st>>>(a);
+  prep_kernel<<<(a.R + kPrepWarps - 1) / kPrepWarps, 32 * kPrepWarps, 0, st>>>(a);
   return cudaGetLastError();
 }
+template <int MT>
+static cudaError_t launch_sgemm_small(const SgemmArgs &a, cudaStream_t st) {
+  const size_t smem = std::max((size_t)(MT + 32) * (a.K + 4), (size_t)kSgemmSmallWarps * MT * 32) * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(sgemm_small_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((a.N + 31) / 32, (a.M + MT - 1) / MT);
+  sgemm_small_kernel<MT><<<grid, 32 * kSgemmSmallWarps, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
 cudaError_t t0b_launch_sgemm(const SgemmArgs &a, cudaStream_t st) {
+  // few rows: the staged small-M kernel (whole K in shared memory)
+  const bool aligned = ((uintptr_t)a.A % 16 == 0) && ((uintptr_t)a.B % 16 == 0) && a.lda % 4 == 0 && a.ldb % 4 == 0;
+  if (a.M > 0 && a.M <= 64 && a.K % 32 == 0 && (size_t)64 * (a.K + 4) * sizeof(float) <= 200 * 1024 && aligned) {
+    if (a.M <= 8) return launch_sgemm_small<8>(a, st);
+    if (a.M <= 16) return launch_sgemm_small<16>(a, st);
+    return launch_sgemm_small<32>(a, st);
+  }
   dim3 grid((a.N + 63) / 64, (a.M + 63) / 64);
   sgemm_nt_kernel<<<grid, 256, 0, st>>>(a);
   return cudaGetLastError();

@@ -50,13 +50,10 @@ struct AttnArgs {
   int max_nrows;  // largest series_nrows entry (host-side bound for the group kernel)
 };
 
-// Small-M dequant GEMM (k_gemm_small.cu).  part/cnt: split-K workspace sized
-// by t0b_small_workspace (counters zero before the first launch, left at zero
-// by every launch), or NULL to run without splitting K.
+// Small-M dequant GEMM (k_gemm_small.cu): thread-block clusters along K,
+// launched as a programmatic dependent of the previous kernel on `st`.
 cudaError_t t0b_launch_gemm_small(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W,
-                                  const Epi &epi, int *err, cudaStream_t st, float *part = nullptr,
-                                  int *cnt = nullptr);
-void t0b_small_workspace(int M, int K, const Epi &epi, size_t *part_floats, size_t *cnt_ints);
+                                  const Epi &epi, int *err, cudaStream_t st);
 cudaError_t t0b_launch_gemm_tc(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
                                int wshift, const Epi &epi, int *err, cudaStream_t st);
 cudaError_t t0b_launch_absmax_scale(const uint8_t *W, size_t nblocks, int bpb, unsigned int *out, cudaStream_t st);

@@ -84,26 +84,12 @@ struct LayerW {
   bool group;
 };
 
-// Grows the small-M GEMM's split-K workspace to at least (part_floats,
-// cnt_ints); newly allocated counters are zeroed on `st` (the kernels leave
-// them at zero).  Only call it while no kernel of `st` uses the buffers.
-cudaError_t reserve_small_ws(DBuf &part, DBuf &cnt, size_t part_floats, size_t cnt_ints, cudaStream_t st) {
-  cudaError_t e = part.reserve(part_floats * 4);
-  if (e != cudaSuccess) return e;
-  if (cnt_ints * 4 > cnt.bytes) {
-    if ((e = cnt.reserve(cnt_ints * 4)) != cudaSuccess) return e;
-    return cudaMemsetAsync(cnt.p, 0, cnt.bytes, st);
-  }
-  return cudaSuccess;
-}
-
 }  // namespace
 
 struct t0b_engine {
   int device = 0;
   int *d_err = nullptr;
   DBuf scratch_xh, scratch_xl, scratch_zh, scratch_zl, scratch_red;
-  DBuf small_part, small_cnt;  // split-K workspace of the small-M GEMM
 };
 
 struct t0b_model {
@@ -124,7 +110,6 @@ struct t0b_model {
   // workspace
   DBuf x, qkv, feat, ssq, xo, dhid, dout, loc, scl;
   DBuf xh, xl, ah, al, hh, hl;
-  DBuf small_part, small_cnt;  // split-K workspace of the small-M GEMM
   DBuf meta;  // row/series metadata
   HBuf hmeta;
   DBuf ctx_stage, out_stage;
@@ -525,13 +510,8 @@ cudaError_t qgemm(t0b_model *m, const __half *ah, const __half *al, int M, int K
     });
   }
   if (epi.kind == EPI_RESID) epi.ssq_out_nt = epi.N / 32;
-  size_t pf = 0, ci = 0;
-  t0b_small_workspace(M, K, epi, &pf, &ci);
-  const bool split = pf && m->small_part.bytes >= pf * 4 && m->small_cnt.bytes >= ci * 4;
-  float *part = split ? m->small_part.as<float>() : nullptr;
-  int *cnt = split ? m->small_cnt.as<int>() : nullptr;
   return launch(m, KC_GEMM_SMALL, flops, bytes, [&] {
-    return t0b_launch_gemm_small(m->qt, ah, al, M, K, W, epi, m->d_err, m->stream, part, cnt);
+    return t0b_launch_gemm_small(m->qt, ah, al, M, K, W, epi, m->d_err, m->stream);
   });
 }
 
@@ -575,22 +555,6 @@ t0b_status ensure_ws(t0b_model *m, size_t T, size_t R, size_t nout) {
   CUDA_TRY(m->qkv.reserve(T * 3 * E * 4));
   CUDA_TRY(m->feat.reserve(T * 96 * 4));
   CUDA_TRY(m->ssq.reserve(T * std::max<size_t>(16, E / 32) * 4));
-  if ((int)T < m->tc_min_tokens) {  // small-M GEMMs: split-K workspace for the layer's four shapes
-    size_t pf = 0, ci = 0;
-    Epi sh[4]{};
-    sh[0].kind = EPI_PLAIN, sh[0].N = 3 * (int)E;
-    sh[1].kind = EPI_RESID, sh[1].N = (int)E;
-    sh[2].kind = EPI_SWIGLU, sh[2].N = 2 * (int)F, sh[2].F = (int)F;
-    sh[3].kind = EPI_RESID, sh[3].N = (int)E;
-    const int Ks[4] = {(int)E, (int)E, (int)E, (int)F};
-    for (int i = 0; i < 4; ++i) {
-      size_t a = 0, b = 0;
-      t0b_small_workspace((int)T, Ks[i], sh[i], &a, &b);
-      pf = std::max(pf, a);
-      ci = std::max(ci, b);
-    }
-    if (pf) CUDA_TRY(reserve_small_ws(m->small_part, m->small_cnt, pf, ci, m->stream));
-  }
   CUDA_TRY(m->xh.reserve(T * E * 2));
   CUDA_TRY(m->xl.reserve(T * E * 2));
   CUDA_TRY(m->ah.reserve(T * E * 2));
@@ -657,7 +621,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
            // the group-attention kernel variant depends on the largest series
            (uint64_t)(ps.s_nrows.empty() ? 0 : *std::max_element(ps.s_nrows.begin(), ps.s_nrows.end()))};
     for (const DBuf *b : {&m->x, &m->qkv, &m->feat, &m->ssq, &m->xo, &m->dhid, &m->dout, &m->loc, &m->scl, &m->xh,
-                          &m->xl, &m->ah, &m->al, &m->hh, &m->hl, &m->small_part, &m->small_cnt, &m->meta})
+                          &m->xl, &m->ah, &m->al, &m->hh, &m->hl, &m->meta})
       key.push_back((uint64_t)(uintptr_t)b->p);
     auto it = m->graphs.find(key);
     if (it != m->graphs.end()) {
@@ -1159,18 +1123,7 @@ cudaError_t engine_qgemm(t0b_engine *e, int qt, const __half *ah, const __half *
                          int wrows, int wshift, Epi &epi, int *err, cudaStream_t st) {
   const bool tc = M >= 128;
   if (tc) return t0b_launch_gemm_tc(qt, ah, al, M, K, W, wrows, wshift, epi, err, st);
-  size_t pf = 0, ci = 0;
-  t0b_small_workspace(M, K, epi, &pf, &ci);
-  if (!pf) return t0b_launch_gemm_small(qt, ah, al, M, K, W, epi, err, st);
-  // a launch earlier in the same call may still use the workspace: let it
-  // finish before the workspace grows
-  if (pf * 4 > e->small_part.bytes || ci * 4 > e->small_cnt.bytes) {
-    cudaError_t w = cudaStreamSynchronize(st);
-    if (w != cudaSuccess) return w;
-  }
-  cudaError_t r = reserve_small_ws(e->small_part, e->small_cnt, pf, ci, st);
-  if (r != cudaSuccess) return r;
-  return t0b_launch_gemm_small(qt, ah, al, M, K, W, epi, err, st, e->small_part.as<float>(), e->small_cnt.as<int>());
+  return t0b_launch_gemm_small(qt, ah, al, M, K, W, epi, err, st);
 }
 
 t0b_status engine_check(t0b_engine *e, cudaStream_t st) {
