@@ -153,6 +153,32 @@ t0b_status t0b_swiglu_q(t0b_engine *e, int ggml_type, const void *w0_dev, const 
                         int N2, const float *x_dev, int M, const float *b0_dev, const float *b2_dev,
                         float *z_dev, float *y_dev, void *stream);
 
+/* ---- resident-weight dequant-GEMMs (asynchronous) ----
+ * The same GEMMs as t0b_gemm_q / t0b_swiglu_q on a weight matrix that stays
+ * resident, the way t0-fast's GpuModel keeps its quantized buffers
+ * (model.rs:302-348) and runs linear() on them (model.rs:406-504).
+ * t0b_qmatrix_create reads the matrix once (synchronously) for its
+ * tensor-core prescale; the matrix must stay valid and unchanged while the
+ * handle lives.  t0b_qmatrix_gemm and t0b_qmatrix_swiglu only queue work on
+ * `stream` (no host synchronisation, so they can be captured in a CUDA graph)
+ * except when the handle's activation scratch has to grow, which first waits
+ * for `stream`.  Kernel-side errors are reported by t0b_qmatrix_sync.  The
+ * handles of one engine share the engine's activation scratch (as
+ * t0b_gemm_q does): their launches must not overlap on different streams,
+ * and a handle is not thread-safe. */
+typedef struct t0b_qmatrix t0b_qmatrix;
+t0b_status t0b_qmatrix_create(t0b_engine *e, int ggml_type, const void *w_dev, int N, int K, t0b_qmatrix **out);
+void t0b_qmatrix_destroy(t0b_qmatrix *q);
+/* y[M, N] = x[M, K] . deq(W)^T (+ bias[N]) */
+t0b_status t0b_qmatrix_gemm(t0b_qmatrix *q, const float *x_dev, int M, const float *bias_dev, float *y_dev,
+                            void *stream);
+/* q0 = w0 [2F, K] (gate rows, then up rows), q2 = w2 [N2, F]; same outputs as
+ * t0b_swiglu_q.  Errors are reported by both handles. */
+t0b_status t0b_qmatrix_swiglu(t0b_qmatrix *q0, t0b_qmatrix *q2, const float *x_dev, int M, const float *b0_dev,
+                              const float *b2_dev, float *z_dev, float *y_dev, void *stream);
+/* Wait for `stream` and report any kernel-side error of q's launches. */
+t0b_status t0b_qmatrix_sync(t0b_qmatrix *q, void *stream);
+
 /* ---- no-allocation dequant-GEMM (no reference counterpart) ----
  * The product of t0b_gemm_q, same arguments minus the engine, computed on
  * the calling thread's current device without allocating any device memory:

@@ -19,7 +19,9 @@ EXPORTED = [
     "t0b_last_error", "t0b_engine_create", "t0b_engine_destroy", "t0b_model_load_gguf", "t0b_model_destroy",
     "t0b_model_info_get", "t0b_model_set_stream", "t0b_model_stream", "t0b_model_set_max_tokens", "t0b_model_use_graphs",
     "t0b_forecast", "t0b_forecast_batch", "t0b_forecast_batch_rows", "t0b_forecast_multiseries",
-    "t0b_forecast_multiseries_device", "t0b_model_sync", "t0b_gemm_q", "t0b_swiglu_q", "t0b_gemm_q_noalloc", "t0b_gguf_validate",
+    "t0b_forecast_multiseries_device", "t0b_model_sync", "t0b_gemm_q", "t0b_swiglu_q", "t0b_gemm_q_noalloc",
+    "t0b_qmatrix_create", "t0b_qmatrix_destroy", "t0b_qmatrix_gemm", "t0b_qmatrix_swiglu", "t0b_qmatrix_sync",
+    "t0b_gguf_validate",
     "t0b_quantize", "t0b_dequantize", "t0b_row_bytes", "t0b_export_gguf", "t0b_model_profile_enable",
     "t0b_model_profile_read", "t0b_model_launch_count",
 ]
@@ -78,6 +80,12 @@ def lib() -> C.CDLL:
     L.t0b_model_sync.argtypes = [vp]
     L.t0b_gemm_q.argtypes = [vp, st, vp, st, st, vp, st, vp, vp, vp]
     L.t0b_swiglu_q.argtypes = [vp, st, vp, vp, st, st, st, vp, st, vp, vp, vp, vp, vp]
+    L.t0b_qmatrix_create.argtypes = [vp, st, vp, st, st, C.POINTER(vp)]
+    L.t0b_qmatrix_destroy.argtypes = [vp]
+    L.t0b_qmatrix_destroy.restype = None
+    L.t0b_qmatrix_gemm.argtypes = [vp, vp, st, vp, vp, vp]
+    L.t0b_qmatrix_swiglu.argtypes = [vp, vp, vp, st, vp, vp, vp, vp, vp]
+    L.t0b_qmatrix_sync.argtypes = [vp, vp]
     L.t0b_gemm_q_noalloc.argtypes = [st, vp, st, st, vp, st, vp, vp, vp]
     L.t0b_gguf_validate.argtypes = [vp, sz, C.POINTER(ModelInfo)]
     L.t0b_quantize.argtypes = [st, vp, sz, vp]

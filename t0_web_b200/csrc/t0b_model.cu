@@ -1096,9 +1096,19 @@ extern "C" t0b_status t0b_forecast_batch_rows(t0b_model *m, const float *ctx, co
 
 // ======================================================= standalone GEMMs
 namespace {
+// Grows engine scratch; growing waits for the stream first, since work
+// already queued may still read the old buffers.
+t0b_status qm_reserve(DBuf &b, size_t bytes, cudaStream_t st) {
+  if (bytes <= b.bytes) return T0B_OK;
+  CUDA_TRY(cudaStreamSynchronize(st));
+  CUDA_TRY(b.reserve(bytes));
+  return T0B_OK;
+}
+
 t0b_status split_input(t0b_engine *e, const float *x, size_t n, cudaStream_t st) {
-  CUDA_TRY(e->scratch_xh.reserve(n * 2));
-  CUDA_TRY(e->scratch_xl.reserve(n * 2));
+  t0b_status s;
+  if ((s = qm_reserve(e->scratch_xh, n * 2, st)) != T0B_OK || (s = qm_reserve(e->scratch_xl, n * 2, st)) != T0B_OK)
+    return s;
   CUDA_TRY(t0b_launch_split_f32(x, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), n, st));
   return T0B_OK;
 }
@@ -1150,8 +1160,9 @@ extern "C" t0b_status t0b_gemm_q(t0b_engine *e, int ggml_type, const void *w_dev
   cudaStream_t st = (cudaStream_t)stream;
   t0b_status s = split_input(e, x_dev, (size_t)M * K, st);
   if (s != T0B_OK) return s;
-  int sh = 0;
-  if ((s = device_weight_shift(e, qt, (const uint8_t *)w_dev, (size_t)N * K, st, &sh)) != T0B_OK) return s;
+  int sh = 0;  // tensor-core prescale; the small-M kernel applies block scales in f32 and needs none
+  if (M >= 128 && (s = device_weight_shift(e, qt, (const uint8_t *)w_dev, (size_t)N * K, st, &sh)) != T0B_OK)
+    return s;
   Epi ep{};
   ep.kind = EPI_PLAIN;
   ep.M = M;
@@ -1178,10 +1189,13 @@ extern "C" t0b_status t0b_swiglu_q(t0b_engine *e, int ggml_type, const void *w0_
   t0b_status s = split_input(e, x_dev, (size_t)M * K, st);
   if (s != T0B_OK) return s;
   int sh0 = 0, sh2 = 0;
-  if ((s = device_weight_shift(e, qt, (const uint8_t *)w0_dev, (size_t)2 * F * K, st, &sh0)) != T0B_OK) return s;
-  if ((s = device_weight_shift(e, qt, (const uint8_t *)w2_dev, (size_t)N2 * F, st, &sh2)) != T0B_OK) return s;
-  CUDA_TRY(e->scratch_zh.reserve((size_t)M * F * 2));
-  CUDA_TRY(e->scratch_zl.reserve((size_t)M * F * 2));
+  if (M >= 128) {
+    if ((s = device_weight_shift(e, qt, (const uint8_t *)w0_dev, (size_t)2 * F * K, st, &sh0)) != T0B_OK) return s;
+    if ((s = device_weight_shift(e, qt, (const uint8_t *)w2_dev, (size_t)N2 * F, st, &sh2)) != T0B_OK) return s;
+  }
+  if ((s = qm_reserve(e->scratch_zh, (size_t)M * F * 2, st)) != T0B_OK ||
+      (s = qm_reserve(e->scratch_zl, (size_t)M * F * 2, st)) != T0B_OK)
+    return s;
   Epi sg{};
   sg.kind = EPI_SWIGLU;
   sg.M = M;
@@ -1203,6 +1217,129 @@ extern "C" t0b_status t0b_swiglu_q(t0b_engine *e, int ggml_type, const void *w0_
   CUDA_TRY(engine_qgemm(e, qt, e->scratch_zh.as<__half>(), e->scratch_zl.as<__half>(), M, F, (const uint8_t *)w2_dev, N2,
                         sh2, dn, e->d_err, st));
   return engine_check(e, st);
+}
+
+// ================================================ resident-weight GEMMs
+// A t0b_qmatrix keeps a device weight matrix's tensor-core prescale (found
+// once, at creation) and its own error word; the activation scratch is the
+// engine's.  Its GEMMs are pure stream work: no host synchronisation, and
+// capturable in a CUDA graph once the scratch has reached its size.
+struct t0b_qmatrix {
+  t0b_engine *eng = nullptr;
+  int qt = 0, N = 0, K = 0, shift = 0;
+  const uint8_t *W = nullptr;
+  int *d_err = nullptr;
+  ~t0b_qmatrix() {
+    if (d_err) cudaFree(d_err);
+  }
+};
+
+
+extern "C" t0b_status t0b_qmatrix_create(t0b_engine *e, int ggml_type, const void *w_dev, int N, int K,
+                                         t0b_qmatrix **out) {
+  if (!e || !w_dev || !out) return fail(T0B_ERR_INVALID, "t0b_qmatrix_create: NULL argument");
+  const int qt = qt_of(ggml_type);
+  if (!qt) return fail(T0B_ERR_UNSUPPORTED, "t0b_qmatrix_create: weight type must be Q8_0 or Q4_0");
+  if (N < 1 || K < 1) return fail(T0B_ERR_INVALID, "t0b_qmatrix_create: empty shape");
+  if (K % 256 || N % 256) return fail(T0B_ERR_UNSUPPORTED, "t0b_qmatrix_create: N and K must be multiples of 256");
+  CUDA_TRY(cudaSetDevice(e->device));
+  auto q = std::make_unique<t0b_qmatrix>();
+  q->eng = e;
+  q->qt = qt;
+  q->N = N;
+  q->K = K;
+  q->W = (const uint8_t *)w_dev;
+  if (cudaMalloc(&q->d_err, sizeof(int)) != cudaSuccess) return fail(T0B_ERR_OOM, "t0b: out of device memory");
+  CUDA_TRY(cudaMemset(q->d_err, 0, sizeof(int)));
+  t0b_status s = device_weight_shift(e, qt, q->W, (size_t)N * K, nullptr, &q->shift);
+  if (s != T0B_OK) return s;
+  *out = q.release();
+  return T0B_OK;
+}
+
+extern "C" void t0b_qmatrix_destroy(t0b_qmatrix *q) {
+  if (!q) return;
+  cudaSetDevice(q->eng->device);
+  delete q;
+}
+
+extern "C" t0b_status t0b_qmatrix_gemm(t0b_qmatrix *q, const float *x_dev, int M, const float *bias_dev, float *y_dev,
+                                       void *stream) {
+  if (!q || !x_dev || !y_dev) return fail(T0B_ERR_INVALID, "t0b_qmatrix_gemm: NULL argument");
+  if (M < 1) return fail(T0B_ERR_INVALID, "t0b_qmatrix_gemm: empty shape");
+  CUDA_TRY(cudaSetDevice(q->eng->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t n = (size_t)M * q->K;
+  t0b_status s;
+  t0b_engine *e = q->eng;
+  if ((s = qm_reserve(e->scratch_xh, n * 2, st)) != T0B_OK || (s = qm_reserve(e->scratch_xl, n * 2, st)) != T0B_OK)
+    return s;
+  CUDA_TRY(t0b_launch_split_f32(x_dev, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), n, st));
+  Epi ep{};
+  ep.kind = EPI_PLAIN;
+  ep.M = M;
+  ep.N = q->N;
+  ep.bias = bias_dev;
+  ep.y = y_dev;
+  ep.ldy = q->N;
+  CUDA_TRY(engine_qgemm(e, q->qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, q->K, q->W, q->N,
+                        q->shift, ep, q->d_err, st));
+  return T0B_OK;
+}
+
+extern "C" t0b_status t0b_qmatrix_swiglu(t0b_qmatrix *q0, t0b_qmatrix *q2, const float *x_dev, int M,
+                                         const float *b0_dev, const float *b2_dev, float *z_dev, float *y_dev,
+                                         void *stream) {
+  if (!q0 || !q2 || !x_dev || !y_dev) return fail(T0B_ERR_INVALID, "t0b_qmatrix_swiglu: NULL argument");
+  if (M < 1) return fail(T0B_ERR_INVALID, "t0b_qmatrix_swiglu: empty shape");
+  if (q0->N % 2 || q2->K != q0->N / 2 || q0->qt != q2->qt || q0->eng != q2->eng)
+    return fail(T0B_ERR_INVALID, "t0b_qmatrix_swiglu: need w0 [2F, K] and w2 [N2, F] of one type and engine");
+  const int F = q0->N / 2, K = q0->K;
+  if (F % 256) return fail(T0B_ERR_UNSUPPORTED, "t0b_qmatrix_swiglu: F must be a multiple of 256");
+  CUDA_TRY(cudaSetDevice(q0->eng->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t n = (size_t)M * K;
+  t0b_status s;
+  t0b_engine *e = q0->eng;
+  if ((s = qm_reserve(e->scratch_xh, n * 2, st)) != T0B_OK || (s = qm_reserve(e->scratch_xl, n * 2, st)) != T0B_OK ||
+      (s = qm_reserve(e->scratch_zh, (size_t)M * F * 2, st)) != T0B_OK ||
+      (s = qm_reserve(e->scratch_zl, (size_t)M * F * 2, st)) != T0B_OK)
+    return s;
+  CUDA_TRY(t0b_launch_split_f32(x_dev, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), n, st));
+  Epi sg{};
+  sg.kind = EPI_SWIGLU;
+  sg.M = M;
+  sg.N = 2 * F;
+  sg.F = F;
+  sg.bias = b0_dev;
+  sg.zh = e->scratch_zh.as<__half>();
+  sg.zl = e->scratch_zl.as<__half>();
+  sg.z32 = z_dev;
+  CUDA_TRY(engine_qgemm(e, q0->qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, q0->W, 2 * F,
+                        q0->shift, sg, q0->d_err, st));
+  Epi dn{};
+  dn.kind = EPI_PLAIN;
+  dn.M = M;
+  dn.N = q2->N;
+  dn.bias = b2_dev;
+  dn.y = y_dev;
+  dn.ldy = q2->N;
+  CUDA_TRY(engine_qgemm(e, q2->qt, e->scratch_zh.as<__half>(), e->scratch_zl.as<__half>(), M, F, q2->W, q2->N,
+                        q2->shift, dn, q2->d_err, st));
+  return T0B_OK;
+}
+
+extern "C" t0b_status t0b_qmatrix_sync(t0b_qmatrix *q, void *stream) {
+  if (!q) return fail(T0B_ERR_INVALID, "t0b_qmatrix_sync: NULL argument");
+  CUDA_TRY(cudaSetDevice(q->eng->device));
+  CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
+  int herr = 0;
+  CUDA_TRY(cudaMemcpy(&herr, q->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (herr) {
+    cudaMemset(q->d_err, 0, sizeof(int));
+    return fail(T0B_ERR_DEVICE, "t0b_qmatrix: a kernel reported device error code " + std::to_string(herr));
+  }
+  return T0B_OK;
 }
 
 // ================================================ no-allocation standalone GEMM
