@@ -33,6 +33,7 @@
 
 #include "common.cuh"
 #include "epilogue.cuh"
+#include "t0b_internal.h"
 
 namespace cg = cooperative_groups;
 
@@ -340,7 +341,7 @@ cudaError_t launch_small_t(const __half *ah, const __half *al, int M, int K, int
   const int cs = K / KS;
   const SmallLayout L = small_layout(QT, KS, MT, cs, epi.ssq_in ? epi.ssq_in_nt : 0);
   auto kfn = gemm_q_small_kernel<QT, NT8>;
-  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.bytes);
+  cudaError_t e = t0b_smem_limit((const void *)kfn, L.bytes);
   if (e != cudaSuccess) return e;
   const int gx = epi.kind == EPI_SWIGLU ? epi.F / 16 : epi.N / kRows;
   cudaLaunchConfig_t cfg{};

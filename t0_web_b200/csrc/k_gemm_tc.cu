@@ -40,6 +40,7 @@
 
 #include "common.cuh"
 #include "epilogue.cuh"
+#include "t0b_internal.h"
 
 namespace {
 
@@ -569,7 +570,7 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
   prm.epi = epi;
   prm.err = err;
   auto kfn = gemm_q_tc_kernel<QT>;
-  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+  cudaError_t e = t0b_smem_limit((const void *)kfn, C::SMEM);
   if (e != cudaSuccess) return e;
   const int grid = prm.n_tiles < sm_count() ? prm.n_tiles : sm_count();  // persistent: one CTA per SM
   kfn<<<grid, NTHREADS, C::SMEM, st>>>(txh, txl, tw, ty, tzh, tzl, prm);

@@ -1092,7 +1092,7 @@ cudaError_t t0b_launch_prep(const PrepArgs &a, cudaStream_t st) {
 template <int MT>
 static cudaError_t launch_sgemm_small(const SgemmArgs &a, cudaStream_t st) {
   const size_t smem = std::max((size_t)(MT + 32) * (a.K + 4), (size_t)kSgemmSmallWarps * MT * 32) * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(sgemm_small_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = t0b_smem_limit((const void *)sgemm_small_kernel<MT>, smem);
   if (e != cudaSuccess) return e;
   dim3 grid((a.N + 31) / 32, (a.M + MT - 1) / MT);
   sgemm_small_kernel<MT><<<grid, 32 * kSgemmSmallWarps, smem, st>>>(a);
@@ -1126,7 +1126,7 @@ cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
   if (a.p <= kAttnMmaMaxP) {
     const int QB = (a.p + 15) / 16, PK = 16 * QB;
     const size_t smem = (size_t)(4 * PK * 72) * sizeof(__half);
-    cudaError_t e = cudaFuncSetAttribute(attn_time_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = t0b_smem_limit((const void *)attn_time_mma_kernel, smem);
     if (e != cudaSuccess) return e;
     attn_time_mma_kernel<<<dim3(a.R, a.H), 32 * QB, smem, st>>>(a);
     return cudaGetLastError();
@@ -1135,13 +1135,13 @@ cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
     const int PP = (a.p + 3) & ~3;
     const size_t smem = (size_t)(PP * 64 * 3 + PP * PP) * sizeof(float);
     cudaError_t e =
-        cudaFuncSetAttribute(attn_time_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        t0b_smem_limit((const void *)attn_time_tiled_kernel, smem);
     if (e != cudaSuccess) return e;
     attn_time_tiled_kernel<<<dim3(a.R, a.H), 128, smem, st>>>(a);
     return cudaGetLastError();
   }
   size_t smem = (size_t)(a.p * (65 + 64 + 64) + 4 * a.p) * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(attn_time_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = t0b_smem_limit((const void *)attn_time_kernel, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.R, a.H);
   attn_time_kernel<<<grid, 128, smem, st>>>(a);

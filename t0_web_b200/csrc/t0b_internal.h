@@ -8,6 +8,11 @@
 
 #include "epilogue.cuh"
 
+// Raises the kernel's dynamic shared memory limit on the current device to at
+// least `bytes`, never lowering it: a CUDA graph captured with a larger launch
+// must stay launchable after smaller launches of the same kernel.
+cudaError_t t0b_smem_limit(const void *kernel, size_t bytes);
+
 struct PrepArgs {
   const float *ctx;      // raw context values (NaN = missing)
   const int64_t *row_off;  // start of row r's values in ctx

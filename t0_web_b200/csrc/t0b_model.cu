@@ -133,6 +133,7 @@ struct t0b_model {
   };
   std::map<std::vector<uint64_t>, GraphEntry> graphs;
   uint64_t graph_clock = 0;
+  std::vector<uint64_t> graph_sig;  // workspace allocations the cached graphs were captured against
   void drop_graphs() {
     for (auto &kv : graphs) cudaGraphExecDestroy(kv.second.exec);
     graphs.clear();
@@ -615,6 +616,18 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   const bool graph = m->use_graphs && !m->prof && m->stream != nullptr;
   std::vector<uint64_t> key;
   if (graph) {
+    // a workspace buffer that was reallocated invalidates every cached graph
+    // (a graph may hold its old allocation, even at an address reused since)
+    std::vector<uint64_t> sig{(uint64_t)(uintptr_t)m->hmeta.p, (uint64_t)m->hmeta.bytes};
+    for (const DBuf *b : {&m->x, &m->qkv, &m->feat, &m->ssq, &m->xo, &m->dhid, &m->dout, &m->loc, &m->scl, &m->xh,
+                          &m->xl, &m->ah, &m->al, &m->hh, &m->hl, &m->meta, &m->ctx_stage, &m->out_stage}) {
+      sig.push_back((uint64_t)(uintptr_t)b->p);
+      sig.push_back((uint64_t)b->bytes);
+    }
+    if (sig != m->graph_sig) {
+      m->drop_graphs();
+      m->graph_sig = std::move(sig);
+    }
     key = {(uint64_t)R, (uint64_t)p, (uint64_t)hp, (uint64_t)ns, (uint64_t)ps.horizon, (uint64_t)o,
            (uint64_t)(uintptr_t)ps.ctx, (uint64_t)(uintptr_t)ps.out, (uint64_t)(uintptr_t)hb,
            (uint64_t)(uintptr_t)rope, (uint64_t)m->tc_min_tokens,
@@ -1092,6 +1105,20 @@ extern "C" t0b_status t0b_forecast_batch_rows(t0b_model *m, const float *ctx, co
       return s;
   }
   return finish_io(m, sg, out, n * horizon * m->nq);
+}
+
+cudaError_t t0b_smem_limit(const void *kernel, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void *, int>, size_t> limit;  // (kernel, device) -> bytes set
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  size_t &cur = limit[{kernel, dev}];
+  if (bytes <= cur) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) cur = bytes;
+  return e;
 }
 
 // ======================================================= standalone GEMMs
