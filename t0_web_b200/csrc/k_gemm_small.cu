@@ -24,8 +24,8 @@
 //     next norm's gain with the weights; the residual rows and the RMSNorm
 //     partial sums with the activations), so the epilogue reads only shared
 //     memory;
-//   * the four warps split the slice's blocks and add their partial tiles
-//     through shared memory; every CTA of a cluster then pushes its tile into
+//   * 16 warps: 8 groups split the slice's blocks, each with one warp per
+//     16-row tile; the groups' partial tiles are added through shared memory; every CTA of a cluster then pushes its tile into
 //     a slot of the first CTA's shared memory (distributed shared memory),
 //     which adds the slots in slice order (deterministic) and runs the fused
 //     epilogue, one warp per token row and one lane per output column.
@@ -39,8 +39,9 @@ namespace cg = cooperative_groups;
 
 namespace {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
+constexpr int kKGroups = 8;  // warps split a slice's blocks 8 ways and its 32 rows into 2 tiles of 16
 constexpr int kRows = 32;        // weight rows (output columns) per CTA
 constexpr int kMaxCluster = 8;   // K slices per row group (portable cluster size)
 constexpr size_t kSmemCap = 200 * 1024;
@@ -61,8 +62,8 @@ struct SmallLayout {
 };
 
 // Shared memory of one CTA: raw weights [32][KS/32 blocks], activations
-// [2 planes][MT tokens][KS (+8 pad) halves], per-warp partial tiles
-// [4][32][MT] f32, cluster slots [cs][32][MT+1] f32 (slot z: the tile of K
+// [2 planes][MT tokens][KS (+8 pad) halves], per-K-group partial tiles
+// [8][32][MT] f32, cluster slots [cs][32][MT+1] f32 (slot z: the tile of K
 // slice z; only the first CTA's slots are used), then the epilogue operands:
 // bias [32], next-norm gain [32], residual rows [MT][32], RMSNorm partial
 // sums [MT][nt].
@@ -73,7 +74,7 @@ __host__ __device__ inline SmallLayout small_layout(int qt, int KS, int MT, int 
   L.w_off = 0;
   L.a_off = L.w_off + kRows * L.wpitch;
   L.red_off = L.a_off + 2 * (size_t)MT * L.apitch;
-  L.slot_off = L.red_off + (size_t)kWarps * kRows * MT * 4;
+  L.slot_off = L.red_off + (size_t)kKGroups * kRows * MT * 4;
   L.eb_off = L.slot_off + (size_t)cs * kRows * (MT + 1) * 4;
   L.eg_off = L.eb_off + kRows * 4;
   L.ex_off = L.eg_off + kRows * 4;
@@ -181,44 +182,39 @@ __global__ void __launch_bounds__(kThreads) gemm_q_small_kernel(const __half *__
     e_ssq[threadIdx.x * nt] = sqrtf(s / (float)epi.ssq_dim + 1e-8f);
   }
 
-  // 3. this warp's blocks of the slice
-  float acc[2][NT8][4];
+  // 3. warp (kg, rt): row tile rt (16 rows) over K group kg's blocks of the slice
+  const int kg = warp % kKGroups, rt = warp / kKGroups;
+  float acc[NT8][4];
 #pragma unroll
-  for (int rt = 0; rt < 2; ++rt)
-#pragma unroll
-    for (int j = 0; j < NT8; ++j) acc[rt][j][0] = acc[rt][j][1] = acc[rt][j][2] = acc[rt][j][3] = 0.0f;
-  const int bpw = KB / kWarps;  // KB is a multiple of 8
+  for (int j = 0; j < NT8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+  const int bpw = KB / kKGroups;  // KB is a multiple of 8
   for (int bi = 0; bi < bpw; ++bi) {
-    const int b = warp * bpw + bi;
-    uint32_t a[2][2][4];
-    float d0[2], d1[2];
+    const int b = kg * bpw + bi;
+    uint32_t a[2][4];
+    const uint8_t *r0 = wst + (size_t)(rt * 16 + g) * L.wpitch + b * BPB;
+    const uint8_t *r1 = r0 + 8 * L.wpitch;
+    const float d0 = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(r0));
+    const float d1 = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(r1));
+    if (QT == 8) {
 #pragma unroll
-    for (int rt = 0; rt < 2; ++rt) {
-      const uint8_t *r0 = wst + (size_t)(rt * 16 + g) * L.wpitch + b * BPB;
-      const uint8_t *r1 = r0 + 8 * L.wpitch;
-      d0[rt] = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(r0));
-      d1[rt] = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(r1));
-      if (QT == 8) {
+      for (int h = 0; h < 2; ++h) {
+        a[h][0] = i8x2_to_h2(*reinterpret_cast<const uint16_t *>(r0 + 2 + 16 * h + 2 * tig));
+        a[h][1] = i8x2_to_h2(*reinterpret_cast<const uint16_t *>(r1 + 2 + 16 * h + 2 * tig));
+        a[h][2] = i8x2_to_h2(*reinterpret_cast<const uint16_t *>(r0 + 2 + 16 * h + 8 + 2 * tig));
+        a[h][3] = i8x2_to_h2(*reinterpret_cast<const uint16_t *>(r1 + 2 + 16 * h + 8 + 2 * tig));
+      }
+    } else {
+      // byte j of a Q4_0 block holds value j (low nibble) and j + 16 (high)
+      const uint32_t w00 = *reinterpret_cast<const uint16_t *>(r0 + 2 + 2 * tig);
+      const uint32_t w10 = *reinterpret_cast<const uint16_t *>(r1 + 2 + 2 * tig);
+      const uint32_t w01 = *reinterpret_cast<const uint16_t *>(r0 + 2 + 8 + 2 * tig);
+      const uint32_t w11 = *reinterpret_cast<const uint16_t *>(r1 + 2 + 8 + 2 * tig);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          a[rt][h][0] = i8x2_to_h2(*reinterpret_cast<const uint16_t *>(r0 + 2 + 16 * h + 2 * tig));
-          a[rt][h][1] = i8x2_to_h2(*reinterpret_cast<const uint16_t *>(r1 + 2 + 16 * h + 2 * tig));
-          a[rt][h][2] = i8x2_to_h2(*reinterpret_cast<const uint16_t *>(r0 + 2 + 16 * h + 8 + 2 * tig));
-          a[rt][h][3] = i8x2_to_h2(*reinterpret_cast<const uint16_t *>(r1 + 2 + 16 * h + 8 + 2 * tig));
-        }
-      } else {
-        // byte j of a Q4_0 block holds value j (low nibble) and j + 16 (high)
-        const uint32_t w00 = *reinterpret_cast<const uint16_t *>(r0 + 2 + 2 * tig);
-        const uint32_t w10 = *reinterpret_cast<const uint16_t *>(r1 + 2 + 2 * tig);
-        const uint32_t w01 = *reinterpret_cast<const uint16_t *>(r0 + 2 + 8 + 2 * tig);
-        const uint32_t w11 = *reinterpret_cast<const uint16_t *>(r1 + 2 + 8 + 2 * tig);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          a[rt][h][0] = nib2_to_h2(w00, h);
-          a[rt][h][1] = nib2_to_h2(w10, h);
-          a[rt][h][2] = nib2_to_h2(w01, h);
-          a[rt][h][3] = nib2_to_h2(w11, h);
-        }
+      for (int h = 0; h < 2; ++h) {
+        a[h][0] = nib2_to_h2(w00, h);
+        a[h][1] = nib2_to_h2(w10, h);
+        a[h][2] = nib2_to_h2(w01, h);
+        a[h][3] = nib2_to_h2(w11, h);
       }
     }
 #pragma unroll
@@ -229,36 +225,31 @@ __global__ void __launch_bounds__(kThreads) gemm_q_small_kernel(const __half *__
       uint32_t bh[4], bl[4];
       ldsm_x4(act + roff, bh[0], bh[1], bh[2], bh[3]);
       ldsm_x4(act + (size_t)MT * L.apitch + roff, bl[0], bl[1], bl[2], bl[3]);
+      float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll
-      for (int rt = 0; rt < 2; ++rt) {
-        float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          mma16816(p0, p1, p2, p3, a[rt][h][0], a[rt][h][1], a[rt][h][2], a[rt][h][3], bh[2 * h], bh[2 * h + 1]);
-          mma16816(p0, p1, p2, p3, a[rt][h][0], a[rt][h][1], a[rt][h][2], a[rt][h][3], bl[2 * h], bl[2 * h + 1]);
-        }
-        acc[rt][j][0] += d0[rt] * p0;
-        acc[rt][j][1] += d0[rt] * p1;
-        acc[rt][j][2] += d1[rt] * p2;
-        acc[rt][j][3] += d1[rt] * p3;
+      for (int h = 0; h < 2; ++h) {
+        mma16816(p0, p1, p2, p3, a[h][0], a[h][1], a[h][2], a[h][3], bh[2 * h], bh[2 * h + 1]);
+        mma16816(p0, p1, p2, p3, a[h][0], a[h][1], a[h][2], a[h][3], bl[2 * h], bl[2 * h + 1]);
       }
+      acc[j][0] += d0 * p0;
+      acc[j][1] += d0 * p1;
+      acc[j][2] += d1 * p2;
+      acc[j][3] += d1 * p3;
     }
   }
 
-  // 4. warps' partial tiles (warp order: deterministic) -> slot z of the
+  // 4. K groups' partial tiles (group order: deterministic) -> slot z of the
   //    first CTA of the cluster
   {
-    float *mine = red + (size_t)warp * kRows * MT;
+    float *mine = red + (size_t)kg * kRows * MT;
 #pragma unroll
-    for (int rt = 0; rt < 2; ++rt)
-#pragma unroll
-      for (int j = 0; j < NT8; ++j) {
-        const int r = rt * 16 + g, t = 8 * j + 2 * tig;
-        mine[r * MT + t] = acc[rt][j][0];
-        mine[r * MT + t + 1] = acc[rt][j][1];
-        mine[(r + 8) * MT + t] = acc[rt][j][2];
-        mine[(r + 8) * MT + t + 1] = acc[rt][j][3];
-      }
+    for (int j = 0; j < NT8; ++j) {
+      const int r = rt * 16 + g, t = 8 * j + 2 * tig;
+      mine[r * MT + t] = acc[j][0];
+      mine[r * MT + t + 1] = acc[j][1];
+      mine[(r + 8) * MT + t] = acc[j][2];
+      mine[(r + 8) * MT + t + 1] = acc[j][3];
+    }
   }
   __syncthreads();
   float *slot = slots + (size_t)z * kRows * LD;
@@ -269,7 +260,7 @@ __global__ void __launch_bounds__(kThreads) gemm_q_small_kernel(const __half *__
   for (int i = threadIdx.x; i < kRows * MT; i += kThreads) {
     float v = red[i];
 #pragma unroll
-    for (int w = 1; w < kWarps; ++w) v += red[(size_t)w * kRows * MT + i];
+    for (int w = 1; w < kKGroups; ++w) v += red[(size_t)w * kRows * MT + i];
     slot[(i / MT) * LD + i % MT] = v;
   }
   if (cs > 1) {
