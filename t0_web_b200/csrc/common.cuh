@@ -289,4 +289,13 @@ T0B_DEV void split_f16(float x, __half &hi, __half &lo) {
   hi = __float2half_rn(x);
   lo = __float2half_rn(x - __half2float(hi));
 }
+// (x0, x1) -> f16x2 hi word and f16x2 lo word (the same values as split_f16
+// element by element, with packed conversions)
+T0B_DEV void split2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const float2 hf = __half22float2(h);
+  const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+  hi = *reinterpret_cast<const uint32_t *>(&h);
+  lo = *reinterpret_cast<const uint32_t *>(&l);
+}
 T0B_DEV float f16_bits_to_f32(uint16_t b) { return __half2float(__ushort_as_half(b)); }

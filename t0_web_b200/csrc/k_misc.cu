@@ -214,6 +214,129 @@ __global__ void __launch_bounds__(32 * kSgemmSmallWarps) sgemm_small_kernel(Sgem
   }
 }
 
+// Many rows, f16-exact weights (the patch encoder / decoder weights are f16
+// on disk): C = A . B^T on the tensor cores as Ah.B + Al.B, A split into two
+// f16 planes as it is read (products exact).  Each 32-wide K step is summed
+// by the MMAs into a fresh partial that is then added to the f32 result
+// (the tensor cores' own accumulation only ever spans 4 MMAs), i.e. the
+// same f32-class arithmetic as the quantized GEMMs.  128 x 64 tile per CTA,
+// 8 warps of 32 x 32, K steps double-buffered with cp.async.
+constexpr int kSgH_BM = 128, kSgH_BN = 64, kSgH_BK = 32;
+constexpr int kSgH_AP = kSgH_BK + 8;  // A row pitch (floats): conflict-free float2 fragment reads
+constexpr int kSgH_BP = kSgH_BK + 8;  // B row pitch (halves): conflict-free ldmatrix rows
+constexpr size_t kSgH_Stage = (size_t)kSgH_BM * kSgH_AP * 4 + (size_t)kSgH_BN * kSgH_BP * 2;
+
+__global__ void __launch_bounds__(256, 2) sgemm_h_kernel(SgemmArgs a) {
+  extern __shared__ __align__(16) uint8_t sgh_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int wm = warp & 3, wn = warp >> 2;  // warp tile rows 32 wm.., cols 32 wn..
+  const int m0 = blockIdx.y * kSgH_BM, n0 = blockIdx.x * kSgH_BN;
+  auto As = [&](int st) { return reinterpret_cast<float *>(sgh_smem + st * kSgH_Stage); };
+  auto Bs = [&](int st) { return reinterpret_cast<__half *>(sgh_smem + st * kSgH_Stage + (size_t)kSgH_BM * kSgH_AP * 4); };
+  auto stage = [&](int st, int k0) {
+    float *as = As(st);
+    __half *bs = Bs(st);
+    // A: 128 rows x 32 floats = 8 granules per row; B: 64 rows x 32 halves = 4 granules per row
+    for (int i = threadIdx.x; i < kSgH_BM * 8; i += 256) {
+      const int r = i >> 3, q = i & 7;
+      const int m = min(m0 + r, a.M - 1);  // rows past M duplicate a valid row; outputs dropped
+      cp_async16(as + r * kSgH_AP + 4 * q, a.A + (size_t)m * a.lda + k0 + 4 * q);
+    }
+    for (int i = threadIdx.x; i < kSgH_BN * 4; i += 256) {
+      const int r = i >> 2, q = i & 3;
+      const int n = min(n0 + r, a.N - 1);
+      cp_async16(bs + r * kSgH_BP + 8 * q, a.B16 + (size_t)n * a.ldb + k0 + 8 * q);
+    }
+    cp_async_commit();
+  };
+  float acc[2][4][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.0f;
+  const int nk = a.K / kSgH_BK;
+  stage(0, 0);
+  for (int kt = 0; kt < nk; ++kt) {
+    if (kt + 1 < nk) {
+      stage((kt + 1) & 1, (kt + 1) * kSgH_BK);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const float *as = As(kt & 1);
+    const __half *bs = Bs(kt & 1);
+    float pp[2][4][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) pp[i][j][0] = pp[i][j][1] = pp[i][j][2] = pp[i][j][3] = 0.0f;
+#pragma unroll
+    for (int kh = 0; kh < 2; ++kh) {  // two k16 steps per stage
+      uint32_t ah[2][4], al[2][4];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const float *r0 = as + (32 * wm + 16 * mt + g) * kSgH_AP + 16 * kh + 2 * t;
+        const float *r1 = r0 + 8 * kSgH_AP;
+        const float2 x0 = *reinterpret_cast<const float2 *>(r0), x1 = *reinterpret_cast<const float2 *>(r1);
+        const float2 x2 = *reinterpret_cast<const float2 *>(r0 + 8), x3 = *reinterpret_cast<const float2 *>(r1 + 8);
+        split2(x0.x, x0.y, ah[mt][0], al[mt][0]);
+        split2(x1.x, x1.y, ah[mt][1], al[mt][1]);
+        split2(x2.x, x2.y, ah[mt][2], al[mt][2]);
+        split2(x3.x, x3.y, ah[mt][3], al[mt][3]);
+      }
+#pragma unroll
+      for (int n2 = 0; n2 < 2; ++n2) {  // n8 tiles 2 n2, 2 n2 + 1
+        // ldmatrix: matrix mi = lane / 8 -> rows (n) (mi / 2) * 8 + lane % 8, k (mi % 2) * 8
+        const __half *br = bs + (32 * wn + 16 * n2 + ((lane >> 4) << 3) + (lane & 7)) * kSgH_BP + 16 * kh +
+                           ((lane >> 3) & 1) * 8;
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4(br, b00, b01, b10, b11);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          float *c0 = pp[mt][2 * n2], *c1 = pp[mt][2 * n2 + 1];
+          mma16816(c0[0], c0[1], c0[2], c0[3], ah[mt][0], ah[mt][1], ah[mt][2], ah[mt][3], b00, b01);
+          mma16816(c0[0], c0[1], c0[2], c0[3], al[mt][0], al[mt][1], al[mt][2], al[mt][3], b00, b01);
+          mma16816(c1[0], c1[1], c1[2], c1[3], ah[mt][0], ah[mt][1], ah[mt][2], ah[mt][3], b10, b11);
+          mma16816(c1[0], c1[1], c1[2], c1[3], al[mt][0], al[mt][1], al[mt][2], al[mt][3], b10, b11);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][j][e] += pp[i][j][e];
+    __syncthreads();  // this stage may be refilled next
+  }
+  // epilogue: rows g / g + 8 of each m16 tile, columns 2t, 2t + 1 of each n8 tile
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int m = m0 + 32 * wm + 16 * mt + g + 8 * hr;
+      if (m >= a.M) continue;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int n = n0 + 32 * wn + 8 * nt + 2 * t;
+        const float v[2] = {acc[mt][nt][2 * hr], acc[mt][nt][2 * hr + 1]};
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          if (n + e >= a.N) continue;
+          float x = v[e];
+          if (a.bias) x = x + a.bias[n + e];
+          if (a.bias2) x = x + a.bias2[n + e];
+          if (a.bias3) x = x + a.bias3[n + e];
+          if (a.relu) x = fmaxf(x, 0.0f);
+          float *c = a.C + (size_t)m * a.ldc + n + e;
+          *c = a.accumulate ? (*c + x) : x;
+        }
+      }
+    }
+}
+
 // ============================================================== rownorm_split
 // One warp per row: xh/xl = split(x * g), ssq[r] = sum x^2 (single slot).
 __global__ void rownorm_split_kernel(const float *x, const float *g, __half *xh, __half *xl, float *ssq, int M,
@@ -588,15 +711,6 @@ T0B_DEV uint32_t pack_h2(__half lo_elem, __half hi_elem) {
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
-// (x0, x1) -> f16x2 hi word and f16x2 lo word (the same values as split_f16
-// element by element, with packed conversions)
-T0B_DEV void split2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
-  const __half2 h = __floats2half2_rn(x0, x1);
-  const float2 hf = __half22float2(h);
-  const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
-  hi = *reinterpret_cast<const uint32_t *>(&h);
-  lo = *reinterpret_cast<const uint32_t *>(&l);
-}
 
 // RoPE on 16 consecutive dims 16cg..16cg+15 (8 pairs) with 16-byte table
 // loads; same arithmetic as rope_pair.
@@ -1106,6 +1220,15 @@ cudaError_t t0b_launch_sgemm(const SgemmArgs &a, cudaStream_t st) {
     if (a.M <= 8) return launch_sgemm_small<8>(a, st);
     if (a.M <= 16) return launch_sgemm_small<16>(a, st);
     return launch_sgemm_small<32>(a, st);
+  }
+  // many rows with f16-exact weights: tensor cores
+  const bool h_ok = a.B16 && a.K % kSgH_BK == 0 && ((uintptr_t)a.B16 % 16 == 0) && a.ldb % 8 == 0;
+  if (h_ok && aligned) {
+    const size_t smem = 2 * kSgH_Stage;
+    cudaError_t e = t0b_smem_limit((const void *)sgemm_h_kernel, smem);
+    if (e != cudaSuccess) return e;
+    sgemm_h_kernel<<<dim3((a.N + kSgH_BN - 1) / kSgH_BN, (a.M + kSgH_BM - 1) / kSgH_BM), 256, smem, st>>>(a);
+    return cudaGetLastError();
   }
   dim3 grid((a.N + 63) / 64, (a.M + 63) / 64);
   sgemm_nt_kernel<<<grid, 256, 0, st>>>(a);

@@ -30,6 +30,7 @@ struct SgemmArgs {
   int lda;
   const float *B;
   int ldb;
+  const __half *B16;  // optional f16 copy of B, exact (B came from f16 on disk): tensor-core path
   float *C;
   int ldc;
   int M, N, K;

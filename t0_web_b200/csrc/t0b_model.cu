@@ -100,6 +100,10 @@ struct t0b_model {
   std::vector<void *> allocs;  // every device allocation of the weights
   const float *enc_hw, *enc_hb, *enc_ow, *enc_ob, *enc_rw, *enc_rb, *temb, *out_g;
   const float *dec_hw, *dec_hb, *dec_ow, *dec_ob, *dec_rw, *dec_rb;
+  // f16 copies of the encoder / decoder matrices when the file stores them as
+  // f16 (exact), for the tensor-core path; NULL otherwise
+  const __half *enc_hw16 = nullptr, *enc_ow16 = nullptr, *enc_rw16 = nullptr;
+  const __half *dec_hw16 = nullptr, *dec_ow16 = nullptr, *dec_rw16 = nullptr;
   int dec_out = 0, enc_in = 0;
   cudaStream_t stream = nullptr;
   bool own_stream = false;
@@ -203,6 +207,21 @@ t0b_status upload_f32(t0b_model *m, const t0b::GgufFile &f, const std::string &n
   CUDA_TRY(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
   m->info.total_weight_bytes += h.size() * 4;
   *dst = (const float *)d;
+  return T0B_OK;
+}
+
+// The f16 bytes of a tensor stored as F16 (exact), or NULL for other types.
+t0b_status upload_f16_copy(t0b_model *m, const t0b::GgufFile &f, const std::string &name, const __half **dst) {
+  *dst = nullptr;
+  auto it = f.tensors.find(name);
+  if (it == f.tensors.end()) return fail(T0B_ERR_FORMAT, "gguf: missing tensor " + name);
+  const auto &t = it->second;
+  if (t.type != t0b::GG_F16) return T0B_OK;
+  void *d = nullptr;
+  if (cudaMalloc(&d, t.n_elements * 2) != cudaSuccess) return fail(T0B_ERR_OOM, "t0b: out of device memory");
+  m->allocs.push_back(d);
+  CUDA_TRY(cudaMemcpy(d, t.data, t.n_elements * 2, cudaMemcpyHostToDevice));
+  *dst = (const __half *)d;
   return T0B_OK;
 }
 
@@ -378,6 +397,15 @@ t0b_status upload_all(t0b_model *m, const t0b::GgufFile &f) {
   UP("decoder.residual_layer.bias", m->dec_rb, (size_t)P * nq);
   m->dec_out = P * nq;
   m->enc_in = 3 * P;
+#define UP16(name, ptr) \
+  if ((s = upload_f16_copy(m, f, name, &(ptr))) != T0B_OK) return s
+  UP16("patch_encoder.projection.mlp.hidden_layer.weight", m->enc_hw16);
+  UP16("patch_encoder.projection.mlp.output_layer.weight", m->enc_ow16);
+  UP16("patch_encoder.projection.residual_layer.weight", m->enc_rw16);
+  UP16("decoder.mlp.hidden_layer.weight", m->dec_hw16);
+  UP16("decoder.mlp.output_layer.weight", m->dec_ow16);
+  UP16("decoder.residual_layer.weight", m->dec_rw16);
+#undef UP16
   for (int l = 0; l < m->L; ++l) {
     LayerW w{};
     const std::string p = "transformer.layers." + std::to_string(l);
@@ -671,6 +699,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   g.A = m->feat.as<float>();
   g.lda = 96;
   g.B = m->enc_hw;
+  g.B16 = m->enc_hw16;
   g.ldb = 96;
   g.C = hid;
   g.ldc = E;
@@ -681,6 +710,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   g.relu = 1;
   LAUNCH(launch(m, KC_SGEMM, 2.0 * g.M * g.N * g.K, 0.0, [&] { return t0b_launch_sgemm(g, m->stream); }));
   g.B = m->enc_rw;
+  g.B16 = m->enc_rw16;
   g.C = x;
   g.bias = m->enc_rb;
   g.bias2 = m->enc_ob;
@@ -690,6 +720,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   g.A = hid;
   g.lda = E;
   g.B = m->enc_ow;
+  g.B16 = m->enc_ow16;
   g.ldb = E;
   g.K = E;
   g.bias = g.bias2 = g.bias3 = nullptr;
@@ -774,6 +805,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   d.A = m->xo.as<float>();
   d.lda = E;
   d.B = m->dec_hw;
+  d.B16 = m->dec_hw16;
   d.ldb = E;
   d.C = m->dhid.as<float>();
   d.ldc = E;
@@ -784,6 +816,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   d.relu = 1;
   LAUNCH(launch(m, KC_SGEMM, 2.0 * d.M * d.N * d.K, 0.0, [&] { return t0b_launch_sgemm(d, m->stream); }));
   d.B = m->dec_rw;
+  d.B16 = m->dec_rw16;
   d.C = m->dout.as<float>();
   d.ldc = m->dec_out;
   d.N = m->dec_out;
@@ -793,6 +826,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   LAUNCH(launch(m, KC_SGEMM, 2.0 * d.M * d.N * d.K, 0.0, [&] { return t0b_launch_sgemm(d, m->stream); }));
   d.A = m->dhid.as<float>();
   d.B = m->dec_ow;
+  d.B16 = m->dec_ow16;
   d.bias = d.bias2 = nullptr;
   d.accumulate = 1;
   LAUNCH(launch(m, KC_SGEMM, 2.0 * d.M * d.N * d.K, 0.0, [&] { return t0b_launch_sgemm(d, m->stream); }));
