@@ -692,7 +692,7 @@ __global__ void __launch_bounds__(128) attn_time_tiled_kernel(AttnArgs a) {
 //     rotated, split into mma fragments), walks the key blocks up to the
 //     diagonal with an online softmax on the score fragments, and accumulates
 //     P.V with P re-split from the score registers (FlashAttention-2 style).
-constexpr int kAttnMmaMaxP = 128;
+constexpr int kAttnMmaMaxP = 256;  // 16 warps, 147 KB of shared memory at p = 256
 
 // RoPE of the adjacent pair (x0, x1) = dims (2i, 2i+1) from a compact table
 // row (cos[32], sin[32] per pair, scale[32], 1/scale[32] per dim mod 32):
@@ -731,7 +731,7 @@ T0B_DEV void rope16(float *x, const float *tab, int cg, bool kside) {
   }
 }
 
-__global__ void __launch_bounds__(256, 2) attn_time_mma_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a) {
   pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
   extern __shared__ uint4 smem_u4[];
   const int r = blockIdx.x, h = blockIdx.y;

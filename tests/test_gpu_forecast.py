@@ -71,6 +71,18 @@ def test_multiseries_ragged_variates(engine, gpu_model, oracle_model):
     assert max_abs(got, ref) <= TOL
 
 
+@pytest.mark.parametrize("t_ctx", [4000, 4096, 7000])
+def test_long_context(engine, gpu_model, oracle_model, t_ctx):
+    """p = 128, 131 and 222 patches per row: the tensor-core time attention
+    beyond 8 query blocks (the context lengths of the box-wide sweep's 4096
+    case and beyond)."""
+    ctx, nv = S.multiseries(2, t_ctx, seed=7, n_variates=2)
+    got = t0_fast.forecast_multiseries(engine, gpu_model("q8_0"), ctx, nv, t_ctx, 96)
+    ref = oracle_model("q8_0").forecast_multiseries(ctx, nv, 96, threads=8)
+    assert np.isfinite(got).all()
+    assert max_abs(got, ref) <= TOL
+
+
 def test_unaligned_context_and_horizon(engine, gpu_model, oracle_model):
     ctx = S.sine_context(77, seed=9)
     got = t0_fast.forecast(engine, gpu_model("q8_0"), ctx, 1, 77, 30)
