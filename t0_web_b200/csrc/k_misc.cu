@@ -24,8 +24,10 @@ constexpr int kPrepChunk = 256;  // steps per chunk (a multiple of the patch siz
 constexpr int kPrepWarps = 4;
 
 __global__ void __launch_bounds__(32 * kPrepWarps) prep_kernel(PrepArgs a) {
-  __shared__ float s_x[kPrepWarps][kPrepChunk], s_cnt[kPrepWarps][kPrepChunk];
-  __shared__ float s_mean[kPrepWarps][kPrepChunk], s_m2[kPrepWarps][kPrepChunk];
+  __shared__ __align__(16) float s_x[kPrepWarps][kPrepChunk];
+  __shared__ __align__(16) float s_cnt[kPrepWarps][kPrepChunk];
+  __shared__ __align__(16) float s_mean[kPrepWarps][kPrepChunk];
+  __shared__ __align__(16) float s_m2[kPrepWarps][kPrepChunk];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kPrepWarps + w;
   if (r >= a.R) return;  // whole warp
@@ -37,26 +39,36 @@ __global__ void __launch_bounds__(32 * kPrepWarps) prep_kernel(PrepArgs a) {
   float count = 0.0f, mean = 0.0f, m2 = 0.0f;  // lane 0's recurrence state
   for (int c0 = 0; c0 < steps; c0 += kPrepChunk) {
     const int n = min(kPrepChunk, steps - c0);
-    // raw values of the chunk (0 outside the context), coalesced
+    // raw values of the chunk, coalesced; steps outside the context read as
+    // NaN here (not observed), which only the recurrence below looks at
     for (int i = lane; i < n; i += 32) {
       const int t = c0 + i;
-      s_x[w][i] = (t >= lead && t < lead + len) ? src[t - lead] : 0.0f;
+      s_x[w][i] = (t >= lead && t < lead + len) ? src[t - lead] : __int_as_float(0x7fc00000);
     }
     __syncwarp();
-    if (lane == 0) {
-      for (int i = 0; i < n; ++i) {
-        const int t = c0 + i;
-        const float x = s_x[w][i];
-        if (t >= lead && t < lead + len && !isnan(x)) {
-          count = __fadd_rn(count, 1.0f);
-          const float delta = __fsub_rn(x, mean);
-          mean = __fadd_rn(mean, __fdiv_rn(delta, count));
-          const float delta2 = __fsub_rn(x, mean);
-          m2 = __fadd_rn(m2, __fmul_rn(delta, delta2));
+    if (lane == 0) {  // n is a multiple of 32: four steps per 16-byte read and write
+#pragma unroll 2
+      for (int i = 0; i < n; i += 4) {
+        const float4 x4 = *reinterpret_cast<const float4 *>(&s_x[w][i]);
+        const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+        float cs[4], ms[4], vs[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float x = xs[u];
+          if (!isnan(x)) {
+            count = __fadd_rn(count, 1.0f);
+            const float delta = __fsub_rn(x, mean);
+            mean = __fadd_rn(mean, __fdiv_rn(delta, count));
+            const float delta2 = __fsub_rn(x, mean);
+            m2 = __fadd_rn(m2, __fmul_rn(delta, delta2));
+          }
+          cs[u] = count;
+          ms[u] = mean;
+          vs[u] = m2;
         }
-        s_cnt[w][i] = count;
-        s_mean[w][i] = mean;
-        s_m2[w][i] = m2;
+        *reinterpret_cast<float4 *>(&s_cnt[w][i]) = make_float4(cs[0], cs[1], cs[2], cs[3]);
+        *reinterpret_cast<float4 *>(&s_mean[w][i]) = make_float4(ms[0], ms[1], ms[2], ms[3]);
+        *reinterpret_cast<float4 *>(&s_m2[w][i]) = make_float4(vs[0], vs[1], vs[2], vs[3]);
       }
     }
     __syncwarp();
