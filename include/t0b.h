@@ -115,6 +115,17 @@ t0b_status t0b_forecast_multiseries(t0b_model *m, const float *ctx, const int32_
 t0b_status t0b_forecast_multiseries_device(t0b_model *m, const float *ctx_dev, const int32_t *n_variates,
                                            size_t n_series, size_t t_ctx, size_t horizon, float *out_dev);
 
+/* Autoregressive rollout for horizons beyond one forward pass (replaces
+ * t0_fast::forecast_rollout, lib.rs:259-345, itself t0-core model.rs:582-665):
+ * one univariate series; a first block of up to 1024 steps, then blocks in
+ * which each query level's quantile path is fed back as observed context
+ * (trailing window of round_up(t_ctx, patch) values), the paths forecast as
+ * one batch, and each step re-reduced to the query levels (quantile.rs).
+ * query: n_query levels ascending inside (0, 1).  Output
+ * [prediction_length, n_query] row-major. */
+t0b_status t0b_forecast_rollout(t0b_model *m, const float *ctx, size_t t_ctx, size_t prediction_length,
+                                const float *query, size_t n_query, float *out);
+
 /* Block until the model's stream is idle and report any kernel-side error. */
 t0b_status t0b_model_sync(t0b_model *m);
 

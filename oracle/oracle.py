@@ -62,6 +62,13 @@ def lib():
                                      C.POINTER(C.c_size_t)]
         L.o_forecast.argtypes = [vp, vp, C.c_int, C.c_int, C.c_int, vp]
         L.o_forecast_batch.argtypes = [vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp]
+        L.o_interpolate_quantiles.argtypes = [vp, C.c_int, vp, vp, C.c_int, vp]
+        L.o_interpolate_quantiles.restype = None
+        L.o_weighted_quantile.argtypes = [vp, C.c_int, vp, vp, C.c_int, vp]
+        L.o_weighted_quantile.restype = None
+        L.o_prob_mass.argtypes = [vp, C.c_int, vp]
+        L.o_prob_mass.restype = None
+        L.o_forecast_rollout.argtypes = [vp, vp, C.c_int, C.c_int, vp, C.c_int, vp]
         L.o_forecast_batch_rows.argtypes = [vp, vp, vp, C.c_int, C.c_int, C.c_int, vp]
         L.o_forecast_multiseries.argtypes = [vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp]
         L.o_forward.argtypes = [vp, C.c_int, C.c_int, vp, vp, vp, vp, vp, vp]
@@ -167,6 +174,34 @@ def scale_input(cfg: dict, variates, mask, group_ids):
     return scaled, loc, sc
 
 
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, np.float32)
+
+
+def interpolate_quantiles(query, levels, values) -> np.ndarray:
+    """quantile.rs:17-43 (oracle/t0_oracle.c o_interpolate_quantiles)."""
+    q, l, v = _f32(query), _f32(levels), _f32(values)
+    out = np.zeros(q.size, np.float32)
+    lib().o_interpolate_quantiles(_p(q), q.size, _p(l), _p(v), l.size, _p(out))
+    return out
+
+
+def weighted_quantile(query, weights, samples) -> np.ndarray:
+    """quantile.rs:47-61."""
+    q, w, s = _f32(query), _f32(weights), _f32(samples)
+    out = np.zeros(q.size, np.float32)
+    lib().o_weighted_quantile(_p(q), q.size, _p(w), _p(s), s.size, _p(out))
+    return out
+
+
+def prob_mass(levels) -> np.ndarray:
+    """quantile.rs:66-78."""
+    l = _f32(levels)
+    out = np.zeros(l.size, np.float32)
+    lib().o_prob_mass(_p(l), l.size, _p(out))
+    return out
+
+
 def gemm_q_f64(qtype: int, w_bytes: np.ndarray, N: int, K: int, x: np.ndarray, bias=None) -> np.ndarray:
     x = np.ascontiguousarray(x, np.float32)
     M = x.shape[0]
@@ -254,6 +289,16 @@ class OracleModel:
                                           _p(out))
         if rc:
             raise ValueError(f"oracle forecast_multiseries failed ({rc})")
+        return out
+
+    def forecast_rollout(self, ctx: np.ndarray, prediction_length: int, query_levels) -> np.ndarray:
+        """t0-core model.rs:582-665: [prediction_length, len(query_levels)]."""
+        ctx = _f32(ctx).reshape(-1)
+        q = _f32(query_levels)
+        out = np.zeros((prediction_length, q.size), np.float32)
+        rc = lib().o_forecast_rollout(self._h, _p(ctx), ctx.size, prediction_length, _p(q), q.size, _p(out))
+        if rc:
+            raise ValueError(f"oracle forecast_rollout failed ({rc})")
         return out
 
     def forward(self, variates, mask, group_ids, variate_type, trace: bool = False):

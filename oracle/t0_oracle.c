@@ -1263,3 +1263,167 @@ int o_swiglu_q_f64(int type, const uint8_t *w0, int F, int K, const uint8_t *w2,
   free(d2);
   return 0;
 }
+
+/* ===================================================== quantile utilities
+ * quantile.rs restated in f32 with the same operation order.  Sorting is
+ * stable (Rust's sort_by), done by insertion on index arrays. */
+static void stable_order(const float *key, int n, int *idx) {
+  for (int i = 0; i < n; ++i) {
+    int j = i;
+    while (j > 0 && key[idx[j - 1]] > key[i]) {
+      idx[j] = idx[j - 1];
+      --j;
+    }
+    idx[j] = i;
+  }
+}
+
+/* quantile.rs:17-43 */
+void o_interpolate_quantiles(const float *query, int nq, const float *levels, const float *values, int n,
+                             float *out) {
+  if (n < 1) return;
+  int *idx = (int *)malloc(sizeof(int) * (size_t)n);
+  float *lv = (float *)malloc(sizeof(float) * (size_t)(n + 2));
+  float *vv = (float *)malloc(sizeof(float) * (size_t)(n + 2));
+  stable_order(levels, n, idx);
+  int len = 0;
+  if (levels[idx[0]] > 0.0f) {  /* insert (0, first value) */
+    lv[len] = 0.0f;
+    vv[len] = values[idx[0]];
+    ++len;
+  }
+  for (int i = 0; i < n; ++i, ++len) {
+    lv[len] = levels[idx[i]];
+    vv[len] = values[idx[i]];
+  }
+  if (lv[len - 1] < 1.0f) {  /* push (1, last value) */
+    lv[len] = 1.0f;
+    vv[len] = vv[len - 1];
+    ++len;
+  }
+  for (int k = 0; k < nq; ++k) {
+    const float q = query[k];
+    int upper = 0;  /* partition_point(l <= q) */
+    while (upper < len && lv[upper] <= q) ++upper;
+    if (upper > len - 1) upper = len - 1;
+    const int lower = upper > 0 ? upper - 1 : 0;
+    const float ll = lv[lower], ul = lv[upper], lo = vv[lower], uo = vv[upper];
+    const float diff = ul - ll;
+    const float w = diff == 0.0f ? 0.0f : (q - ll) / diff;
+    out[k] = lo + w * (uo - lo);
+  }
+  free(idx);
+  free(lv);
+  free(vv);
+}
+
+/* quantile.rs:47-61 */
+void o_weighted_quantile(const float *query, int nq, const float *weights, const float *samples, int n,
+                         float *out) {
+  float sum = 0.0f;
+  for (int i = 0; i < n; ++i) sum += weights[i];
+  int *idx = (int *)malloc(sizeof(int) * (size_t)n);
+  float *ss = (float *)malloc(sizeof(float) * (size_t)n);
+  float *cw = (float *)malloc(sizeof(float) * (size_t)n);
+  stable_order(samples, n, idx);
+  float cum = 0.0f;
+  for (int i = 0; i < n; ++i) {
+    ss[i] = samples[idx[i]];
+    cum += weights[idx[i]] / sum;
+    cw[i] = cum < 0.0f ? 0.0f : (cum > 1.0f ? 1.0f : cum);
+  }
+  o_interpolate_quantiles(query, nq, cw, ss, n, out);
+  free(idx);
+  free(ss);
+  free(cw);
+}
+
+/* quantile.rs:66-78 */
+void o_prob_mass(const float *levels, int n, float *out) {
+  float sum = 0.0f;
+  for (int i = 0; i < n; ++i) {
+    const float lo = i == 0 ? 0.0f : levels[i - 1];
+    const float hi = i == n - 1 ? 1.0f : levels[i + 1];
+    out[i] = (hi - lo) / 2.0f;
+  }
+  for (int i = 0; i < n; ++i) sum += out[i];
+  for (int i = 0; i < n; ++i) out[i] /= sum;
+}
+
+/* ================================================ autoregressive rollout
+ * t0-core model.rs:582-665: a first single-window block of up to
+ * MAX_HORIZON steps, then blocks in which each query-level path feeds its
+ * own previous block back as observed context (trailing context_width
+ * window), the paths are forecast as one batch, and every step's
+ * path x trained-level outputs are reduced back to the query levels by
+ * weighted_quantile over the trained-mass x query-mass grid. */
+int o_forecast_rollout(const o_model *m, const float *ctx, int t_ctx, int prediction_length, const float *query,
+                       int nq, float *out) {
+  const int P = m->cfg.patch_size, ntr = m->cfg.n_quantiles, MAXH = 1024;
+  const float *trained = m->cfg.quantile_levels;
+  if (t_ctx < 1 || prediction_length < 1 || nq < 1) return -1;
+  float trained_mass[32], *query_mass = (float *)malloc(sizeof(float) * (size_t)nq);
+  o_prob_mass(trained, ntr, trained_mass);
+  o_prob_mass(query, nq, query_mass);
+  const int context_width = (t_ctx + P - 1) / P * P;
+  int horizon0 = (prediction_length + P - 1) / P * P;
+  if (horizon0 > MAXH) horizon0 = MAXH;
+  const int total = prediction_length + MAXH + P;  /* output buffer incl. the last block's overshoot */
+  float *res = (float *)malloc(sizeof(float) * (size_t)total * nq);
+  float *block0 = (float *)malloc(sizeof(float) * (size_t)horizon0 * ntr);
+  int rc = o_forecast(m, ctx, 1, t_ctx, horizon0, block0);
+  if (rc) goto done;
+  for (int h = 0; h < horizon0; ++h) o_interpolate_quantiles(query, nq, trained, block0 + (size_t)h * ntr, ntr,
+                                                             res + (size_t)h * nq);
+  if (prediction_length > horizon0) {
+    const int npath = nq;
+    /* each path's buffer: the context followed by everything fed back */
+    const int cap = t_ctx + prediction_length + MAXH + P;
+    float *paths = (float *)malloc(sizeof(float) * (size_t)npath * cap);
+    int plen = t_ctx;
+    for (int j = 0; j < npath; ++j) memcpy(paths + (size_t)j * cap, ctx, sizeof(float) * (size_t)t_ctx);
+    int remaining = prediction_length - horizon0, prev_off = 0, prev_width = horizon0, done_steps = horizon0;
+    float *batch = (float *)malloc(sizeof(float) * (size_t)npath * context_width);
+    float *blocks = (float *)malloc(sizeof(float) * (size_t)npath * MAXH * ntr);
+    float *samples = (float *)malloc(sizeof(float) * (size_t)npath * ntr);
+    float *weights = (float *)malloc(sizeof(float) * (size_t)npath * ntr);
+    for (int j = 0; j < npath; ++j)
+      for (int pq = 0; pq < ntr; ++pq) weights[j * ntr + pq] = trained_mass[pq] * query_mass[j];
+    while (remaining > 0 && rc == 0) {
+      for (int j = 0; j < npath; ++j)
+        for (int h = 0; h < prev_width; ++h) paths[(size_t)j * cap + plen + h] = res[(size_t)(prev_off + h) * nq + j];
+      plen += prev_width;
+      int horizon = (remaining + P - 1) / P * P;
+      if (horizon > MAXH) horizon = MAXH;
+      for (int j = 0; j < npath; ++j) {
+        const int w = plen < context_width ? plen : context_width;
+        float *dst = batch + (size_t)j * context_width;
+        memset(dst, 0, sizeof(float) * (size_t)context_width);
+        memcpy(dst + (context_width - w), paths + (size_t)j * cap + (plen - w), sizeof(float) * (size_t)w);
+      }
+      rc = o_forecast_batch(m, batch, npath, context_width, horizon, npath, blocks);
+      if (rc) break;
+      for (int h = 0; h < horizon; ++h) {
+        for (int j = 0; j < npath; ++j)
+          for (int pq = 0; pq < ntr; ++pq)
+            samples[j * ntr + pq] = blocks[((size_t)j * horizon + h) * ntr + pq];
+        o_weighted_quantile(query, nq, weights, samples, npath * ntr, res + (size_t)(done_steps + h) * nq);
+      }
+      prev_off = done_steps;
+      prev_width = horizon;
+      done_steps += horizon;
+      remaining = remaining > horizon ? remaining - horizon : 0;
+    }
+    free(paths);
+    free(batch);
+    free(blocks);
+    free(samples);
+    free(weights);
+  }
+  if (rc == 0) memcpy(out, res, sizeof(float) * (size_t)prediction_length * nq);
+done:
+  free(res);
+  free(block0);
+  free(query_mass);
+  return rc;
+}

@@ -84,6 +84,17 @@ int o_forecast(const o_model *m, const float *ctx, int v, int t_ctx,
                int horizon, float *out);                         /* model.rs:322-333 */
 int o_forecast_batch(const o_model *m, const float *ctx, int n, int t_ctx,
                      int horizon, int chunk, float *out);        /* model.rs:385-407 */
+
+/* ---- quantile utilities (t0-core quantile.rs) and autoregressive rollout
+ * (t0-core model.rs:582-665).  Query levels sorted ascending, inside (0, 1).
+ * o_forecast_rollout writes [prediction_length, nq] (query-level minor). */
+void o_interpolate_quantiles(const float *query, int nq, const float *levels, const float *values, int n,
+                             float *out);                                                  /* quantile.rs:17-43 */
+void o_weighted_quantile(const float *query, int nq, const float *weights, const float *samples, int n,
+                         float *out);                                                      /* quantile.rs:47-61 */
+void o_prob_mass(const float *levels, int n, float *out);                                 /* quantile.rs:66-78 */
+int o_forecast_rollout(const o_model *m, const float *ctx, int t_ctx, int prediction_length, const float *query,
+                       int nq, float *out);
 int o_forecast_batch_rows(const o_model *m, const float *ctx,
                           const int64_t *lengths, int n, int horizon,
                           int chunk, float *out);    /* t0-fast lib.rs:175-242 */

@@ -19,7 +19,7 @@ EXPORTED = [
     "t0b_last_error", "t0b_engine_create", "t0b_engine_destroy", "t0b_model_load_gguf", "t0b_model_destroy",
     "t0b_model_info_get", "t0b_model_set_stream", "t0b_model_stream", "t0b_model_set_max_tokens", "t0b_model_use_graphs",
     "t0b_forecast", "t0b_forecast_batch", "t0b_forecast_batch_rows", "t0b_forecast_multiseries",
-    "t0b_forecast_multiseries_device", "t0b_model_sync", "t0b_gemm_q", "t0b_swiglu_q", "t0b_gemm_q_noalloc",
+    "t0b_forecast_multiseries_device", "t0b_forecast_rollout", "t0b_model_sync", "t0b_gemm_q", "t0b_swiglu_q", "t0b_gemm_q_noalloc",
     "t0b_qmatrix_create", "t0b_qmatrix_destroy", "t0b_qmatrix_gemm", "t0b_qmatrix_swiglu", "t0b_qmatrix_sync",
     "t0b_gguf_validate",
     "t0b_quantize", "t0b_dequantize", "t0b_row_bytes", "t0b_export_gguf", "t0b_model_profile_enable",
@@ -77,6 +77,7 @@ def lib() -> C.CDLL:
     L.t0b_forecast_batch_rows.argtypes = [vp, vp, vp, sz, sz, sz, vp]
     L.t0b_forecast_multiseries.argtypes = [vp, vp, vp, sz, sz, sz, vp]
     L.t0b_forecast_multiseries_device.argtypes = [vp, vp, vp, sz, sz, sz, vp]
+    L.t0b_forecast_rollout.argtypes = [vp, vp, sz, sz, vp, sz, vp]
     L.t0b_model_sync.argtypes = [vp]
     L.t0b_gemm_q.argtypes = [vp, st, vp, st, st, vp, st, vp, vp, vp]
     L.t0b_swiglu_q.argtypes = [vp, st, vp, vp, st, st, st, vp, st, vp, vp, vp, vp, vp]

@@ -45,7 +45,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
         o = os.path.join(OBJ, src + ".o")
         objs.append(o)
         if force or _stale(o, [s] + headers):
-            cmd = [nvcc, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-rdc=false",
+            cmd = [nvcc, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-ffp-contract=off", "-rdc=false",
                    "-I", CSRC, "-I", os.path.join(ROOT, "include"), "-c", s, "-o", o]
             if verbose:
                 cmd.insert(1, "-Xptxas=-v")
@@ -56,7 +56,8 @@ def build(verbose: bool = False, force: bool = False) -> str:
         o = os.path.join(OBJ, src + ".o")
         objs.append(o)
         if force or _stale(o, [s] + headers):
-            subprocess.run(["g++", "-O2", "-fPIC", "-std=c++17", "-I", CSRC, "-c", s, "-o", o], check=True)
+            subprocess.run(["g++", "-O2", "-fPIC", "-ffp-contract=off", "-std=c++17", "-I", CSRC, "-c", s, "-o", o],
+                           check=True)
     if force or _stale(LIB, objs):
         subprocess.run([nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"], check=True)
     return LIB

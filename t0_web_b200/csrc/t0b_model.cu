@@ -1155,6 +1155,129 @@ cudaError_t t0b_smem_limit(const void *kernel, size_t bytes) {
   return e;
 }
 
+// ================================================== autoregressive rollout
+// t0-fast lib.rs:259-345 (port of t0-core model.rs:582-665) over this
+// library's own forecast entry points; the quantile reductions are host f32
+// code restating t0-core quantile.rs with the same operation order.
+namespace {
+// indices of key in stable ascending order (Rust's sort_by is stable)
+std::vector<int> stable_order(const float *key, int n) {
+  std::vector<int> idx(n);
+  for (int i = 0; i < n; ++i) idx[i] = i;
+  std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return key[a] < key[b]; });
+  return idx;
+}
+
+// quantile.rs:17-43
+void interpolate_quantiles(const float *query, int nq, const float *levels, const float *values, int n, float *out) {
+  const std::vector<int> idx = stable_order(levels, n);
+  std::vector<float> lv, vv;
+  lv.reserve(n + 2);
+  vv.reserve(n + 2);
+  if (levels[idx[0]] > 0.0f) lv.push_back(0.0f), vv.push_back(values[idx[0]]);
+  for (int i : idx) lv.push_back(levels[i]), vv.push_back(values[i]);
+  if (lv.back() < 1.0f) lv.push_back(1.0f), vv.push_back(vv.back());
+  const int len = (int)lv.size();
+  for (int k = 0; k < nq; ++k) {
+    const float q = query[k];
+    int upper = (int)(std::upper_bound(lv.begin(), lv.end(), q) - lv.begin());  // partition_point(l <= q)
+    upper = std::min(upper, len - 1);
+    const int lower = upper > 0 ? upper - 1 : 0;
+    const float ll = lv[lower], ul = lv[upper], lo = vv[lower], uo = vv[upper];
+    const float diff = ul - ll;
+    const float w = diff == 0.0f ? 0.0f : (q - ll) / diff;
+    const float step = w * (uo - lo);
+    out[k] = lo + step;
+  }
+}
+
+// quantile.rs:47-61
+void weighted_quantile(const float *query, int nq, const float *weights, const float *samples, int n, float *out) {
+  float sum = 0.0f;
+  for (int i = 0; i < n; ++i) sum += weights[i];
+  const std::vector<int> idx = stable_order(samples, n);
+  std::vector<float> ss(n), cw(n);
+  float cum = 0.0f;
+  for (int i = 0; i < n; ++i) {
+    ss[i] = samples[idx[i]];
+    cum += weights[idx[i]] / sum;
+    cw[i] = std::min(std::max(cum, 0.0f), 1.0f);
+  }
+  interpolate_quantiles(query, nq, cw.data(), ss.data(), n, out);
+}
+
+// quantile.rs:66-78
+std::vector<float> prob_mass(const float *levels, int n) {
+  std::vector<float> mass(n);
+  for (int i = 0; i < n; ++i) {
+    const float lo = i == 0 ? 0.0f : levels[i - 1];
+    const float hi = i == n - 1 ? 1.0f : levels[i + 1];
+    mass[i] = (hi - lo) / 2.0f;
+  }
+  float sum = 0.0f;
+  for (float v : mass) sum += v;
+  for (float &v : mass) v /= sum;
+  return mass;
+}
+}  // namespace
+
+extern "C" t0b_status t0b_forecast_rollout(t0b_model *m, const float *ctx, size_t t_ctx, size_t prediction_length,
+                                           const float *query, size_t n_query, float *out) {
+  if (!m || !ctx || !query || !out) return fail(T0B_ERR_INVALID, "t0b_forecast_rollout: NULL argument");
+  if (t_ctx == 0 || prediction_length == 0 || n_query == 0 || n_query > 64)
+    return fail(T0B_ERR_INVALID, "t0b_forecast_rollout: need t_ctx >= 1, prediction_length >= 1, 1..64 levels");
+  for (size_t i = 0; i < n_query; ++i)
+    if (!(query[i] > 0.0f && query[i] < 1.0f) || (i && !(query[i] > query[i - 1])))
+      return fail(T0B_ERR_INVALID, "t0b_forecast_rollout: query levels must be ascending and inside (0, 1)");
+  const size_t P = (size_t)m->P, kMaxH = (size_t)kMaxHorizon;
+  const int ntr = m->nq, nq = (int)n_query;
+  const float *trained = m->info.quantile_levels;
+  const std::vector<float> trained_mass = prob_mass(trained, ntr), query_mass = prob_mass(query, nq);
+  const size_t context_width = (t_ctx + P - 1) / P * P;
+  const size_t horizon0 = std::min((prediction_length + P - 1) / P * P, kMaxH);
+
+  std::vector<float> block((size_t)horizon0 * ntr);
+  t0b_status st = t0b_forecast(m, ctx, 1, t_ctx, horizon0, block.data());
+  if (st != T0B_OK) return st;
+  std::vector<float> res(horizon0 * nq);  // all blocks, query-level minor
+  for (size_t h = 0; h < horizon0; ++h)
+    interpolate_quantiles(query, nq, trained, block.data() + h * ntr, ntr, res.data() + h * nq);
+  if (prediction_length > horizon0) {
+    // each query level is one path: its context plus everything fed back
+    std::vector<std::vector<float>> paths(nq, std::vector<float>(ctx, ctx + t_ctx));
+    size_t remaining = prediction_length - horizon0, prev_off = 0, prev_width = horizon0;
+    std::vector<float> weights((size_t)nq * ntr), samples((size_t)nq * ntr), batch, blocks;
+    for (int j = 0; j < nq; ++j)
+      for (int pq = 0; pq < ntr; ++pq) weights[(size_t)j * ntr + pq] = trained_mass[pq] * query_mass[j];
+    while (remaining > 0) {
+      for (int j = 0; j < nq; ++j)
+        for (size_t h = 0; h < prev_width; ++h) paths[j].push_back(res[(prev_off + h) * nq + j]);
+      const size_t horizon = std::min((remaining + P - 1) / P * P, kMaxH);
+      batch.assign((size_t)nq * context_width, 0.0f);
+      for (int j = 0; j < nq; ++j) {  // trailing window, right-aligned
+        const size_t w = std::min(context_width, paths[j].size());
+        std::copy(paths[j].end() - w, paths[j].end(), batch.begin() + (size_t)j * context_width + (context_width - w));
+      }
+      // the n_query paths are one batch: one device pass per block
+      blocks.assign((size_t)nq * horizon * ntr, 0.0f);
+      if ((st = t0b_forecast_batch(m, batch.data(), nq, context_width, horizon, nq, blocks.data())) != T0B_OK)
+        return st;
+      prev_off = res.size() / nq;
+      res.resize(res.size() + horizon * nq);
+      for (size_t h = 0; h < horizon; ++h) {
+        for (int j = 0; j < nq; ++j)
+          for (int pq = 0; pq < ntr; ++pq)
+            samples[(size_t)j * ntr + pq] = blocks[((size_t)j * horizon + h) * ntr + pq];
+        weighted_quantile(query, nq, weights.data(), samples.data(), nq * ntr, res.data() + (prev_off + h) * nq);
+      }
+      prev_width = horizon;
+      remaining = remaining > horizon ? remaining - horizon : 0;  // the last block may overshoot
+    }
+  }
+  std::memcpy(out, res.data(), prediction_length * n_query * sizeof(float));
+  return T0B_OK;
+}
+
 // ======================================================= standalone GEMMs
 namespace {
 // Grows engine scratch; growing waits for the stream first, since work

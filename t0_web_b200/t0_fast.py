@@ -145,6 +145,19 @@ def forecast(engine: Engine, model: GpuModel, context, v: int, t_ctx: int, horiz
     return out
 
 
+def forecast_rollout(engine: Engine, model: GpuModel, context, t_ctx: int, prediction_length: int,
+                     query_quantile_levels) -> np.ndarray:
+    """One univariate series, any horizon: [prediction_length, len(levels)]
+    (t_ctx values of context; levels ascending inside (0, 1))."""
+    ctx = _f32(context).reshape(-1)
+    if ctx.size != t_ctx:
+        raise T0bError(1, f"forecast_rollout: context has {ctx.size} values, expected t_ctx = {t_ctx}")
+    q = _f32(query_quantile_levels).reshape(-1)
+    out = np.empty((prediction_length, q.size), np.float32)
+    check(lib().t0b_forecast_rollout(model.handle, ptr(ctx), t_ctx, prediction_length, ptr(q), q.size, ptr(out)))
+    return out
+
+
 def forecast_batch_chunked(engine: Engine, model: GpuModel, contexts, n_signals: int, t_ctx: int, horizon: int,
                            chunk_size: int = DEFAULT_BATCH_CHUNK) -> np.ndarray:
     """n_signals independent univariate series, [n_signals, t_ctx]."""

@@ -143,6 +143,27 @@ def test_graph_replay_matches_eager_launches(engine, gpu_model):
         assert m.launch_count() - n0 == eager_launches
 
 
+DECILES = [0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9]
+
+
+@pytest.mark.parametrize("pred,levels", [(100, DECILES), (1100, DECILES), (1300, [0.1, 0.25, 0.5, 0.75, 0.9])],
+                         ids=["one_block", "two_blocks_deciles", "two_blocks_trained_levels"])
+def test_rollout_vs_oracle(engine, gpu_model, oracle_model, pred, levels):
+    """forecast_rollout (t0-fast lib.rs:259-345): horizons beyond one
+    forward pass, every query-level path fed back and re-reduced."""
+    ctx = S.sine_context(512, seed=0)
+    got = t0_fast.forecast_rollout(engine, gpu_model("q8_0"), ctx, 512, pred, levels)
+    ref = oracle_model("q8_0").forecast_rollout(ctx, pred, levels)
+    assert got.shape == (pred, len(levels))
+    assert np.isfinite(got).all()
+    assert max_abs(got, ref) <= TOL
+
+
+def test_rollout_rejects_unsorted_levels(engine, gpu_model):
+    with pytest.raises(T0bError):
+        t0_fast.forecast_rollout(engine, gpu_model("q8_0"), S.sine_context(64), 64, 2000, [0.5, 0.1])
+
+
 def test_horizon_limit_is_an_error(engine, gpu_model):
     with pytest.raises(T0bError):
         t0_fast.forecast(engine, gpu_model("q8_0"), S.sine_context(64), 1, 64, 1025)

@@ -210,3 +210,69 @@ def test_lcg_kernel_recipe(qtype, m):
     ref = np.array([[np.float32(np.dot(x[i].astype(np.float32), wd[j])) for j in range(n)] for i in range(m)])
     got = O.gemm_q_f64(qtype, wb, n, k, x)
     assert np.max(np.abs(got - ref)) < 1e-5
+
+
+# ------------------------------------------------------------ quantile.rs
+def _np_interpolate(query, levels, values):
+    """quantile.rs:17-43 restated in numpy float32 (stable sort, flat ends)."""
+    levels = np.asarray(levels, np.float32)
+    values = np.asarray(values, np.float32)
+    idx = np.argsort(levels, kind="stable")
+    lv, vv = list(levels[idx]), list(values[idx])
+    if lv[0] > 0:
+        lv.insert(0, np.float32(0.0))
+        vv.insert(0, vv[0])
+    if lv[-1] < 1:
+        lv.append(np.float32(1.0))
+        vv.append(vv[-1])
+    lv, vv = np.array(lv, np.float32), np.array(vv, np.float32)
+    out = []
+    for q in np.asarray(query, np.float32):
+        upper = min(int(np.searchsorted(lv, q, side="right")), len(lv) - 1)
+        lower = max(upper - 1, 0)
+        diff = np.float32(lv[upper] - lv[lower])
+        w = np.float32(0.0) if diff == 0 else np.float32(np.float32(q - lv[lower]) / diff)
+        out.append(np.float32(vv[lower] + np.float32(w * np.float32(vv[upper] - vv[lower]))))
+    return np.array(out, np.float32)
+
+
+def _np_weighted(query, weights, samples):
+    """quantile.rs:47-61: running f32 sums in the reference's order."""
+    w = np.asarray(weights, np.float32)
+    s = np.asarray(samples, np.float32)
+    total = np.float32(0.0)
+    for x in w:
+        total = np.float32(total + x)
+    idx = np.argsort(s, kind="stable")
+    cum, cw = np.float32(0.0), []
+    for i in idx:
+        cum = np.float32(cum + np.float32(w[i] / total))
+        cw.append(np.float32(min(max(cum, 0.0), 1.0)))
+    return _np_interpolate(query, cw, s[idx])
+
+
+def test_quantile_reference_known_answers():
+    """quantile.rs:82-97: identity at the trained levels; probability mass sums to 1."""
+    lv = [0.1, 0.25, 0.5, 0.75, 0.9]
+    assert np.max(np.abs(O.interpolate_quantiles(lv, lv, [1, 2, 3, 4, 5]) - np.arange(1, 6))) < 1e-6
+    assert abs(float(O.prob_mass(lv).sum()) - 1.0) < 1e-6
+
+
+def test_prob_mass_hand_computed():
+    """Trapezoid masses (b[i+2] - b[i]) / 2 over [0, levels, 1], normalised."""
+    m = O.prob_mass([0.1, 0.25, 0.5, 0.75, 0.9])
+    raw = np.array([0.125, 0.2, 0.25, 0.2, 0.125])
+    assert np.allclose(m, raw / raw.sum(), atol=1e-7)
+
+
+@pytest.mark.parametrize("seed", range(5))
+def test_quantile_utilities_match_numpy_restatement(seed):
+    rng = np.random.default_rng(seed)
+    trained = np.array([0.1, 0.25, 0.5, 0.75, 0.9], np.float32)
+    query = np.sort(rng.uniform(0.01, 0.99, 9)).astype(np.float32)
+    values = np.sort(rng.standard_normal(5)).astype(np.float32) * np.float32(50)
+    assert np.array_equal(O.interpolate_quantiles(query, trained, values), _np_interpolate(query, trained, values))
+    w = rng.uniform(0.01, 1.0, 25).astype(np.float32)
+    s = rng.standard_normal(25).astype(np.float32)
+    s[3] = s[7]  # a tie keeps the stable order
+    assert np.array_equal(O.weighted_quantile(query, w, s), _np_weighted(query, w, s))
