@@ -989,69 +989,354 @@ __global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a) {
   }
 }
 
+// ------------------------------------------------- 128-dim heads (t0-beta)
+// Time attention for heads of HD = 128 dims, p <= 192, with the arithmetic
+// of attn_time_mma_kernel (split-f16 QK^T and PV on mma.sync, online
+// softmax).  At most 8 warps, each taking query blocks warp, warp + 8, ...;
+// k / v rows are staged in 64-dim halves after a sum-of-squares pass, so no
+// thread holds a whole row.
+constexpr int kAttnWideMaxP = 192;  // 4 f16 planes of [192][136]: 209 KB of shared memory
+
+// RoPE on dims 16cg .. 16cg + 15 from a compact table row [2 HD]
+// (cos[HD/2], sin[HD/2] per pair, scale[HD/2], 1/scale[HD/2] per dim mod
+// HD/2); same arithmetic as rope16.
+template <int HD>
+T0B_DEV void rope16_hd(float *x, const float *tab, int cg, bool kside) {
+  constexpr int HALF = HD / 2;
+  const float *cs = tab + 8 * cg, *sn = tab + HALF + 8 * cg;
+  const float *sv = tab + (kside ? 3 * HALF : 2 * HALF) + ((16 * cg) % HALF);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float a0 = x[2 * i], a1 = x[2 * i + 1];
+    x[2 * i] = a0 * cs[i] * sv[2 * i] + (-a1) * sn[i] * sv[2 * i];
+    x[2 * i + 1] = a1 * cs[i] * sv[2 * i + 1] + a0 * sn[i] * sv[2 * i + 1];
+  }
+}
+template <int HD>
+T0B_DEV void rope_pair_hd(float &x0, float &x1, const float *tab, int i, bool kside) {
+  constexpr int HALF = HD / 2;
+  const float c = tab[i], sn = tab[HALF + i];
+  const float *sc = tab + (kside ? 3 * HALF : 2 * HALF);
+  const float s0 = sc[(2 * i) % HALF], s1 = sc[(2 * i + 1) % HALF];
+  const float a0 = x0, a1 = x1;
+  x0 = a0 * c * s0 + (-a1) * sn * s0;
+  x1 = a1 * c * s1 + a0 * sn * s1;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256, 1) attn_time_wide_kernel(AttnArgs a) {
+  pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
+  constexpr int PITCH = HD + 8;  // halves: conflict-free ldmatrix rows
+  constexpr int NKC = HD / 16;   // 16-dim chunks of a head
+  constexpr int NDT = HD / 8;    // n8 tiles of the output
+  extern __shared__ uint4 smem_u4[];
+  const int r = blockIdx.x, h = blockIdx.y;
+  const int p = a.p, E = a.E;
+  const int QB = (p + 15) >> 4;  // blocks of 16 queries (= keys)
+  const int PK = QB * 16;
+  __half *Kh = reinterpret_cast<__half *>(smem_u4);
+  __half *Kl = Kh + PK * PITCH;
+  __half *Vh = Kl + PK * PITCH;
+  __half *Vl = Vh + PK * PITCH;
+  const size_t tok0 = (size_t)r * p;
+  const bool rope = a.use_rope != 0;
+  const int lo = a.row_first_valid[r];
+  const float qk_scale = 1.0f / sqrtf((float)HD);
+
+  // ---- staging: rows [0, PK) are v rows, [PK, 2 PK) k rows (rows >= p zero)
+  for (int row = threadIdx.x; row < 2 * PK; row += blockDim.x) {
+    const bool is_k = row >= PK;
+    const int j = is_k ? row - PK : row;
+    const float *src = a.qkv + (tok0 + (j < p ? j : 0)) * 3 * E + (is_k ? E : 2 * E) + h * HD;
+    float rdn = 1.0f;
+    if (is_k && j < p) {  // QK-norm over the whole head
+      float ss = 0.0f;
+#pragma unroll 4
+      for (int c = 0; c < HD / 4; ++c) {
+        const float4 x4 = reinterpret_cast<const float4 *>(src)[c];
+        ss += x4.x * x4.x;
+        ss += x4.y * x4.y;
+        ss += x4.z * x4.z;
+        ss += x4.w * x4.w;
+      }
+      rdn = 1.0f / sqrtf(ss / (float)HD + 1e-8f);
+    }
+    __half *dh = (is_k ? Kh : Vh) + j * PITCH, *dl = (is_k ? Kl : Vl) + j * PITCH;
+#pragma unroll 1
+    for (int hf = 0; hf < HD / 64; ++hf) {
+      float xv[64];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const float4 x4 = j < p ? reinterpret_cast<const float4 *>(src + 64 * hf)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        xv[4 * c] = x4.x, xv[4 * c + 1] = x4.y, xv[4 * c + 2] = x4.z, xv[4 * c + 3] = x4.w;
+      }
+      if (is_k && j < p) {
+        const float *gk = a.kn + 64 * hf;
+#pragma unroll
+        for (int d = 0; d < 64; ++d) xv[d] = xv[d] * rdn * gk[d];
+        if (rope) {
+          const float *tab = a.rope_c + (size_t)j * 2 * HD;
+#pragma unroll
+          for (int cg = 0; cg < 4; ++cg) rope16_hd<HD>(xv + 16 * cg, tab, 4 * hf + cg, true);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) split2(xv[8 * u + 2 * e], xv[8 * u + 2 * e + 1], hw[e], lw[e]);
+        *reinterpret_cast<uint4 *>(dh + 64 * hf + 8 * u) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4 *>(dl + 64 * hf + 8 * u) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      }
+    }
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  for (int qb = warp; qb < QB; qb += nw) {
+    const int ia = qb * 16 + g, ib = ia + 8;  // this thread's two query rows
+    uint32_t qh[NKC][4], ql[NKC][4];
+    {
+      // dims 16 kc + {2t, 2t+1, 2t+8, 2t+9} of rows ia, ib (rows >= p are zero)
+      float qa[NKC][4], qv[NKC][4];
+      const float *ra = a.qkv + (tok0 + min(ia, p - 1)) * 3 * E + h * HD;
+      const float *rb = a.qkv + (tok0 + min(ib, p - 1)) * 3 * E + h * HD;
+      float sa = 0.0f, sb = 0.0f;
+#pragma unroll
+      for (int kc = 0; kc < NKC; ++kc) {
+        const float2 u0 = *reinterpret_cast<const float2 *>(ra + 16 * kc + 2 * t);
+        const float2 u1 = *reinterpret_cast<const float2 *>(ra + 16 * kc + 2 * t + 8);
+        const float2 w0 = *reinterpret_cast<const float2 *>(rb + 16 * kc + 2 * t);
+        const float2 w1 = *reinterpret_cast<const float2 *>(rb + 16 * kc + 2 * t + 8);
+        qa[kc][0] = ia < p ? u0.x : 0.0f, qa[kc][1] = ia < p ? u0.y : 0.0f;
+        qa[kc][2] = ia < p ? u1.x : 0.0f, qa[kc][3] = ia < p ? u1.y : 0.0f;
+        qv[kc][0] = ib < p ? w0.x : 0.0f, qv[kc][1] = ib < p ? w0.y : 0.0f;
+        qv[kc][2] = ib < p ? w1.x : 0.0f, qv[kc][3] = ib < p ? w1.y : 0.0f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sa += qa[kc][e] * qa[kc][e], sb += qv[kc][e] * qv[kc][e];
+      }
+      sa += __shfl_xor_sync(0xffffffffu, sa, 1);
+      sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+      sb += __shfl_xor_sync(0xffffffffu, sb, 1);
+      sb += __shfl_xor_sync(0xffffffffu, sb, 2);
+      const float ra_n = 1.0f / sqrtf(sa / (float)HD + 1e-8f), rb_n = 1.0f / sqrtf(sb / (float)HD + 1e-8f);
+      const float *ta = a.rope_c + (size_t)min(ia, p - 1) * 2 * HD, *tb = a.rope_c + (size_t)min(ib, p - 1) * 2 * HD;
+#pragma unroll
+      for (int kc = 0; kc < NKC; ++kc) {
+        const float2 g0 = *reinterpret_cast<const float2 *>(a.qn + 16 * kc + 2 * t);
+        const float2 g1 = *reinterpret_cast<const float2 *>(a.qn + 16 * kc + 2 * t + 8);
+        const float gg[4] = {g0.x, g0.y, g1.x, g1.y};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          qa[kc][e] = qa[kc][e] * ra_n * gg[e];
+          qv[kc][e] = qv[kc][e] * rb_n * gg[e];
+        }
+        if (rope) {
+#pragma unroll
+          for (int e = 0; e < 4; e += 2) {
+            const int pi = 8 * kc + t + (e >> 1) * 4;  // pair index of dims (2pi, 2pi+1)
+            rope_pair_hd<HD>(qa[kc][e], qa[kc][e + 1], ta, pi, false);
+            rope_pair_hd<HD>(qv[kc][e], qv[kc][e + 1], tb, pi, false);
+          }
+        }
+        split2(qa[kc][0], qa[kc][1], qh[kc][0], ql[kc][0]);
+        split2(qv[kc][0], qv[kc][1], qh[kc][1], ql[kc][1]);
+        split2(qa[kc][2], qa[kc][3], qh[kc][2], ql[kc][2]);
+        split2(qv[kc][2], qv[kc][3], qh[kc][3], ql[kc][3]);
+      }
+    }
+
+    const bool any_masked = qb * 16 < lo;  // a whole-padding query in this block
+    const int kb0 = any_masked ? 0 : (lo >> 4), kb1 = any_masked ? QB - 1 : qb;
+    float o[NDT][4];
+  #pragma unroll
+    for (int nd = 0; nd < NDT; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.0f;
+    float ma = -INFINITY, mb = -INFINITY, la = 0.0f, lb = 0.0f;
+    for (int kb = kb0; kb <= kb1; ++kb) {
+      float sc[2][4];
+  #pragma unroll
+      for (int nh = 0; nh < 2; ++nh) sc[nh][0] = sc[nh][1] = sc[nh][2] = sc[nh][3] = 0.0f;
+      // ldmatrix rows: matrix m = lane / 8 -> keys (m / 2) * 8 + (lane % 8), dims (m % 2) * 8
+      const int koff = (kb * 16 + ((lane >> 4) << 3) + (lane & 7)) * PITCH + ((lane >> 3) & 1) * 8;
+  #pragma unroll
+      for (int kc = 0; kc < NKC; ++kc) {
+        uint32_t h00, h01, h10, h11, l00, l01, l10, l11;  // [key half][dim half]
+        ldsm_x4(Kh + koff + 16 * kc, h00, h01, h10, h11);
+        ldsm_x4(Kl + koff + 16 * kc, l00, l01, l10, l11);
+        mma16816(sc[0][0], sc[0][1], sc[0][2], sc[0][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], h00, h01);
+        mma16816(sc[1][0], sc[1][1], sc[1][2], sc[1][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], h10, h11);
+        mma16816(sc[0][0], sc[0][1], sc[0][2], sc[0][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], l00, l01);
+        mma16816(sc[1][0], sc[1][1], sc[1][2], sc[1][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], l10, l11);
+        mma16816(sc[0][0], sc[0][1], sc[0][2], sc[0][3], ql[kc][0], ql[kc][1], ql[kc][2], ql[kc][3], h00, h01);
+        mma16816(sc[1][0], sc[1][1], sc[1][2], sc[1][3], ql[kc][0], ql[kc][1], ql[kc][2], ql[kc][3], h10, h11);
+      }
+      // scale + masks; e = 0,1: row ia, e = 2,3: row ib
+      float bma = -INFINITY, bmb = -INFINITY;
+  #pragma unroll
+      for (int nh = 0; nh < 2; ++nh)
+  #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int row = e < 2 ? ia : ib;
+          const int key = kb * 16 + nh * 8 + 2 * t + (e & 1);
+          float s = sc[nh][e] * qk_scale;
+          if (row >= p || row < lo)  // padding row / whole-padding query: uniform over the p keys
+            s = key < p ? -1.0e9f : -INFINITY;
+          else if (key < lo || key > row)
+            s = -INFINITY;
+          sc[nh][e] = s;
+          if (e < 2) bma = fmaxf(bma, s); else bmb = fmaxf(bmb, s);
+        }
+      bma = fmaxf(bma, __shfl_xor_sync(0xffffffffu, bma, 1));
+      bma = fmaxf(bma, __shfl_xor_sync(0xffffffffu, bma, 2));
+      bmb = fmaxf(bmb, __shfl_xor_sync(0xffffffffu, bmb, 1));
+      bmb = fmaxf(bmb, __shfl_xor_sync(0xffffffffu, bmb, 2));
+      const float na = fmaxf(ma, bma), nb = fmaxf(mb, bmb);
+      const float ua = na == -INFINITY ? 0.0f : na, ub = nb == -INFINITY ? 0.0f : nb;
+      const float ca = expf(ma - ua), cb = expf(mb - ub);  // rescale of what came before (0 at the start)
+      ma = na;
+      mb = nb;
+      la *= ca;
+      lb *= cb;
+  #pragma unroll
+      for (int nd = 0; nd < NDT; ++nd) {
+        o[nd][0] *= ca, o[nd][1] *= ca;
+        o[nd][2] *= cb, o[nd][3] *= cb;
+      }
+  #pragma unroll
+      for (int nh = 0; nh < 2; ++nh)
+  #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float pe = expf(sc[nh][e] - (e < 2 ? ua : ub));
+          sc[nh][e] = pe;
+          if (e < 2) la += pe; else lb += pe;
+        }
+      // P as the A operand (16 queries x 16 keys of this block), split hi/lo
+      uint32_t ph[4], pl[4];
+      split2(sc[0][0], sc[0][1], ph[0], pl[0]);
+      split2(sc[0][2], sc[0][3], ph[1], pl[1]);
+      split2(sc[1][0], sc[1][1], ph[2], pl[2]);
+      split2(sc[1][2], sc[1][3], ph[3], pl[3]);
+      // transposed ldmatrix rows: matrix m -> keys (m % 2) * 8 + (lane % 8), dims (m / 2) * 8
+      const int voff = (kb * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * PITCH + ((lane >> 4) << 3);
+  #pragma unroll
+      for (int n2 = 0; n2 < NKC; ++n2) {  // dims 16 n2 .. 16 n2 + 15 = n8 blocks 2 n2, 2 n2 + 1
+        uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+        ldsm_x4_trans(Vh + voff + 16 * n2, h0, h1, h2, h3);
+        ldsm_x4_trans(Vl + voff + 16 * n2, l0, l1, l2, l3);
+        float *oa = o[2 * n2], *ob = o[2 * n2 + 1];
+        mma16816(oa[0], oa[1], oa[2], oa[3], ph[0], ph[1], ph[2], ph[3], h0, h1);
+        mma16816(ob[0], ob[1], ob[2], ob[3], ph[0], ph[1], ph[2], ph[3], h2, h3);
+        mma16816(oa[0], oa[1], oa[2], oa[3], ph[0], ph[1], ph[2], ph[3], l0, l1);
+        mma16816(ob[0], ob[1], ob[2], ob[3], ph[0], ph[1], ph[2], ph[3], l2, l3);
+        mma16816(oa[0], oa[1], oa[2], oa[3], pl[0], pl[1], pl[2], pl[3], h0, h1);
+        mma16816(ob[0], ob[1], ob[2], ob[3], pl[0], pl[1], pl[2], pl[3], h2, h3);
+      }
+    }
+    la += __shfl_xor_sync(0xffffffffu, la, 1);
+    la += __shfl_xor_sync(0xffffffffu, la, 2);
+    lb += __shfl_xor_sync(0xffffffffu, lb, 1);
+    lb += __shfl_xor_sync(0xffffffffu, lb, 2);
+    const float inva = 1.0f / la, invb = 1.0f / lb;
+#pragma unroll
+    for (int nd = 0; nd < NDT; ++nd) {
+      const int d = nd * 8 + 2 * t;
+      if (ia < p) {
+        const float x0 = o[nd][0] * inva, x1 = o[nd][1] * inva;
+        const size_t oo = (tok0 + ia) * E + h * HD + d;
+        uint32_t hw, lw;
+        split2(x0, x1, hw, lw);
+        *reinterpret_cast<uint32_t *>(a.oh + oo) = hw;
+        *reinterpret_cast<uint32_t *>(a.ol + oo) = lw;
+        if (a.o32) *reinterpret_cast<float2 *>(a.o32 + oo) = make_float2(x0, x1);
+      }
+      if (ib < p) {
+        const float x0 = o[nd][2] * invb, x1 = o[nd][3] * invb;
+        const size_t oo = (tok0 + ib) * E + h * HD + d;
+        uint32_t hw, lw;
+        split2(x0, x1, hw, lw);
+        *reinterpret_cast<uint32_t *>(a.oh + oo) = hw;
+        *reinterpret_cast<uint32_t *>(a.ol + oo) = lw;
+        if (a.o32) *reinterpret_cast<float2 *>(a.o32 + oo) = make_float2(x0, x1);
+      }
+    }
+  }
+}
+
 // Group attention for one (series, patch): every head (one warp each) over
 // the series' variate rows at that patch (mask.rs:69-82).  Rows whose patch
 // is whole padding are blocked keys; such a query averages V over the
 // series' rows.  q and k get their per-head RMSNorm as they are read (no
 // RoPE on GROUP layers).
+template <int HD>
 __global__ void __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
   pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
+  constexpr int DPL = HD / 32;  // dims per lane: lane + 32 c
   const int s = blockIdx.x, patch = blockIdx.y;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (h >= a.H) return;
   const int r0 = a.series_row0[s], nv = a.series_nrows[s];
   const int p = a.p, E = a.E;
-  const float qg0 = a.qn[lane], qg1 = a.qn[lane + 32], kg0 = a.kn[lane], kg1 = a.kn[lane + 32];
+  const float qk_scale = 1.0f / sqrtf((float)HD);
+  float qg[DPL], kg[DPL];
+#pragma unroll
+  for (int c = 0; c < DPL; ++c) qg[c] = a.qn[lane + 32 * c], kg[c] = a.kn[lane + 32 * c];
+  // the normalised key of row kb, this lane's dims
+  auto key = [&](int kb, float *kv) {
+    const float *krow = a.qkv + ((size_t)(r0 + kb) * p + patch) * 3 * E + E + h * HD;
+    float sk = 0.0f;
+#pragma unroll
+    for (int c = 0; c < DPL; ++c) kv[c] = krow[lane + 32 * c], sk += kv[c] * kv[c];
+    const float rdn = 1.0f / sqrtf(warp_sum(sk) / (float)HD + 1e-8f);
+#pragma unroll
+    for (int c = 0; c < DPL; ++c) kv[c] = kv[c] * rdn * kg[c];
+  };
   for (int qa = 0; qa < nv; ++qa) {
     const size_t tq = (size_t)(r0 + qa) * p + patch;
-    const float *qrow = a.qkv + tq * 3 * E + h * 64;
-    float q0 = qrow[lane], q1 = qrow[lane + 32];
-    {
-      const float rdn = 1.0f / sqrtf(warp_sum(q0 * q0 + q1 * q1) / 64.0f + 1e-8f);
-      q0 = q0 * rdn * qg0;
-      q1 = q1 * rdn * qg1;
-    }
+    const float *qrow = a.qkv + tq * 3 * E + h * HD;
+    float q[DPL], sq = 0.0f;
+#pragma unroll
+    for (int c = 0; c < DPL; ++c) q[c] = qrow[lane + 32 * c], sq += q[c] * q[c];
+    const float rq = 1.0f / sqrtf(warp_sum(sq) / (float)HD + 1e-8f);
+#pragma unroll
+    for (int c = 0; c < DPL; ++c) q[c] = q[c] * rq * qg[c];
     const bool qmasked = patch < a.row_first_valid[r0 + qa];
-    // two passes over keys: max, then exp-sum and output (nv is small)
+    // two passes over keys: max, then exp-sum and output
     float mx = -INFINITY;
     for (int kb = 0; kb < nv; ++kb) {
       const bool kvalid = patch >= a.row_first_valid[r0 + kb];
-      const size_t tk = (size_t)(r0 + kb) * p + patch;
-      const float *krow = a.qkv + tk * 3 * E + E + h * 64;
-      const float k0 = krow[lane], k1 = krow[lane + 32];
-      const float rdn = 1.0f / sqrtf(warp_sum(k0 * k0 + k1 * k1) / 64.0f + 1e-8f);
-      const float d = warp_sum(q0 * (k0 * rdn * kg0) + q1 * (k1 * rdn * kg1));
-      float sc = qmasked ? -1.0e9f : (kvalid ? d * 0.125f : -INFINITY);
-      mx = fmaxf(mx, sc);
+      float kv[DPL], dp = 0.0f;
+      key(kb, kv);
+#pragma unroll
+      for (int c = 0; c < DPL; ++c) dp += q[c] * kv[c];
+      const float d = warp_sum(dp);
+      mx = fmaxf(mx, qmasked ? -1.0e9f : (kvalid ? d * qk_scale : -INFINITY));
     }
-    float sum = 0.0f, o0 = 0.0f, o1 = 0.0f;
+    float sum = 0.0f, o[DPL];
+#pragma unroll
+    for (int c = 0; c < DPL; ++c) o[c] = 0.0f;
     for (int kb = 0; kb < nv; ++kb) {
       const bool kvalid = patch >= a.row_first_valid[r0 + kb];
-      const size_t tk = (size_t)(r0 + kb) * p + patch;
-      const float *krow = a.qkv + tk * 3 * E + E + h * 64;
-      const float k0 = krow[lane], k1 = krow[lane + 32];
-      const float rdn = 1.0f / sqrtf(warp_sum(k0 * k0 + k1 * k1) / 64.0f + 1e-8f);
-      const float d = warp_sum(q0 * (k0 * rdn * kg0) + q1 * (k1 * rdn * kg1));
-      float sc = qmasked ? -1.0e9f : (kvalid ? d * 0.125f : -INFINITY);
-      float e = expf(sc - mx);
+      float kv[DPL], dp = 0.0f;
+      key(kb, kv);
+#pragma unroll
+      for (int c = 0; c < DPL; ++c) dp += q[c] * kv[c];
+      const float d = warp_sum(dp);
+      const float e = expf((qmasked ? -1.0e9f : (kvalid ? d * qk_scale : -INFINITY)) - mx);
       sum += e;
-      const float *vrow = a.qkv + tk * 3 * E + 2 * E + h * 64;
-      o0 = fmaf(e, vrow[lane], o0);
-      o1 = fmaf(e, vrow[lane + 32], o1);
+      const float *vrow = a.qkv + ((size_t)(r0 + kb) * p + patch) * 3 * E + 2 * E + h * HD;
+#pragma unroll
+      for (int c = 0; c < DPL; ++c) o[c] = fmaf(e, vrow[lane + 32 * c], o[c]);
     }
-    o0 = o0 / sum;
-    o1 = o1 / sum;
-    const size_t oo = tq * E + h * 64;
-    __half hh, ll;
-    split_f16(o0, hh, ll);
-    a.oh[oo + lane] = hh;
-    a.ol[oo + lane] = ll;
-    split_f16(o1, hh, ll);
-    a.oh[oo + lane + 32] = hh;
-    a.ol[oo + lane + 32] = ll;
-    if (a.o32) {
-      a.o32[oo + lane] = o0;
-      a.o32[oo + lane + 32] = o1;
+    const size_t oo = tq * E + h * HD;
+#pragma unroll
+    for (int c = 0; c < DPL; ++c) {
+      const float x = o[c] / sum;
+      __half hh, ll;
+      split_f16(x, hh, ll);
+      a.oh[oo + lane + 32 * c] = hh;
+      a.ol[oo + lane + 32 * c] = ll;
+      if (a.o32) a.o32[oo + lane + 32 * c] = x;
     }
   }
 }
@@ -1060,40 +1345,49 @@ __global__ void __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
 // warp per head loads k and v of all NV (>= the series' row count) variate
 // rows at this patch with independent loads, normalises the keys once, then
 // answers every query row (same semantics as attn_group_kernel).
-template <int NV>
+template <int NV, int HD>
 __global__ void __launch_bounds__(256) attn_group_reg_kernel(AttnArgs a) {
   pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
+  constexpr int DPL = HD / 32;  // dims per lane: lane + 32 c
   const int s = blockIdx.x, patch = blockIdx.y;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (h >= a.H) return;
   const int r0 = a.series_row0[s], nv = a.series_nrows[s];
   const int p = a.p, E = a.E;
-  float q0[NV], q1[NV], k0[NV], k1[NV], v0[NV], v1[NV];
+  const float qk_scale = 1.0f / sqrtf((float)HD);
+  float q[NV][DPL], k[NV][DPL], v[NV][DPL];
   uint32_t kvalid = 0;
 #pragma unroll
   for (int b = 0; b < NV; ++b) {
-    q0[b] = q1[b] = k0[b] = k1[b] = v0[b] = v1[b] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < DPL; ++c) q[b][c] = k[b][c] = v[b][c] = 0.0f;
     if (b < nv) {
-      const float *row = a.qkv + ((size_t)(r0 + b) * p + patch) * 3 * E + h * 64;
-      q0[b] = row[lane];
-      q1[b] = row[lane + 32];
-      k0[b] = row[E + lane];
-      k1[b] = row[E + lane + 32];
-      v0[b] = row[2 * E + lane];
-      v1[b] = row[2 * E + lane + 32];
+      const float *row = a.qkv + ((size_t)(r0 + b) * p + patch) * 3 * E + h * HD;
+#pragma unroll
+      for (int c = 0; c < DPL; ++c) {
+        q[b][c] = row[lane + 32 * c];
+        k[b][c] = row[E + lane + 32 * c];
+        v[b][c] = row[2 * E + lane + 32 * c];
+      }
       if (patch >= a.row_first_valid[r0 + b]) kvalid |= 1u << b;
     }
   }
-  const float qg0 = a.qn[lane], qg1 = a.qn[lane + 32], kg0 = a.kn[lane], kg1 = a.kn[lane + 32];
+  float qg[DPL], kg[DPL];
+#pragma unroll
+  for (int c = 0; c < DPL; ++c) qg[c] = a.qn[lane + 32 * c], kg[c] = a.kn[lane + 32 * c];
 #pragma unroll
   for (int b = 0; b < NV; ++b) {
     if (b < nv) {
-      const float rk = 1.0f / sqrtf(warp_sum(k0[b] * k0[b] + k1[b] * k1[b]) / 64.0f + 1e-8f);
-      k0[b] = k0[b] * rk * kg0;
-      k1[b] = k1[b] * rk * kg1;
-      const float rq = 1.0f / sqrtf(warp_sum(q0[b] * q0[b] + q1[b] * q1[b]) / 64.0f + 1e-8f);
-      q0[b] = q0[b] * rq * qg0;
-      q1[b] = q1[b] * rq * qg1;
+      float sk = k[b][0] * k[b][0], sq = q[b][0] * q[b][0];
+#pragma unroll
+      for (int c = 1; c < DPL; ++c) sk += k[b][c] * k[b][c], sq += q[b][c] * q[b][c];
+      const float rk = 1.0f / sqrtf(warp_sum(sk) / (float)HD + 1e-8f);
+      const float rq = 1.0f / sqrtf(warp_sum(sq) / (float)HD + 1e-8f);
+#pragma unroll
+      for (int c = 0; c < DPL; ++c) {
+        k[b][c] = k[b][c] * rk * kg[c];
+        q[b][c] = q[b][c] * rq * qg[c];
+      }
     }
   }
 #pragma unroll
@@ -1106,34 +1400,35 @@ __global__ void __launch_bounds__(256) attn_group_reg_kernel(AttnArgs a) {
     for (int b = 0; b < NV; ++b) {
       sc[b] = -INFINITY;
       if (b < nv) {
-        const float d = warp_sum(q0[qa] * k0[b] + q1[qa] * k1[b]);
-        sc[b] = qmasked ? -1.0e9f : (((kvalid >> b) & 1u) ? d * 0.125f : -INFINITY);
+        float dp = q[qa][0] * k[b][0];
+#pragma unroll
+        for (int c = 1; c < DPL; ++c) dp += q[qa][c] * k[b][c];
+        const float d = warp_sum(dp);
+        sc[b] = qmasked ? -1.0e9f : (((kvalid >> b) & 1u) ? d * qk_scale : -INFINITY);
         mx = fmaxf(mx, sc[b]);
       }
     }
-    float sum = 0.0f, o0 = 0.0f, o1 = 0.0f;
+    float sum = 0.0f, o[DPL];
+#pragma unroll
+    for (int c = 0; c < DPL; ++c) o[c] = 0.0f;
 #pragma unroll
     for (int b = 0; b < NV; ++b) {
       if (b < nv) {
         const float e = expf(sc[b] - mx);
         sum += e;
-        o0 = fmaf(e, v0[b], o0);
-        o1 = fmaf(e, v1[b], o1);
+#pragma unroll
+        for (int c = 0; c < DPL; ++c) o[c] = fmaf(e, v[b][c], o[c]);
       }
     }
-    o0 = o0 / sum;
-    o1 = o1 / sum;
-    const size_t oo = ((size_t)(r0 + qa) * p + patch) * E + h * 64;
-    __half hh, ll;
-    split_f16(o0, hh, ll);
-    a.oh[oo + lane] = hh;
-    a.ol[oo + lane] = ll;
-    split_f16(o1, hh, ll);
-    a.oh[oo + lane + 32] = hh;
-    a.ol[oo + lane + 32] = ll;
-    if (a.o32) {
-      a.o32[oo + lane] = o0;
-      a.o32[oo + lane + 32] = o1;
+    const size_t oo = ((size_t)(r0 + qa) * p + patch) * E + h * HD;
+#pragma unroll
+    for (int c = 0; c < DPL; ++c) {
+      const float x = o[c] / sum;
+      __half hh, ll;
+      split_f16(x, hh, ll);
+      a.oh[oo + lane + 32 * c] = hh;
+      a.ol[oo + lane + 32 * c] = ll;
+      if (a.o32) a.o32[oo + lane + 32 * c] = x;
     }
   }
 }
@@ -1258,6 +1553,16 @@ cudaError_t t0b_launch_resid_split(float *x, const float *y, const float *g, __h
   return cudaGetLastError();
 }
 cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
+  if (a.E / a.H == 128) {
+    if (a.p > kAttnWideMaxP) return cudaErrorInvalidValue;
+    const int QB = (a.p + 15) / 16, PK = 16 * QB;
+    const size_t smem = (size_t)(4 * PK * (128 + 8)) * sizeof(__half);
+    cudaError_t e = t0b_smem_limit((const void *)attn_time_wide_kernel<128>, smem);
+    if (e != cudaSuccess) return e;
+    attn_time_wide_kernel<128><<<dim3(a.R, a.H), 32 * (QB < 8 ? QB : 8), smem, st>>>(a);
+    return cudaGetLastError();
+  }
+  if (a.E / a.H != 64) return cudaErrorInvalidValue;
   if (a.p <= kAttnMmaMaxP) {
     const int QB = (a.p + 15) / 16, PK = 16 * QB;
     const size_t smem = (size_t)(4 * PK * 72) * sizeof(__half);
@@ -1282,18 +1587,21 @@ cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
   attn_time_kernel<<<grid, 128, smem, st>>>(a);
   return cudaGetLastError();
 }
-cudaError_t t0b_launch_attn_group(const AttnArgs &a, cudaStream_t st) {
+template <int HD>
+static cudaError_t launch_attn_group_hd(const AttnArgs &a, cudaStream_t st) {
   dim3 grid(a.n_series, a.p);
-  if (a.max_nrows <= 8) {
-    attn_group_reg_kernel<8><<<grid, 32 * a.H, 0, st>>>(a);
-    return cudaGetLastError();
-  }
-  if (a.max_nrows <= 16) {
-    attn_group_reg_kernel<16><<<grid, 32 * a.H, 0, st>>>(a);
-    return cudaGetLastError();
-  }
-  attn_group_kernel<<<grid, 32 * a.H, 0, st>>>(a);
+  if (a.max_nrows <= 8)
+    attn_group_reg_kernel<8, HD><<<grid, 32 * a.H, 0, st>>>(a);
+  else if (a.max_nrows <= 16)
+    attn_group_reg_kernel<16, HD><<<grid, 32 * a.H, 0, st>>>(a);
+  else
+    attn_group_kernel<HD><<<grid, 32 * a.H, 0, st>>>(a);
   return cudaGetLastError();
+}
+cudaError_t t0b_launch_attn_group(const AttnArgs &a, cudaStream_t st) {
+  if (a.E / a.H == 128) return launch_attn_group_hd<128>(a, st);
+  if (a.E / a.H == 64) return launch_attn_group_hd<64>(a, st);
+  return cudaErrorInvalidValue;
 }
 cudaError_t t0b_launch_dec_gather(const float *x, const float *g, float *xo, int R, int p, int hp, int E,
                                   cudaStream_t st) {

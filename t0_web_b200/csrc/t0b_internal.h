@@ -44,12 +44,13 @@ struct AttnArgs {
   float *o32;        // optional f32 output
   const int *row_first_valid;  // whole-padding patches at the start of each row
   const int *series_row0, *series_nrows;
-  // per-head QK RMSNorm gains [64] (eps 1e-8, ops.rs:175-177), applied to q
+  // per-head QK RMSNorm gains [hd] (eps 1e-8, ops.rs:175-177), applied to q
   // and k as they are read; on TIME layers (use_rope) then xpos RoPE with the
-  // tables rope = [4][p][64]: cos, sin, scale, 1/scale (k uses 1/scale).
+  // tables rope = [4][p][hd]: cos, sin, scale, 1/scale (k uses 1/scale).
+  // hd = E / H is 64 or 128.
   const float *qn, *kn, *rope;
-  // the same tables without duplicates, [p][128]: cos[32], sin[32] per
-  // rotated pair, scale[32], 1/scale[32] per dim mod 32
+  // the same tables without duplicates, [p][2 hd]: cos[hd/2], sin[hd/2] per
+  // rotated pair, scale[hd/2], 1/scale[hd/2] per dim mod hd/2
   const float *rope_c;
   int use_rope;
   int R, p, E, H, n_series;

@@ -311,8 +311,8 @@ t0b_status parse_config(const t0b::GgufFile &f, t0b_model *m) {
   const int gen = I.group_every_n;
   m->L = gen > 0 ? (I.num_layers / gen) * gen : I.num_layers;
   if (m->P != 32) return fail(T0B_ERR_UNSUPPORTED, "t0b: patch_size must be 32");
-  if (m->H <= 0 || m->E % m->H || m->E / m->H != 64)
-    return fail(T0B_ERR_UNSUPPORTED, "t0b: head_dim must be 64 (embed_dim / num_heads)");
+  if (m->H <= 0 || m->E % m->H || (m->E / m->H != 64 && m->E / m->H != 128))
+    return fail(T0B_ERR_UNSUPPORTED, "t0b: head_dim (embed_dim / num_heads) must be 64 or 128");
   if (m->E % 256 || m->F % 256)
     return fail(T0B_ERR_UNSUPPORTED, "t0b: embed_dim and mlp_hidden_dim must be multiples of 256");
   if (m->H > 8) return fail(T0B_ERR_UNSUPPORTED, "t0b: at most 8 heads");
@@ -420,8 +420,8 @@ t0b_status upload_all(t0b_model *m, const t0b::GgufFile &f) {
     UP(p + ".mlp.2.bias", w.b2, (size_t)E);
     UP(p + ".attention_block.norm.scale", w.g_attn, (size_t)E);
     UP(p + ".norm.scale", w.g_mlp, (size_t)E);
-    UP(p + ".attention_block.attention.q_norm.scale", w.qn, (size_t)64);
-    UP(p + ".attention_block.attention.k_norm.scale", w.kn, (size_t)64);
+    UP(p + ".attention_block.attention.q_norm.scale", w.qn, (size_t)(E / m->H));
+    UP(p + ".attention_block.attention.k_norm.scale", w.kn, (size_t)(E / m->H));
     m->layers.push_back(w);
   }
 #undef UP
@@ -435,9 +435,9 @@ t0b_status rope_tables(t0b_model *m, int p, const float **out) {
     *out = it->second;
     return T0B_OK;
   }
-  const int hd = 64, half = 32;
-  // [4][p][hd] full tables, then the [p][128] compact copy
-  std::vector<float> h((size_t)4 * p * hd + (size_t)p * 128);
+  const int hd = m->E / m->H, half = hd / 2;
+  // [4][p][hd] full tables, then the [p][2 hd] compact copy
+  std::vector<float> h((size_t)4 * p * hd + (size_t)p * 2 * hd);
   float *cs = h.data(), *sn = cs + (size_t)p * hd, *sc = sn + (size_t)p * hd, *si = sc + (size_t)p * hd;
   const double theta = 10000.0, base512 = 512.0;
   const double max_half = std::floor((double)(p - 1) / 2.0);
@@ -457,10 +457,10 @@ t0b_status rope_tables(t0b_model *m, int p, const float **out) {
   float *cc = si + (size_t)p * hd;
   for (int pos = 0; pos < p; ++pos)
     for (int j = 0; j < half; ++j) {
-      cc[pos * 128 + j] = cs[pos * hd + 2 * j];
-      cc[pos * 128 + 32 + j] = sn[pos * hd + 2 * j];
-      cc[pos * 128 + 64 + j] = sc[pos * hd + j];
-      cc[pos * 128 + 96 + j] = si[pos * hd + j];
+      cc[pos * 2 * hd + j] = cs[pos * hd + 2 * j];
+      cc[pos * 2 * hd + half + j] = sn[pos * hd + 2 * j];
+      cc[pos * 2 * hd + 2 * half + j] = sc[pos * hd + j];
+      cc[pos * 2 * hd + 3 * half + j] = si[pos * hd + j];
     }
   float *d = nullptr;
   if (cudaMalloc(&d, h.size() * 4) != cudaSuccess) return fail(T0B_ERR_OOM, "t0b: out of device memory");
@@ -747,7 +747,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   aa.max_nrows = ps.s_nrows.empty() ? 0 : *std::max_element(ps.s_nrows.begin(), ps.s_nrows.end());
   const int M = (int)T;
   aa.rope = rope;
-  aa.rope_c = rope + (size_t)4 * p * 64;
+  aa.rope_c = rope + (size_t)4 * p * (E / m->H);  // after the [4][p][hd] full tables
 
   for (int l = 0; l < m->L; ++l) {
     const LayerW &w = m->layers[l];
@@ -771,7 +771,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
       LAUNCH(launch(m, KC_ATTN_GROUP, 0.0, T * (3.0 * E * 4 + E * 4.0), [&] { return t0b_launch_attn_group(aa, m->stream); }));
     } else {
       // causal pairs per row: p(p+1)/2, each 2*hd flops for q.k and 2*hd for p.v, per head
-      const double fl = (double)R * m->H * (p * (p + 1) / 2.0) * 4.0 * 64.0;
+      const double fl = (double)R * m->H * (p * (p + 1) / 2.0) * 4.0 * (E / m->H);
       LAUNCH(launch(m, KC_ATTN_TIME, fl, T * (3.0 * E * 4 + E * 4.0), [&] { return t0b_launch_attn_time(aa, m->stream); }));
     }
     // the q|k|v buffer is free again: it holds the residual branch outputs
@@ -895,6 +895,8 @@ t0b_status run_series(t0b_model *m, const float *ctx_dev, const std::vector<RowS
                       size_t max_rows_hint) {
   const int hpad = (horizon + 31) / 32 * 32;
   const int p = (ctx_w + hpad) / 32, hp = hpad / 32;
+  if (m->E / m->H == 128 && p > 192)
+    return fail(T0B_ERR_UNSUPPORTED, "t0b: 128-dim heads run at most 192 patches per row (context + horizon)");
   size_t max_rows = std::max<size_t>(1, m->max_tokens / (size_t)p);
   if (max_rows_hint) max_rows = std::min(max_rows, max_rows_hint);
   size_t s = 0, row = 0;

@@ -33,7 +33,17 @@ ALPHA = dict(
     scaler_eps_mode="variance_offset",
 )
 
-# The smallest model of the same family the engine runs (head_dim 64,
+# t0-beta's shape (the reference's docs/BENCHMARKS.md:340): embed_dim 1024
+# (head_dim 128), 21 quantile levels, `std_clamp` scaler with eps 0.01; the
+# other fields as t0-alpha.  The 21 levels are 0.01, 0.05, 0.10, ..., 0.95,
+# 0.99 (the documented range; the exact list is this project's choice).
+BETA = dict(ALPHA, embed_dim=1024,
+            quantile_levels=[0.01] + [round(0.05 * i, 2) for i in range(1, 20)] + [0.99],
+            scaler_eps=0.01, scaler_eps_mode="std_clamp")
+# a 3-layer (TIME, TIME, GROUP) model of t0-beta's widths, for parity tests
+BETA_SMALL = dict(BETA, num_layers=3)
+
+# The smallest model of the same family the engine runs (head_dim 64 or 128,
 # embed_dim and mlp_hidden_dim multiples of 256): quick CPU checks and fixtures.
 TINY = dict(ALPHA, embed_dim=256, num_layers=3, num_heads=4, mlp_hidden_dim=256)
 

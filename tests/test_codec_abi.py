@@ -193,6 +193,16 @@ def test_validate_alpha_quantizable_bytes(gguf_bytes, quant, expected):
     assert (info.embed_dim, info.num_layers, info.mlp_hidden_dim) == (512, 24, 2048)
 
 
+def test_validate_info_beta_shape():
+    """t0-beta's config fields (embed_dim 1024 -> head_dim 128, 21 levels,
+    std_clamp scaler with eps 0.01) come through the metadata."""
+    info = gguf.validate(gguf.export_gguf(S.random_weights(S.BETA_SMALL, seed=2), S.BETA_SMALL, "q4_0"))
+    assert (info.embed_dim, info.num_heads, info.num_layers, info.n_quantiles) == (1024, 8, 3, 21)
+    assert info.variance_offset == 0 and abs(info.scaler_eps - 0.01) < 1e-9
+    assert np.allclose(list(info.quantile_levels)[:21], S.BETA["quantile_levels"], atol=1e-7)
+    assert info.weight_type == Q4_0
+
+
 @pytest.fixture(scope="module")
 def tiny_q8():
     return gguf.export_gguf(S.random_weights(S.TINY, seed=4), S.TINY, "q8_0")
@@ -236,9 +246,9 @@ def test_validate_rejects_wrong_shape():
 
 def test_validate_unsupported_shapes_and_types():
     """Files that are well-formed but outside what this engine runs give
-    T0B_ERR_UNSUPPORTED: head_dim != 64, and f16 big matmuls (the engine
-    keeps only Q8_0/Q4_0 weights resident)."""
-    cfg = dict(S.TINY, num_heads=2)
+    T0B_ERR_UNSUPPORTED: head_dim other than 64 and 128, and f16 big matmuls
+    (the engine keeps only Q8_0/Q4_0 weights resident)."""
+    cfg = dict(S.TINY, num_heads=1)
     with pytest.raises(T0bError) as ei:
         gguf.validate(gguf.export_gguf(S.random_weights(cfg, seed=1), cfg, "q8_0"))
     assert ei.value.status == _lib.T0B_ERR_UNSUPPORTED
