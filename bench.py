@@ -42,6 +42,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--quant", default="q8_0", choices=["q8_0", "q4_0"])
+    ap.add_argument("--model", default="alpha", choices=["alpha", "beta"],
+                    help="t0-alpha shape (default, the headline) or t0-beta shape (embed_dim 1024, head_dim 128, "
+                         "21 quantiles); random-init weights either way")
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--series", type=int, default=8192)
     ap.add_argument("--horizon", type=int, default=96)
@@ -82,7 +85,7 @@ def config_block(args, nv, world):
                      f"{'v~U{' + args.variates.replace('-', '..') + '}' if '-' in args.variates else 'v=' + args.variates}"
                      f", seed {args.seed}"
                      f"{'' if args.strong else ' + rank'}), ctx {args.ctx}, horizon {args.horizon}, "
-                     f"t0-alpha shape random-init weights as {args.quant.upper()} GGUF"),
+                     f"t0-{args.model} shape random-init weights as {args.quant.upper()} GGUF"),
         "series": args.series, "series_total": args.series * (1 if args.strong else world),
         "rows": rows, "patches_per_row": p, "tokens": rows * p,
         "ctx": args.ctx, "horizon": args.horizon, "quant": args.quant,
@@ -173,8 +176,16 @@ def measured_peaks():
         return 1400.0, 6650.0, "fallback"
 
 
-def committed_traffic(quant):
-    """DRAM bytes per gemm_tc launch from the committed ncu summary, if any."""
+def model_cfg(args):
+    from t0_web_b200 import synthetic as S
+    return S.BETA if getattr(args, "model", "alpha") == "beta" else S.ALPHA
+
+
+def committed_traffic(quant, model="alpha"):
+    """DRAM bytes per gemm_tc launch from the committed ncu summary (t0-alpha
+    shapes only), if any."""
+    if model != "alpha":
+        return None
     try:
         with open(os.path.join(ROOT, "profiles", "gemm_tc_traffic.json")) as f:
             return json.load(f).get(quant)
@@ -198,8 +209,9 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
 
-    weights = S.random_weights(S.ALPHA, seed=0)
-    gbytes = gguf.export_gguf(weights, S.ALPHA, args.quant)
+    cfg = model_cfg(args)
+    weights = S.random_weights(cfg, seed=0)
+    gbytes = gguf.export_gguf(weights, cfg, args.quant)
     del weights
     # weak scaling: every rank its own series; strong: one set split across ranks
     ctx, nv = workload(args, args.seed if args.strong else args.seed + rank)
@@ -313,7 +325,7 @@ def run_ours(args):
     if g.get("launches"):
         per_launch_ms = g["total_ms"] / g["launches"]
         achieved = g["flops"] / (g["total_ms"] / 1e3) / 1e12
-        tr = committed_traffic(args.quant)
+        tr = committed_traffic(args.quant, args.model)
         if tr:  # per-token DRAM bytes of one launch (ncu) x this run's tokens per launch
             n_gemm = 4 * model.info.num_layers
             tok_per_launch = (int(nv_shard.sum()) * config_block(args, nv, world)["patches_per_row"] * n_gemm
@@ -363,8 +375,9 @@ def run_single(args):
 
     from t0_web_b200 import gguf, synthetic as S, t0_fast
     quant = args.quant
-    weights = S.random_weights(S.ALPHA, seed=0)
-    gbytes = gguf.export_gguf(weights, S.ALPHA, quant)
+    cfg = model_cfg(args)
+    weights = S.random_weights(cfg, seed=0)
+    gbytes = gguf.export_gguf(weights, cfg, quant)
     del weights
     engine = t0_fast.Engine(0)
     model = t0_fast.load_model_from_gguf(engine, gbytes)
@@ -399,7 +412,7 @@ def run_single(args):
     n = nsteps
     print(json.dumps({"metric": "single forecast latency (ctx 512, h 96, univariate)", "value": float(np.median(times)),
                       "unit": "ms", "higher_is_better": False, "n_gpus": 1, "steps": n, "dtype": "f32",
-                      "data": "synthetic", "config": {"workload": f"cfg1 sine context, t0-alpha random-init {quant}",
+                      "data": "synthetic", "config": {"workload": f"cfg1 sine context, t0-{args.model} random-init {quant}",
                                                       "tokens_per_gemm": 19},
                       "eager_launch_ms": float(np.median(eager)),
                       "device_ms_per_forecast": sum(v["total_ms"] for v in prof.values()) / n,
@@ -532,8 +545,9 @@ def run_reference(args):
     if rank != 0:
         return
     from t0_web_b200 import gguf, synthetic as S
-    weights = S.random_weights(S.ALPHA, seed=0)
-    gbytes = gguf.export_gguf(weights, S.ALPHA, args.quant)
+    cfg = model_cfg(args)
+    weights = S.random_weights(cfg, seed=0)
+    gbytes = gguf.export_gguf(weights, cfg, args.quant)
     del weights
     ctx, nv = workload(args, args.seed)
     th = cpu_threads()
