@@ -93,8 +93,7 @@ struct TcParams {
 // 16 columns of (main + correction) accumulator for this thread's row.
 T0B_DEV void tmem_ld_pair16(uint32_t taddr, float *v, float scale) {
   float c[16];
-  tmem_ld16(taddr, v);
-  tmem_ld16(taddr + BN, c);
+  tmem_ld16x2(taddr, taddr + BN, v, c);
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = (v[i] + c[i]) * scale;
 }
@@ -402,6 +401,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // no early exit: every epilogue thread runs every iteration so the
       // named barrier above always sees all 512 of them (after an abort the
       // waits return at once and no work is done)
+      // TMEM is released as soon as this thread's last columns are in
+      // registers, so the next tile's MMAs overlap the last chunk's stores
+      bool released = false;
+      auto release = [&] {
+        tc_fence_before();
+        mbar_arrive(acc_empty);  // TMEM is free for the next tile's MMAs
+        released = true;
+      };
       if (have) {
         if (swiglu) {
 #pragma unroll 1
@@ -410,6 +417,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             float gv[16], uv[16];
             tmem_ld_pair16(trow + g0, gv, sc);
             tmem_ld_pair16(trow + 128 + g0, uv, sc);
+            if (c == 1) release();
             uint32_t h[8], l[8];
 #pragma unroll
             for (int i = 0; i < 16; i += 2) {
@@ -453,6 +461,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int c0 = 64 * quarter + 16 * c;
             float v[16];
             tmem_ld_pair16(trow + c0, v, sc);
+            if (c == 3) release();
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] += sb[c0 + i];
             if (lane == 0) bulk_wait_read0();  // the previous chunk has left the staging buffer
@@ -471,8 +480,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(acc_empty);  // TMEM is free for the next tile's MMAs
+      if (!released) release();
     }
     if (lane == 0) bulk_wait_all();  // stores complete before the CTA exits
   }
