@@ -1341,6 +1341,190 @@ __global__ void __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
   }
 }
 
+// Group attention on the tensor cores, 64-dim heads, up to 16 variate rows
+// per series: one warp per head of one (series, patch).  The rows are the 16
+// MMA rows (queries) and the 16 keys of the tile, padded with zeros; scores
+// Q.K^T and P.V use the split-f16 three-term products of the time attention
+// (f32-class), the softmax runs on the score fragments.  Semantics as
+// attn_group_kernel (mask.rs:69-82).
+template <int NT>  // key / query tiles of 8 rows: 1 (up to 8 variates) or 2 (up to 16)
+__global__ void __launch_bounds__(256, NT == 1 ? 3 : 2) attn_group_mma_kernel(AttnArgs a) {
+  pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
+  __shared__ __align__(16) __half vs[8][2][16 * 72];  // per warp: v rows as f16 hi / lo planes
+  const int s = blockIdx.x, patch = blockIdx.y;
+  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (h >= a.H) return;
+  const int g = lane >> 2, t = lane & 3;
+  const int r0 = a.series_row0[s], nv = a.series_nrows[s];
+  const int p = a.p, E = a.E;
+  // per row (g, then g + 8) and its dims 16 kc + {2t, 2t+1, 2t+8, 2t+9}:
+  // QK-norm (the quad t = 0..3 holds the row's 64 dims), then the q / k
+  // mma fragments and the v row into this warp's shared planes
+  uint32_t qh[4][4], ql[4][4], kh[4][4], kl[4][4];
+  bool valid[2] = {false, false};
+#pragma unroll
+  for (int kc = 0; kc < 4; ++kc)
+#pragma unroll
+    for (int x = 0; x < 4; ++x) qh[kc][x] = ql[kc][x] = kh[kc][x] = kl[kc][x] = 0u;  // rows >= 8 NT: zero
+#pragma unroll
+  for (int hr = 0; hr < NT; ++hr) {
+    const int b = g + 8 * hr;
+    const bool in = b < nv;
+    valid[hr] = in && patch >= a.row_first_valid[r0 + min(b, nv - 1)];
+    const float *row = a.qkv + ((size_t)(r0 + min(b, nv - 1)) * p + patch) * 3 * E + h * 64;
+    float q[16], k[16];
+    __half *vh = vs[h][0] + b * 72, *vl = vs[h][1] + b * 72;
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int d = 16 * kc + 2 * t + 8 * u;
+        const float2 qq = *reinterpret_cast<const float2 *>(row + d);
+        const float2 kk = *reinterpret_cast<const float2 *>(row + E + d);
+        const float2 vv = *reinterpret_cast<const float2 *>(row + 2 * E + d);
+        q[4 * kc + 2 * u] = in ? qq.x : 0.0f, q[4 * kc + 2 * u + 1] = in ? qq.y : 0.0f;
+        k[4 * kc + 2 * u] = in ? kk.x : 0.0f, k[4 * kc + 2 * u + 1] = in ? kk.y : 0.0f;
+        uint32_t hw, lw;
+        split2(in ? vv.x : 0.0f, in ? vv.y : 0.0f, hw, lw);
+        *reinterpret_cast<uint32_t *>(vh + d) = hw;
+        *reinterpret_cast<uint32_t *>(vl + d) = lw;
+      }
+    float sq = 0.0f, sk = 0.0f;
+#pragma unroll
+    for (int x = 0; x < 16; ++x) sq += q[x] * q[x], sk += k[x] * k[x];
+    sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+    sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+    sk += __shfl_xor_sync(0xffffffffu, sk, 1);
+    sk += __shfl_xor_sync(0xffffffffu, sk, 2);
+    const float rq = 1.0f / sqrtf(sq / 64.0f + 1e-8f), rk = 1.0f / sqrtf(sk / 64.0f + 1e-8f);
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {
+      const float2 gq0 = *reinterpret_cast<const float2 *>(a.qn + 16 * kc + 2 * t);
+      const float2 gq1 = *reinterpret_cast<const float2 *>(a.qn + 16 * kc + 2 * t + 8);
+      const float2 gk0 = *reinterpret_cast<const float2 *>(a.kn + 16 * kc + 2 * t);
+      const float2 gk1 = *reinterpret_cast<const float2 *>(a.kn + 16 * kc + 2 * t + 8);
+      const float gq[4] = {gq0.x, gq0.y, gq1.x, gq1.y}, gk[4] = {gk0.x, gk0.y, gk1.x, gk1.y};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        q[4 * kc + e] = q[4 * kc + e] * rq * gq[e];
+        k[4 * kc + e] = k[4 * kc + e] * rk * gk[e];
+      }
+      // A fragment (queries): regs 0/2 row g, 1/3 row g + 8; B fragment of key
+      // tile hr (keys 8 hr + g): regs 2 hr (dims 2t..) and 2 hr + 1 (dims 2t+8..)
+      split2(q[4 * kc], q[4 * kc + 1], qh[kc][hr], ql[kc][hr]);
+      split2(q[4 * kc + 2], q[4 * kc + 3], qh[kc][2 + hr], ql[kc][2 + hr]);
+      split2(k[4 * kc], k[4 * kc + 1], kh[kc][2 * hr], kl[kc][2 * hr]);
+      split2(k[4 * kc + 2], k[4 * kc + 3], kh[kc][2 * hr + 1], kl[kc][2 * hr + 1]);
+    }
+  }
+  if (NT == 1) {  // keys 8-15 enter P.V with P = 0: their v rows must be finite
+    __half *vh = vs[h][0] + (g + 8) * 72, *vl = vs[h][1] + (g + 8) * 72;
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        *reinterpret_cast<uint32_t *>(vh + 16 * kc + 2 * t + 8 * u) = 0u;
+        *reinterpret_cast<uint32_t *>(vl + 16 * kc + 2 * t + 8 * u) = 0u;
+      }
+  }
+  // scores S[query][key], key tiles 0 (keys 0-7) and 1 (keys 8-15)
+  float sc[2][4];
+#pragma unroll
+  for (int nh = 0; nh < 2; ++nh) sc[nh][0] = sc[nh][1] = sc[nh][2] = sc[nh][3] = 0.0f;
+#pragma unroll
+  for (int kc = 0; kc < 4; ++kc)
+#pragma unroll
+    for (int nh = 0; nh < NT; ++nh) {
+      mma16816(sc[nh][0], sc[nh][1], sc[nh][2], sc[nh][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], kh[kc][2 * nh],
+               kh[kc][2 * nh + 1]);
+      mma16816(sc[nh][0], sc[nh][1], sc[nh][2], sc[nh][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], kl[kc][2 * nh],
+               kl[kc][2 * nh + 1]);
+      mma16816(sc[nh][0], sc[nh][1], sc[nh][2], sc[nh][3], ql[kc][0], ql[kc][1], ql[kc][2], ql[kc][3], kh[kc][2 * nh],
+               kh[kc][2 * nh + 1]);
+    }
+  // key validity of keys 2t, 2t+1 (+8 nh) comes from the lanes holding those rows
+  uint32_t kvalid = 0;
+#pragma unroll
+  for (int hr = 0; hr < NT; ++hr) kvalid |= (valid[hr] ? 1u : 0u) << (g + 8 * hr);
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) kvalid |= __shfl_xor_sync(0xffffffffu, kvalid, o);
+  // e = 0,1: query row g, e = 2,3: query row g + 8
+  float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int nh = 0; nh < 2; ++nh)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int qrow = g + 8 * (e >> 1), key = 8 * nh + 2 * t + (e & 1);
+      const bool qmasked = !((kvalid >> qrow) & 1u);
+      float x = -INFINITY;
+      if (key < nv) x = qmasked ? -1.0e9f : (((kvalid >> key) & 1u) ? sc[nh][e] * 0.125f : -INFINITY);
+      sc[nh][e] = x;
+      mx[e >> 1] = fmaxf(mx[e >> 1], x);
+    }
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 1));
+    mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
+    if (mx[hr] == -INFINITY) mx[hr] = 0.0f;  // padding query rows (>= nv): all zero
+  }
+  float sum[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int nh = 0; nh < 2; ++nh)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float pe = expf(sc[nh][e] - mx[e >> 1]);
+      sc[nh][e] = pe;
+      sum[e >> 1] += pe;
+    }
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    sum[hr] += __shfl_xor_sync(0xffffffffu, sum[hr], 1);
+    sum[hr] += __shfl_xor_sync(0xffffffffu, sum[hr], 2);
+  }
+  // P as the A operand (16 queries x 16 keys), split hi / lo
+  uint32_t ph[4], pl[4];
+  split2(sc[0][0], sc[0][1], ph[0], pl[0]);
+  split2(sc[0][2], sc[0][3], ph[1], pl[1]);
+  split2(sc[1][0], sc[1][1], ph[2], pl[2]);
+  split2(sc[1][2], sc[1][3], ph[3], pl[3]);
+  __syncwarp();  // this warp's v planes are written
+  float o[8][4];
+#pragma unroll
+  for (int nd = 0; nd < 8; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.0f;
+  // transposed ldmatrix rows: matrix m -> keys (m % 2) * 8 + (lane % 8), dims (m / 2) * 8
+  const int voff = (((lane >> 3) & 1) * 8 + (lane & 7)) * 72 + ((lane >> 4) << 3);
+#pragma unroll
+  for (int n2 = 0; n2 < 4; ++n2) {
+    uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+    ldsm_x4_trans(vs[h][0] + voff + 16 * n2, h0, h1, h2, h3);
+    ldsm_x4_trans(vs[h][1] + voff + 16 * n2, l0, l1, l2, l3);
+    float *oa = o[2 * n2], *ob = o[2 * n2 + 1];
+    mma16816(oa[0], oa[1], oa[2], oa[3], ph[0], ph[1], ph[2], ph[3], h0, h1);
+    mma16816(ob[0], ob[1], ob[2], ob[3], ph[0], ph[1], ph[2], ph[3], h2, h3);
+    mma16816(oa[0], oa[1], oa[2], oa[3], ph[0], ph[1], ph[2], ph[3], l0, l1);
+    mma16816(ob[0], ob[1], ob[2], ob[3], ph[0], ph[1], ph[2], ph[3], l2, l3);
+    mma16816(oa[0], oa[1], oa[2], oa[3], pl[0], pl[1], pl[2], pl[3], h0, h1);
+    mma16816(ob[0], ob[1], ob[2], ob[3], pl[0], pl[1], pl[2], pl[3], h2, h3);
+  }
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int qa = g + 8 * hr;
+    if (qa >= nv) continue;
+    const float inv = 1.0f / sum[hr];
+    const size_t oo = ((size_t)(r0 + qa) * p + patch) * E + h * 64;
+#pragma unroll
+    for (int nd = 0; nd < 8; ++nd) {
+      const int d = nd * 8 + 2 * t;
+      const float x0 = o[nd][2 * hr] * inv, x1 = o[nd][2 * hr + 1] * inv;
+      uint32_t hw, lw;
+      split2(x0, x1, hw, lw);
+      *reinterpret_cast<uint32_t *>(a.oh + oo + d) = hw;
+      *reinterpret_cast<uint32_t *>(a.ol + oo + d) = lw;
+      if (a.o32) *reinterpret_cast<float2 *>(a.o32 + oo + d) = make_float2(x0, x1);
+    }
+  }
+}
+
 // Group attention with the series' keys and values held in registers: one
 // warp per head loads k and v of all NV (>= the series' row count) variate
 // rows at this patch with independent loads, normalises the keys once, then
@@ -1590,7 +1774,11 @@ cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
 template <int HD>
 static cudaError_t launch_attn_group_hd(const AttnArgs &a, cudaStream_t st) {
   dim3 grid(a.n_series, a.p);
-  if (a.max_nrows <= 8)
+  if (HD == 64 && a.max_nrows <= 8 && a.H <= 8)
+    attn_group_mma_kernel<1><<<grid, 32 * a.H, 0, st>>>(a);
+  else if (HD == 64 && a.max_nrows <= 16 && a.H <= 8)
+    attn_group_mma_kernel<2><<<grid, 32 * a.H, 0, st>>>(a);
+  else if (a.max_nrows <= 8)
     attn_group_reg_kernel<8, HD><<<grid, 32 * a.H, 0, st>>>(a);
   else if (a.max_nrows <= 16)
     attn_group_reg_kernel<16, HD><<<grid, 32 * a.H, 0, st>>>(a);
