@@ -23,7 +23,8 @@ enum : int {
   T0B_DEVERR_WAIT_DEQ = 3,   // dequantized tile never published
   T0B_DEVERR_WAIT_EMPTY = 4, // MMA never released a stage
   T0B_DEVERR_WAIT_ACC = 5,   // accumulator never completed
-  T0B_DEVERR_SHAPE = 6       // kernel launched with an unsupported shape
+  T0B_DEVERR_SHAPE = 6,      // kernel launched with an unsupported shape
+  T0B_DEVERR_WAIT_ATTN = 7   // attention k / v tiles never arrived
 };
 
 T0B_DEV void record_error(int *err, int code) {

@@ -587,6 +587,15 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
 
 }  // namespace
 
+// f32 row-major [outer][inner] tensor (rows row_bytes apart), box
+// [box_outer][box_inner], optionally with the 128-byte swizzle: for other
+// kernels' TMA loads.
+bool t0b_make_tmap_f32_2d(CUtensorMap *tm, const float *ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                          uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  return make_tmap_2d(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ptr, inner, outer, row_bytes, box_inner, box_outer,
+                      swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 // Host entry.  qt: 8 = Q8_0, 4 = Q4_0.  Requires K % 256 == 0, N % 256 == 0
 // (SWIGLU: F % 128 == 0), M >= 1, 16-byte aligned A rows.  `wrows` is the
 // number of rows of W (N, or 2F for SWIGLU); `wshift` the weight prescale

@@ -10,6 +10,7 @@
 //     model.rs:487-531).
 #include "common.cuh"
 #include <algorithm>
+#include <cstring>
 
 #include "t0b_internal.h"
 
@@ -743,15 +744,17 @@ T0B_DEV void rope16(float *x, const float *tab, int cg, bool kside) {
   }
 }
 
-__global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a, const __grid_constant__ CUtensorMap tm_qkv,
+                                                               int use_tma) {
   pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
-  extern __shared__ uint4 smem_u4[];
+  extern __shared__ __align__(128) uint4 smem_u4[];
   const int r = blockIdx.x, h = blockIdx.y;
   const int p = a.p, E = a.E;
   const int QB = (p + 15) >> 4;  // blocks of 16 queries (= keys)
   const int PK = QB * 16;
-  // k and v row-major [PK][72] f16 (72-half pitch: conflict-free ldmatrix rows)
-  __half *Kh = reinterpret_cast<__half *>(smem_u4);
+  // k and v row-major [PK][72] f16 (72-half pitch: conflict-free ldmatrix rows),
+  // from a 1024-byte aligned base (the TMA swizzle atom)
+  __half *Kh = reinterpret_cast<__half *>(smem_u4 + ((1024u - (smem_u32(smem_u4) & 1023u)) & 1023u) / 16);
   __half *Kl = Kh + PK * 72;
   __half *Vh = Kl + PK * 72;
   __half *Vl = Vh + PK * 72;
@@ -760,17 +763,50 @@ __global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a) {
   const int lo = a.row_first_valid[r];
 
   // ---- staging (blockDim = 32 QB = 2 PK): threads [0, PK) take the v row of
-  // token j, threads [PK, 2 PK) the k row; every load of a row is issued
-  // before any conversion
+  // token j, threads [PK, 2 PK) the k row.  With use_tma the row's k and v
+  // tiles ([p][64] f32 each) arrive by TMA loads into the start of the (not
+  // yet written) f16 planes and each thread reads its row from there;
+  // otherwise every load of a row is issued from global memory before any
+  // conversion.
   {
     const bool is_k = threadIdx.x >= PK;
     const int j = is_k ? threadIdx.x - PK : threadIdx.x;
-    const float *src = a.qkv + (tok0 + (j < p ? j : 0)) * 3 * E + h * 64 + (is_k ? E : 2 * E);
     float xv[64];
+    if (use_tma) {
+      // four boxes of [p][32] f32 with the 128-byte swizzle (16-byte unit u
+      // of row r at unit u ^ (r & 7)): k dims 0-31, k 32-63, v 0-31, v 32-63
+      uint8_t *tb = reinterpret_cast<uint8_t *>(Kh);  // 1024-byte aligned
+      uint64_t *bar = reinterpret_cast<uint64_t *>(Kh + 4 * PK * 72);
+      if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_barrier_init();
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(bar, (uint32_t)(4 * p * 32 * sizeof(float)));
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      const float4 x4 = j < p ? *reinterpret_cast<const float4 *>(src + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      xv[4 * c] = x4.x, xv[4 * c + 1] = x4.y, xv[4 * c + 2] = x4.z, xv[4 * c + 3] = x4.w;
+        for (int bx = 0; bx < 4; ++bx)
+          tma_load_2d(tb + (size_t)bx * PK * 128, &tm_qkv, bar, (bx < 2 ? E : 2 * E) + h * 64 + 32 * (bx & 1), (int)tok0);
+      }
+      const bool ok = mbar_wait(bar, 0, a.err, T0B_DEVERR_WAIT_ATTN, nullptr) && j < p;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const uint8_t *rowp = tb + ((size_t)((is_k ? 0 : 2) + hf) * PK + j) * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float4 x4 = ok ? *reinterpret_cast<const float4 *>(rowp + ((u ^ (j & 7)) << 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          xv[32 * hf + 4 * u] = x4.x, xv[32 * hf + 4 * u + 1] = x4.y;
+          xv[32 * hf + 4 * u + 2] = x4.z, xv[32 * hf + 4 * u + 3] = x4.w;
+        }
+      }
+      __syncthreads();  // every row is in registers before the planes overwrite the tiles
+    } else {
+      const float *src = a.qkv + (tok0 + (j < p ? j : 0)) * 3 * E + h * 64 + (is_k ? E : 2 * E);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const float4 x4 = j < p ? *reinterpret_cast<const float4 *>(src + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        xv[4 * c] = x4.x, xv[4 * c + 1] = x4.y, xv[4 * c + 2] = x4.z, xv[4 * c + 3] = x4.w;
+      }
     }
     if (is_k && j < p) {  // QK-norm over the whole row, then RoPE
       float ss = 0.0f;
@@ -1749,10 +1785,15 @@ cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
   if (a.E / a.H != 64) return cudaErrorInvalidValue;
   if (a.p <= kAttnMmaMaxP) {
     const int QB = (a.p + 15) / 16, PK = 16 * QB;
-    const size_t smem = (size_t)(4 * PK * 72) * sizeof(__half);
+    const size_t smem = (size_t)(4 * PK * 72) * sizeof(__half) + 16 + 1024;  // planes, mbarrier, alignment slack
     cudaError_t e = t0b_smem_limit((const void *)attn_time_mma_kernel, smem);
     if (e != cudaSuccess) return e;
-    attn_time_mma_kernel<<<dim3(a.R, a.H), 32 * QB, smem, st>>>(a);
+    // k / v tiles by TMA: a [p][64] f32 box of the [R p][3E] q|k|v tensor
+    CUtensorMap tm;
+    std::memset(&tm, 0, sizeof(tm));
+    const int use_tma = t0b_make_tmap_f32_2d(&tm, a.qkv, (uint64_t)3 * a.E, (uint64_t)a.R * a.p,
+                                             (uint64_t)3 * a.E * sizeof(float), 32, (uint32_t)a.p, true) ? 1 : 0;
+    attn_time_mma_kernel<<<dim3(a.R, a.H), 32 * QB, smem, st>>>(a, tm, use_tma);
     return cudaGetLastError();
   }
   if (a.p <= kAttnTiledMaxP) {

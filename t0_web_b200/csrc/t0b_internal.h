@@ -2,6 +2,7 @@
 // the host orchestration (t0b_model.cu) and the kernel files.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -55,7 +56,15 @@ struct AttnArgs {
   int use_rope;
   int R, p, E, H, n_series;
   int max_nrows;  // largest series_nrows entry (host-side bound for the group kernel)
+  int *err;       // device error word (a bounded wait that ran out)
 };
+
+// Tensor map of an f32 row-major [outer][inner] tensor with rows row_bytes
+// apart and a [box_outer][box_inner] box, optionally 128-byte swizzled (a
+// 32-float inner box); false if the driver entry point is unavailable or
+// rejects the layout (k_gemm_tc.cu).
+bool t0b_make_tmap_f32_2d(CUtensorMap *tm, const float *ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                          uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 
 // Small-M dequant GEMM (k_gemm_small.cu): thread-block clusters along K,
 // launched as a programmatic dependent of the previous kernel on `st`.

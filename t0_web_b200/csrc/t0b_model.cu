@@ -745,6 +745,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   aa.H = m->H;
   aa.n_series = ns;
   aa.max_nrows = ps.s_nrows.empty() ? 0 : *std::max_element(ps.s_nrows.begin(), ps.s_nrows.end());
+  aa.err = m->d_err;
   const int M = (int)T;
   aa.rope = rope;
   aa.rope_c = rope + (size_t)4 * p * (E / m->H);  // after the [4][p][hd] full tables
