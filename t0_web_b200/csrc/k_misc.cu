@@ -744,6 +744,17 @@ T0B_DEV void rope16(float *x, const float *tab, int cg, bool kside) {
   }
 }
 
+// Shared-memory layout of attn_time_mma_kernel past its 1024-byte aligned
+// base: the four f16 planes [4][PK][72] (the k / v TMA tiles alias their
+// start), the q tile [2][PK][32] f32 (1024-byte aligned), the mbarrier.
+__host__ __device__ constexpr size_t attn_planes_bytes(int PK) { return (size_t)4 * PK * 72 * 2; }
+__host__ __device__ constexpr size_t attn_q_off(int PK) { return (attn_planes_bytes(PK) + 1023) / 1024 * 1024; }
+__host__ __device__ constexpr size_t attn_smem_bytes(int PK) { return attn_q_off(PK) + (size_t)PK * 256 + 16; }
+T0B_DEV uint8_t *attn_qtile(__half *base, int PK) { return reinterpret_cast<uint8_t *>(base) + attn_q_off(PK); }
+T0B_DEV uint64_t *attn_bar(__half *base, int PK) {
+  return reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(base) + attn_q_off(PK) + (size_t)PK * 256);
+}
+
 __global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a, const __grid_constant__ CUtensorMap tm_qkv,
                                                                int use_tma) {
   pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
@@ -776,17 +787,20 @@ __global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a, const
       // four boxes of [p][32] f32 with the 128-byte swizzle (16-byte unit u
       // of row r at unit u ^ (r & 7)): k dims 0-31, k 32-63, v 0-31, v 32-63
       uint8_t *tb = reinterpret_cast<uint8_t *>(Kh);  // 1024-byte aligned
-      uint64_t *bar = reinterpret_cast<uint64_t *>(Kh + 4 * PK * 72);
+      uint64_t *bar = attn_bar(Kh, PK);
       if (threadIdx.x == 0) {
         mbar_init(bar, 1);
         fence_barrier_init();
       }
       __syncthreads();
       if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(bar, (uint32_t)(4 * p * 32 * sizeof(float)));
+        mbar_arrive_expect_tx(bar, (uint32_t)(6 * p * 32 * sizeof(float)));
 #pragma unroll
         for (int bx = 0; bx < 4; ++bx)
           tma_load_2d(tb + (size_t)bx * PK * 128, &tm_qkv, bar, (bx < 2 ? E : 2 * E) + h * 64 + 32 * (bx & 1), (int)tok0);
+        uint8_t *qt = attn_qtile(Kh, PK);  // q dims 0-31 and 32-63, kept past the staging
+        tma_load_2d(qt, &tm_qkv, bar, h * 64, (int)tok0);
+        tma_load_2d(qt + (size_t)PK * 128, &tm_qkv, bar, h * 64 + 32, (int)tok0);
       }
       const bool ok = mbar_wait(bar, 0, a.err, T0B_DEVERR_WAIT_ATTN, nullptr) && j < p;
 #pragma unroll
@@ -844,7 +858,20 @@ __global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a, const
   const int g = lane >> 2, t = lane & 3;
   const int ia = qb * 16 + g, ib = ia + 8;  // this thread's two query rows
   float qa[16], qbv[16];                    // dims 16kc + {2t, 2t+1, 2t+8, 2t+9}
-  {
+  if (use_tma) {  // from the swizzled q tile (16-byte unit u of row r at u ^ (r & 7))
+    const uint8_t *qt = attn_qtile(Kh, PK);
+    const int ra_ = min(ia, p - 1), rb_ = min(ib, p - 1);
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc)
+#pragma unroll
+      for (int u8 = 0; u8 < 2; ++u8) {
+        const int d = 16 * kc + 2 * t + 8 * u8, hf = d >> 5, uu = (d & 31) >> 2, off = (d & 3) * 4;
+        const float2 x = *reinterpret_cast<const float2 *>(qt + ((size_t)hf * PK + ra_) * 128 + ((uu ^ (ra_ & 7)) << 4) + off);
+        const float2 y = *reinterpret_cast<const float2 *>(qt + ((size_t)hf * PK + rb_) * 128 + ((uu ^ (rb_ & 7)) << 4) + off);
+        qa[4 * kc + 2 * u8] = x.x, qa[4 * kc + 2 * u8 + 1] = x.y;
+        qbv[4 * kc + 2 * u8] = y.x, qbv[4 * kc + 2 * u8 + 1] = y.y;
+      }
+  } else {
     const float *ra = a.qkv + (tok0 + min(ia, p - 1)) * 3 * E + h * 64;
     const float *rb = a.qkv + (tok0 + min(ib, p - 1)) * 3 * E + h * 64;
 #pragma unroll
@@ -1785,7 +1812,7 @@ cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
   if (a.E / a.H != 64) return cudaErrorInvalidValue;
   if (a.p <= kAttnMmaMaxP) {
     const int QB = (a.p + 15) / 16, PK = 16 * QB;
-    const size_t smem = (size_t)(4 * PK * 72) * sizeof(__half) + 16 + 1024;  // planes, mbarrier, alignment slack
+    const size_t smem = attn_smem_bytes(PK) + 1024;  // planes, q tile, mbarrier, alignment slack
     cudaError_t e = t0b_smem_limit((const void *)attn_time_mma_kernel, smem);
     if (e != cudaSuccess) return e;
     // k / v tiles by TMA: a [p][64] f32 box of the [R p][3E] q|k|v tensor
