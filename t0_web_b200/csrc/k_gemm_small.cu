@@ -354,16 +354,24 @@ cudaError_t launch_small_t(const __half *ah, const __half *al, int M, int K, int
   return cudaLaunchKernelEx(&cfg, kfn, ah, al, M, K, KS, W, epi, err);
 }
 
+// Tokens per CTA (8 * nt8) that fit in shared memory for this K; 0 if none.
+template <int QT>
+int small_nt8(int M, int K, const Epi &epi) {
+  const int KS = small_slice(K);
+  int nt8 = (M + 7) / 8 < 4 ? (M + 7) / 8 : 4;
+  const int cs = K / KS, nt = epi.ssq_in ? epi.ssq_in_nt : 0;
+  while (nt8 > 1 && small_layout(QT, KS, 8 * nt8, cs, nt).bytes > kSmemCap) --nt8;
+  return small_layout(QT, KS, 8 * nt8, cs, nt).bytes > kSmemCap ? 0 : nt8;
+}
+
 template <int QT>
 cudaError_t launch_small_q(const __half *ah, const __half *al, int M, int K, const uint8_t *W, const Epi &epi,
                            int *err, cudaStream_t st) {
   const int KS = small_slice(K);
   // tokens per CTA: up to 32, fewer when a wide slice would not fit in
   // shared memory
-  int nt8 = (M + 7) / 8 < 4 ? (M + 7) / 8 : 4;
-  const int cs = K / KS, nt = epi.ssq_in ? epi.ssq_in_nt : 0;
-  while (nt8 > 1 && small_layout(QT, KS, 8 * nt8, cs, nt).bytes > kSmemCap) --nt8;
-  if (small_layout(QT, KS, 8 * nt8, cs, nt).bytes > kSmemCap) return cudaErrorInvalidValue;
+  const int nt8 = small_nt8<QT>(M, K, epi);
+  if (!nt8) return cudaErrorInvalidValue;
   switch (nt8) {
     case 1: return launch_small_t<QT, 1>(ah, al, M, K, KS, W, epi, err, st);
     case 2: return launch_small_t<QT, 2>(ah, al, M, K, KS, W, epi, err, st);
@@ -373,6 +381,11 @@ cudaError_t launch_small_q(const __half *ah, const __half *al, int M, int K, con
 }
 
 }  // namespace
+
+bool t0b_small_supports(int qt, int M, int K, const Epi &epi) {
+  if (M <= 0 || K <= 0 || K % 256) return false;
+  return (qt == 8 ? small_nt8<8>(M, K, epi) : small_nt8<4>(M, K, epi)) > 0;
+}
 
 // Host entry.  qt: 8 = Q8_0, 4 = Q4_0.  Requires K % 256 == 0 and the output
 // column count (N, or F for SWIGLU) a multiple of 32 (16 for SWIGLU).

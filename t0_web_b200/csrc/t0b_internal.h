@@ -70,6 +70,10 @@ bool t0b_make_tmap_f32_2d(CUtensorMap *tm, const float *ptr, uint64_t inner, uin
 // launched as a programmatic dependent of the previous kernel on `st`.
 cudaError_t t0b_launch_gemm_small(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W,
                                   const Epi &epi, int *err, cudaStream_t st);
+// Whether the small-M kernel runs this shape: K is split into at most 8
+// slices of a multiple of 256 values (a divisor of K), which must fit in
+// shared memory; otherwise callers use the tensor-core kernel.
+bool t0b_small_supports(int qt, int M, int K, const Epi &epi);
 cudaError_t t0b_launch_gemm_tc(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
                                int wshift, const Epi &epi, int *err, cudaStream_t st);
 cudaError_t t0b_launch_absmax_scale(const uint8_t *W, size_t nblocks, int bpb, unsigned int *out, cudaStream_t st);

@@ -480,6 +480,10 @@ struct Pass {
 };
 
 bool use_tc(const t0b_model *m, int M) { return M >= m->tc_min_tokens; }
+// the tensor-core kernel also takes the small shapes the small-M kernel cannot
+bool use_tc(const t0b_model *m, int M, int K, const Epi &epi) {
+  return use_tc(m, M) || !t0b_small_supports(m->qt, M, K, epi);
+}
 
 enum { KC_GEMM_TC = 0, KC_GEMM_SMALL, KC_ATTN_TIME, KC_ATTN_GROUP, KC_PREP, KC_SGEMM, KC_OTHER, KC_N };
 const char *kKcNames[KC_N] = {"gemm_tc", "gemm_small", "attn_time", "attn_group", "prep", "sgemm", "other"};
@@ -533,7 +537,7 @@ cudaError_t qgemm(t0b_model *m, const __half *ah, const __half *al, int M, int K
   const double outc = epi.kind == EPI_SWIGLU ? (double)epi.F : (double)epi.N;
   const double flops = 2.0 * M * (double)wrows * K;
   const double bytes = wbytes + 4.0 * M * K + 4.0 * M * outc * (epi.kind == EPI_RESID ? 2.0 : 1.0);
-  if (use_tc(m, M)) {
+  if (use_tc(m, M, K, epi)) {
     return launch(m, KC_GEMM_TC, flops, bytes, [&] {
       return t0b_launch_gemm_tc(m->qt, ah, al, M, K, W, wrows, wshift, epi, m->d_err, m->stream);
     });
@@ -556,7 +560,7 @@ cudaError_t resid_gemm(t0b_model *m, const __half *ah, const __half *al, int M, 
   r.M = M;
   r.N = E;
   r.bias = bias;
-  if (use_tc(m, M)) {
+  if (use_tc(m, M, K, r)) {
     r.kind = EPI_PLAIN;
     r.y = ybuf;
     r.ldy = E;
@@ -1316,9 +1320,13 @@ t0b_status device_weight_shift(t0b_engine *e, int qt, const uint8_t *W, size_t n
   return T0B_OK;
 }
 
+// The standalone GEMMs take the tensor-core path from 128 tokens, and for
+// the small shapes the small-M kernel cannot run.
+bool engine_use_tc(int qt, int M, int K, const Epi &epi) { return M >= 128 || !t0b_small_supports(qt, M, K, epi); }
+
 cudaError_t engine_qgemm(t0b_engine *e, int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W,
                          int wrows, int wshift, Epi &epi, int *err, cudaStream_t st) {
-  const bool tc = M >= 128;
+  const bool tc = engine_use_tc(qt, M, K, epi);
   if (tc) return t0b_launch_gemm_tc(qt, ah, al, M, K, W, wrows, wshift, epi, err, st);
   return t0b_launch_gemm_small(qt, ah, al, M, K, W, epi, err, st);
 }
@@ -1347,9 +1355,6 @@ extern "C" t0b_status t0b_gemm_q(t0b_engine *e, int ggml_type, const void *w_dev
   cudaStream_t st = (cudaStream_t)stream;
   t0b_status s = split_input(e, x_dev, (size_t)M * K, st);
   if (s != T0B_OK) return s;
-  int sh = 0;  // tensor-core prescale; the small-M kernel applies block scales in f32 and needs none
-  if (M >= 128 && (s = device_weight_shift(e, qt, (const uint8_t *)w_dev, (size_t)N * K, st, &sh)) != T0B_OK)
-    return s;
   Epi ep{};
   ep.kind = EPI_PLAIN;
   ep.M = M;
@@ -1357,6 +1362,10 @@ extern "C" t0b_status t0b_gemm_q(t0b_engine *e, int ggml_type, const void *w_dev
   ep.bias = bias_dev;
   ep.y = y_dev;
   ep.ldy = N;
+  int sh = 0;  // tensor-core prescale; the small-M kernel applies block scales in f32 and needs none
+  if (engine_use_tc(qt, M, K, ep) &&
+      (s = device_weight_shift(e, qt, (const uint8_t *)w_dev, (size_t)N * K, st, &sh)) != T0B_OK)
+    return s;
   CUDA_TRY(engine_qgemm(e, qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, (const uint8_t *)w_dev, N,
                         sh, ep, e->d_err, st));
   return engine_check(e, st);
@@ -1375,11 +1384,6 @@ extern "C" t0b_status t0b_swiglu_q(t0b_engine *e, int ggml_type, const void *w0_
   cudaStream_t st = (cudaStream_t)stream;
   t0b_status s = split_input(e, x_dev, (size_t)M * K, st);
   if (s != T0B_OK) return s;
-  int sh0 = 0, sh2 = 0;
-  if (M >= 128) {
-    if ((s = device_weight_shift(e, qt, (const uint8_t *)w0_dev, (size_t)2 * F * K, st, &sh0)) != T0B_OK) return s;
-    if ((s = device_weight_shift(e, qt, (const uint8_t *)w2_dev, (size_t)N2 * F, st, &sh2)) != T0B_OK) return s;
-  }
   if ((s = qm_reserve(e->scratch_zh, (size_t)M * F * 2, st)) != T0B_OK ||
       (s = qm_reserve(e->scratch_zl, (size_t)M * F * 2, st)) != T0B_OK)
     return s;
@@ -1392,8 +1396,6 @@ extern "C" t0b_status t0b_swiglu_q(t0b_engine *e, int ggml_type, const void *w0_
   sg.zh = e->scratch_zh.as<__half>();
   sg.zl = e->scratch_zl.as<__half>();
   sg.z32 = z_dev;
-  CUDA_TRY(engine_qgemm(e, qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, (const uint8_t *)w0_dev,
-                        2 * F, sh0, sg, e->d_err, st));
   Epi dn{};
   dn.kind = EPI_PLAIN;
   dn.M = M;
@@ -1401,6 +1403,15 @@ extern "C" t0b_status t0b_swiglu_q(t0b_engine *e, int ggml_type, const void *w0_
   dn.bias = b2_dev;
   dn.y = y_dev;
   dn.ldy = N2;
+  int sh0 = 0, sh2 = 0;  // tensor-core prescales, where that path runs
+  if (engine_use_tc(qt, M, K, sg) &&
+      (s = device_weight_shift(e, qt, (const uint8_t *)w0_dev, (size_t)2 * F * K, st, &sh0)) != T0B_OK)
+    return s;
+  if (engine_use_tc(qt, M, F, dn) &&
+      (s = device_weight_shift(e, qt, (const uint8_t *)w2_dev, (size_t)N2 * F, st, &sh2)) != T0B_OK)
+    return s;
+  CUDA_TRY(engine_qgemm(e, qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, (const uint8_t *)w0_dev,
+                        2 * F, sh0, sg, e->d_err, st));
   CUDA_TRY(engine_qgemm(e, qt, e->scratch_zh.as<__half>(), e->scratch_zl.as<__half>(), M, F, (const uint8_t *)w2_dev, N2,
                         sh2, dn, e->d_err, st));
   return engine_check(e, st);
@@ -1609,7 +1620,7 @@ extern "C" t0b_status t0b_gemm_q_noalloc(int ggml_type, const void *w_dev, int N
   ep.bias = bias_dev;
   ep.y = y_dev;
   ep.ldy = N;
-  if (M >= 128)
+  if (engine_use_tc(qt, M, K, ep))
     CUDA_TRY(t0b_launch_gemm_tc(qt, xh, xl, M, K, (const uint8_t *)w_dev, N, sh, ep, err, st));
   else
     CUDA_TRY(t0b_launch_gemm_small(qt, xh, xl, M, K, (const uint8_t *)w_dev, ep, err, st));

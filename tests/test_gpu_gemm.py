@@ -50,6 +50,23 @@ def test_gemm_vs_oracle(engine, qtype, M):
 
 
 @pytest.mark.parametrize("qtype", [Q8_0, Q4_0], ids=["q8_0", "q4_0"])
+@pytest.mark.parametrize("K", [256, 768, 4096, 4352])
+@pytest.mark.parametrize("M", [5, 19, 77])
+def test_small_m_k_slices(engine, qtype, K, M):
+    """Small-M K slicing: one slice (K = 256), a 3-CTA cluster (768), eight
+    slices of 512 (4096), and K = 17 x 256, which has no split into at most 8
+    slices and goes to the tensor-core kernel instead."""
+    N = 512
+    w, x = S.gemm_case(N, K, M, seed=K + M)
+    wb = gguf.quantize(w, qtype)
+    bias = (np.random.default_rng(K).standard_normal(N) * 0.02).astype(np.float32)
+    y = _gemm(engine, qtype, wb, N, K, x, bias)
+    ref = O.gemm_q_f64(qtype, wb, N, K, x, bias)
+    assert np.isfinite(y).all()
+    assert _rel(y, ref) <= REL_TIGHT
+
+
+@pytest.mark.parametrize("qtype", [Q8_0, Q4_0], ids=["q8_0", "q4_0"])
 @pytest.mark.parametrize("M", [16, 256, 4096])
 def test_gemm_config2_shape(engine, qtype, M):
     """N=3072, K=1024 (the standalone GEMM configuration); rows sampled for large M."""
