@@ -94,6 +94,15 @@ T0B_DEV void tma_store_2d(const void *tmap, const void *src, int x, int y) {
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
+// 2-D tiled bulk tensor reduction shared -> global: global += the tile
+// (element type from the tensor map; bulk-group completion).  Same
+// coordinate rules as tma_store_2d.
+T0B_DEV void tma_reduce_add_2d(const void *tmap, const void *src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   (uint64_t)tmap),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
 T0B_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until no committed bulk store still reads shared memory.
 T0B_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }

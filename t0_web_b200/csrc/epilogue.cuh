@@ -20,9 +20,11 @@ struct Epi {
   // un-normalised row, ssq_in[m * ssq_in_nt + slot], over ssq_dim columns
   const float *ssq_in;
   int ssq_in_nt, ssq_dim;
-  // EPI_PLAIN: y [M, ldy] = acc / row denominator + bias
+  // EPI_PLAIN: y [M, ldy] = acc / row denominator + bias (reduce_add: y +=
+  // that instead; tensor-core kernel only)
   float *y;
   int ldy;
+  int reduce_add;
   // EPI_RESID: x[m, n] += acc + bias (f32 residual stream, in place); then
   // x*gnext split into f16 (xh, xl) for the next RMSNorm-fused GEMM and the
   // sum of x^2 over this thread's columns written to ssq_out[m*nt + slot].

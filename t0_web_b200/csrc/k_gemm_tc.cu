@@ -21,8 +21,8 @@
 // accumulator is ready (the bias is staged in shared memory), and its
 // global writes are asynchronous TMA stores of swizzled 32-row chunks, so its
 // cost is a short burst of TMEM loads, math and shared-memory stores.
-// Residual adds, QK-norm and RoPE run in the row kernels that consume these
-// outputs.
+// Residual adds are TMA reduce-adds of the output tile into the residual
+// stream; QK-norm and RoPE run in the attention kernels.
 //
 // Warp roles (896 threads):
 //   warp 0      TMA producer: Ah/Al tiles and the raw blocks of the tile's
@@ -474,7 +474,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(&tm_y, stg, nt * BN + c0, row0);
+              if (e.reduce_add)
+                tma_reduce_add_2d(&tm_y, stg, nt * BN + c0, row0);  // y += tile, in L2
+              else
+                tma_store_2d(&tm_y, stg, nt * BN + c0, row0);
               bulk_commit();
             }
           }
@@ -600,7 +603,8 @@ bool t0b_make_tmap_f32_2d(CUtensorMap *tm, const float *ptr, uint64_t inner, uin
 // (SWIGLU: F % 128 == 0), M >= 1, 16-byte aligned A rows.  `wrows` is the
 // number of rows of W (N, or 2F for SWIGLU); `wshift` the weight prescale
 // exponent from t0b_weight_shift.  Epilogue kinds: PLAIN (bias + optional
-// RMSNorm row scale) and SWIGLU; others are rejected (cudaErrorInvalidValue).
+// RMSNorm row scale; with reduce_add the tile is added into y by TMA
+// reduce-adds) and SWIGLU; others are rejected (cudaErrorInvalidValue).
 cudaError_t t0b_launch_gemm_tc(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
                                int wshift, const Epi &epi, int *err, cudaStream_t st) {
   if (qt == 8) return launch_tc_t<8>(ah, al, M, K, W, wrows, wshift, epi, err, st);

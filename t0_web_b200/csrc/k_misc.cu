@@ -358,15 +358,22 @@ __global__ void rownorm_split_kernel(const float *x, const float *g, __half *xh,
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
-  const float *xr = x + (size_t)row * E;
+  // 16-byte loads of x and g, 8-byte stores of each f16 plane (E % 4 == 0)
+  const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)row * E);
+  const float4 *g4 = reinterpret_cast<const float4 *>(g);
+  uint2 *hr = reinterpret_cast<uint2 *>(xh + (size_t)row * E), *lr = reinterpret_cast<uint2 *>(xl + (size_t)row * E);
   float s = 0.0f;
-  for (int c = lane; c < E; c += 32) {
-    float v = xr[c];
-    s += v * v;
-    __half h, l;
-    split_f16(v * g[c], h, l);
-    xh[(size_t)row * E + c] = h;
-    xl[(size_t)row * E + c] = l;
+  for (int c = lane; c < E / 4; c += 32) {
+    const float4 v = xr[c], gg = g4[c];
+    s += v.x * v.x;
+    s += v.y * v.y;
+    s += v.z * v.z;
+    s += v.w * v.w;
+    uint32_t h0, l0, h1, l1;
+    split2(v.x * gg.x, v.y * gg.y, h0, l0);
+    split2(v.z * gg.z, v.w * gg.w, h1, l1);
+    hr[c] = make_uint2(h0, h1);
+    lr[c] = make_uint2(l0, l1);
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -1680,39 +1687,6 @@ __global__ void __launch_bounds__(256) attn_group_reg_kernel(AttnArgs a) {
   }
 }
 
-// ============================================================== residual
-// One warp per row: x += y (the bias-added output of the wO / mlp.2 GEMM),
-// then xh/xl = split(x * g) for the next RMSNorm-fused GEMM and ssq[row] =
-// sum x^2 (single slot).  E % 128 == 0; 16-byte accesses.
-__global__ void resid_split_kernel(float *x, const float *y, const float *g, __half *xh, __half *xl, float *ssq,
-                                   int M, int E) {
-  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= M) return;
-  float4 *xr = reinterpret_cast<float4 *>(x + (size_t)row * E);
-  const float4 *yr = reinterpret_cast<const float4 *>(y + (size_t)row * E);
-  const float4 *g4 = reinterpret_cast<const float4 *>(g);
-  uint2 *hr = reinterpret_cast<uint2 *>(xh + (size_t)row * E);
-  uint2 *lr = reinterpret_cast<uint2 *>(xl + (size_t)row * E);
-  float s = 0.0f;
-  for (int c = lane; c < E / 4; c += 32) {
-    const float4 a = xr[c], b = yr[c], gg = g4[c];
-    const float4 v = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
-    xr[c] = v;
-    s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-    __half h0, l0, h1, l1, h2, l2, h3, l3;
-    split_f16(v.x * gg.x, h0, l0);
-    split_f16(v.y * gg.y, h1, l1);
-    split_f16(v.z * gg.z, h2, l2);
-    split_f16(v.w * gg.w, h3, l3);
-    __half2 ha = __halves2half2(h0, h1), hb = __halves2half2(h2, h3);
-    __half2 la = __halves2half2(l0, l1), lb = __halves2half2(l2, l3);
-    hr[c] = make_uint2(*reinterpret_cast<uint32_t *>(&ha), *reinterpret_cast<uint32_t *>(&hb));
-    lr[c] = make_uint2(*reinterpret_cast<uint32_t *>(&la), *reinterpret_cast<uint32_t *>(&lb));
-  }
-  s = warp_sum(s);
-  if (lane == 0) ssq[row] = s;
-}
 
 // ============================================================== decoder
 // Gather the output-patch tokens of every row and apply out_norm (one warp
@@ -1790,13 +1764,8 @@ cudaError_t t0b_launch_sgemm(const SgemmArgs &a, cudaStream_t st) {
 }
 cudaError_t t0b_launch_rownorm_split(const float *x, const float *g, __half *xh, __half *xl, float *ssq, int M, int E,
                                      cudaStream_t st) {
+  if (E % 4) return cudaErrorInvalidValue;
   rownorm_split_kernel<<<(M + 7) / 8, 256, 0, st>>>(x, g, xh, xl, ssq, M, E);
-  return cudaGetLastError();
-}
-cudaError_t t0b_launch_resid_split(float *x, const float *y, const float *g, __half *xh, __half *xl, float *ssq,
-                                   int M, int E, cudaStream_t st) {
-  if (E % 128) return cudaErrorInvalidValue;
-  resid_split_kernel<<<(M + 7) / 8, 256, 0, st>>>(x, y, g, xh, xl, ssq, M, E);
   return cudaGetLastError();
 }
 cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {

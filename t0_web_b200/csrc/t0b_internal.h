@@ -90,9 +90,6 @@ inline int t0b_weight_shift(float max_d, int qt) {
 }
 cudaError_t t0b_launch_prep(const PrepArgs &a, cudaStream_t st);
 cudaError_t t0b_launch_sgemm(const SgemmArgs &a, cudaStream_t st);
-// x[m, :] += y[m, :]; xh/xl = split(x * g); ssq[m] = sum x^2 (one slot).
-cudaError_t t0b_launch_resid_split(float *x, const float *y, const float *g, __half *xh, __half *xl, float *ssq,
-                                   int M, int E, cudaStream_t st);
 cudaError_t t0b_launch_rownorm_split(const float *x, const float *g, __half *xh, __half *xl, float *ssq, int M, int E,
                                      cudaStream_t st);
 cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st);

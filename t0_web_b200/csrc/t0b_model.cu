@@ -549,27 +549,30 @@ cudaError_t qgemm(t0b_model *m, const __half *ah, const __half *al, int M, int K
 }
 
 // Residual branch output GEMM (wO or mlp.2): x += A . W^T + bias, then the
-// split of x * gnext and its sum of squares for the next RMSNorm-fused GEMM.
-// The tensor-core path writes the branch output to `ybuf` and a row kernel
-// does the rest; the small-M path fuses it into the GEMM epilogue.  Sets
-// *ssq_nt to the number of partial sums of squares per row it leaves.
+// split of x * gnext and its sums of squares for the next RMSNorm-fused GEMM.
+// The tensor-core path adds into x with TMA reduce-adds from its epilogue and
+// a row kernel does the split; the small-M path fuses everything into its
+// epilogue.  Sets *ssq_nt to the number of partial sums of squares per row.
 cudaError_t resid_gemm(t0b_model *m, const __half *ah, const __half *al, int M, int K, const uint8_t *W,
-                       int wshift, const float *bias, float *x, const float *gnext, float *ybuf, int *ssq_nt) {
+                       int wshift, const float *bias, float *x, const float *gnext, int *ssq_nt) {
   const int E = m->E;
   Epi r{};
   r.M = M;
   r.N = E;
   r.bias = bias;
   if (use_tc(m, M, K, r)) {
+    // the epilogue adds the branch output into x with TMA reduce-adds (in
+    // L2), then a row kernel makes x * gnext's split and sum of squares
     r.kind = EPI_PLAIN;
-    r.y = ybuf;
+    r.y = x;
     r.ldy = E;
+    r.reduce_add = 1;
     cudaError_t e = qgemm(m, ah, al, M, K, W, E, wshift, r);
     if (e != cudaSuccess) return e;
     *ssq_nt = 1;
-    return launch(m, KC_OTHER, 0.0, (double)M * E * 16.0, [&] {
-      return t0b_launch_resid_split(x, ybuf, gnext, m->xh.as<__half>(), m->xl.as<__half>(), m->ssq.as<float>(), M,
-                                    E, m->stream);
+    return launch(m, KC_OTHER, 0.0, (double)M * E * 8.0, [&] {
+      return t0b_launch_rownorm_split(x, gnext, m->xh.as<__half>(), m->xl.as<__half>(), m->ssq.as<float>(), M, E,
+                                      m->stream);
     });
   }
   r.kind = EPI_RESID;
@@ -779,10 +782,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
       const double fl = (double)R * m->H * (p * (p + 1) / 2.0) * 4.0 * (E / m->H);
       LAUNCH(launch(m, KC_ATTN_TIME, fl, T * (3.0 * E * 4 + E * 4.0), [&] { return t0b_launch_attn_time(aa, m->stream); }));
     }
-    // the q|k|v buffer is free again: it holds the residual branch outputs
-    float *ybuf = m->qkv.as<float>();
-    LAUNCH(resid_gemm(m, m->ah.as<__half>(), m->al.as<__half>(), M, E, w.wo, w.sh_o, w.bo, x, w.g_mlp, ybuf,
-                      &ssq_nt));
+    LAUNCH(resid_gemm(m, m->ah.as<__half>(), m->al.as<__half>(), M, E, w.wo, w.sh_o, w.bo, x, w.g_mlp, &ssq_nt));
 
     Epi sg{};
     sg.kind = EPI_SWIGLU;
@@ -798,8 +798,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
     LAUNCH(qgemm(m, m->xh.as<__half>(), m->xl.as<__half>(), M, E, w.w0, 2 * F, w.sh_0, sg));
 
     const float *gnext = (l + 1 < m->L) ? m->layers[l + 1].g_attn : m->out_g;
-    LAUNCH(resid_gemm(m, m->hh.as<__half>(), m->hl.as<__half>(), M, F, w.w2, w.sh_2, w.b2, x, gnext, ybuf,
-                      &ssq_nt));
+    LAUNCH(resid_gemm(m, m->hh.as<__half>(), m->hl.as<__half>(), M, F, w.w2, w.sh_2, w.b2, x, gnext, &ssq_nt));
   }
 
   // decoder on the output patches only: rmsnorm(out_norm) -> residual block
