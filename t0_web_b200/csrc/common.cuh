@@ -136,6 +136,80 @@ T0B_DEV void umma_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
+// ------------------------------------------------- CTA pairs (cta_group::2)
+// Two CTAs of a 2-CTA cluster share one MMA: A rows split between the CTAs
+// (each holds its 128 rows), B columns split between them (CTA 0 holds the
+// first N/2), each CTA's TMEM receives its own 128 rows x N columns.  The
+// MMA is issued by CTA 0; operand tiles sit at the same shared-memory
+// offsets in both CTAs.
+T0B_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+T0B_DEV uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+T0B_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+T0B_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// arrive on an mbarrier given by its shared::cluster address, possibly in
+// the peer CTA (default release semantics)
+T0B_DEV void mbar_arrive_cluster(uint32_t cl_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
+}
+// 2-D tiled TMA load into this CTA's shared memory whose completion bytes
+// are counted on an mbarrier that may sit in the peer CTA (shared::cluster
+// address `bar_cl`).  No multicast.
+T0B_DEV void tma_load_2d_pair(void *dst, const void *tmap, uint32_t bar_cl, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)tmap), "r"(bar_cl), "r"(x), "r"(y)
+      : "memory");
+}
+// TMEM allocation for a CTA pair: one warp (same warp index) of each CTA.
+T0B_DEV void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+T0B_DEV void tmem_relinquish_pair() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;"); }
+T0B_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D (+)= A . B^T over the CTA pair (issued by CTA 0, one thread).
+T0B_DEV void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the mbarrier at this shared-memory offset in both CTAs of
+// the pair when the pair MMAs issued so far by this thread complete (one
+// commit signalling both CTAs; this is not a TMA load).
+T0B_DEV void umma_commit_pair_both(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+// Same, for the mbarrier at shared::cluster address `bar_cl` only.
+T0B_DEV void umma_commit_pair(uint32_t bar_cl) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cl)
+               : "memory");
+}
+
 // 32 lanes x 32 consecutive f32 columns -> 32 registers per thread.
 T0B_DEV void tmem_ld32(uint32_t taddr, float *v) {
   uint32_t r[32];

@@ -38,9 +38,18 @@
 //               in shared memory and written by TMA stores.
 #include <cuda.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "common.cuh"
 #include "epilogue.cuh"
 #include "t0b_internal.h"
+
+// 1: CTA-pair kernel (cta_group::2) for every launch; 0: single-CTA kernel
+#ifndef T0B_TC_PAIR
+#define T0B_TC_PAIR 1
+#endif
 
 namespace {
 
@@ -96,25 +105,6 @@ T0B_DEV void tmem_ld_pair16(uint32_t taddr, float *v, float scale) {
   tmem_ld16x2(taddr, taddr + BN, v, c);
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = (v[i] + c[i]) * scale;
-}
-
-// 16 values as f16 hi/lo pairs, 8 per 16-byte store.
-T0B_DEV void store_split16(__half *hi, __half *lo, size_t off, const float *v) {
-#pragma unroll
-  for (int i = 0; i < 16; i += 8) {
-    uint32_t h[4], l[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      __half h0, l0, h1, l1;
-      split_f16(v[i + 2 * j], h0, l0);
-      split_f16(v[i + 2 * j + 1], h1, l1);
-      __half2 hh = __halves2half2(h0, h1), ll = __halves2half2(l0, l1);
-      h[j] = *reinterpret_cast<uint32_t *>(&hh);
-      l[j] = *reinterpret_cast<uint32_t *>(&ll);
-    }
-    *reinterpret_cast<uint4 *>(hi + off + i) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4 *>(lo + off + i) = make_uint4(l[0], l[1], l[2], l[3]);
-  }
 }
 
 T0B_DEV void store_f32x16(float *dst, const float *v) {
@@ -496,6 +486,371 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------- CTA pairs
+// The same product on CTA pairs (cta_group::2): a 2-CTA cluster owns a
+// 256-token x 256-column output tile.  CTA r holds tokens m0 + 128 r of the
+// activation planes and weight rows 128 r .. 128 r + 127 of the tile (SWIGLU:
+// CTA 0 the 128 gate rows, CTA 1 the matching up rows); one M = 256 MMA
+// issued by CTA 0 reads both CTAs' tiles and writes each CTA's 128 rows x
+// 256 columns into its own TMEM.  Per CTA and K stage this halves the
+// dequantized weight tile, the raw blocks and the weight-operand reads
+// (~92 KB of shared-memory traffic instead of ~144 KB for three MMA terms).
+// Roles are those of the single-CTA kernel; the dequant warps form two
+// groups of four that take alternate stages.  Barriers that the peer CTA
+// feeds live in CTA 0: the activation-full barrier (TMA byte counts of both
+// CTAs), the dequantized-full barrier and the accumulator-empty barrier.
+// CTA 0's MMA thread signals the stage-empty and accumulator-full barriers
+// of both CTAs with one commit each.
+#ifndef T0B_PXS
+#define T0B_PXS 4
+#endif
+#ifndef T0B_PWS
+#define T0B_PWS 4
+#endif
+#ifndef T0B_PRS
+#define T0B_PRS 4
+#endif
+#ifndef T0B_STG_N
+#define T0B_STG_N 2
+#endif
+constexpr int PXS = T0B_PXS, PWS = T0B_PWS, PRS = T0B_PRS;  // ring depths per CTA
+constexpr int STG_N = T0B_STG_N;                             // staging buffers per epilogue warp
+constexpr uint32_t PW_TILE = 128 * BK * 2;    // 8 KB: one of hi / lo for this CTA's 128 weight rows
+constexpr uint32_t P_OFF_XH = 0;
+constexpr uint32_t P_OFF_XL = P_OFF_XH + PXS * X_TILE;
+constexpr uint32_t P_OFF_WH = P_OFF_XL + PXS * X_TILE;
+constexpr uint32_t P_OFF_WL = P_OFF_WH + PWS * PW_TILE;
+constexpr uint32_t P_OFF_RAW = P_OFF_WL + PWS * PW_TILE;  // 128 KB
+
+template <int QT>
+struct PCfg {
+  static constexpr uint32_t RAW_SLOT = (uint32_t)TQ<QT>::rawb * 128;
+  static constexpr uint32_t OFF_EPI = P_OFF_RAW + PRS * RAW_SLOT;
+  static constexpr uint32_t OFF_STG = (OFF_EPI + BN * 4 + 1023u) & ~1023u;
+  static constexpr uint32_t OFF_BAR = OFF_STG + STG_N * EPI_WARPS * STG_BYTES;
+  static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;
+  static_assert(SMEM <= 232448, "shared memory over the 227 KB per-block limit");
+};
+
+template <int N>
+T0B_DEV void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int QT>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    gemm_q_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
+                          const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_y,
+                          const __grid_constant__ CUtensorMap tm_zh, const __grid_constant__ CUtensorMap tm_zl,
+                          TcParams prm) {
+  using C = PCfg<QT>;
+  constexpr int BPB = TQ<QT>::bpb, RAWB = TQ<QT>::rawb;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_u32 = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t *smem = smem_raw + (base_u32 - smem_u32(smem_raw));
+  if (cluster_size() != 2) {  // launched without the 2-CTA cluster: nothing is touched
+    if (threadIdx.x == 0) record_error(prm.err, T0B_DEVERR_SHAPE);
+    return;
+  }
+  const uint32_t rank = cluster_rank();
+
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
+  uint64_t *x_full = bars;               // [PXS] TMA bytes of both CTAs -> MMA (CTA 0's)
+  uint64_t *x_empty = x_full + PXS;      // [PXS] MMA -> TMA (each CTA's)
+  uint64_t *raw_full = x_empty + PXS;    // [PRS] TMA -> dequant
+  uint64_t *raw_empty = raw_full + PRS;  // [PRS] dequant -> TMA
+  uint64_t *w_full = raw_empty + PRS;    // [PWS] dequant warps of both CTAs -> MMA (CTA 0's)
+  uint64_t *w_empty = w_full + PWS;      // [PWS] MMA -> dequant (each CTA's)
+  uint64_t *acc_full = w_empty + PWS;    // MMA -> epilogue (each CTA's)
+  uint64_t *acc_empty = acc_full + 1;    // epilogue warps of both CTAs -> MMA (CTA 0's)
+  uint64_t *mma_done = acc_empty + 1;    // every issued MMA has completed (CTA 0)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(mma_done + 2);
+  float *epi_s = reinterpret_cast<float *>(smem + C::OFF_EPI);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int M = prm.M, K = prm.K;
+  const int S = K / BK;
+  const bool swiglu = prm.swiglu_F > 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < PXS; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], 1);
+    }
+    for (int i = 0; i < PRS; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], 128);
+    }
+    for (int i = 0; i < PWS; ++i) {
+      mbar_init(&w_full[i], 8);  // lane 0 of the 4 dequant warps of a stage, in both CTAs
+      mbar_init(&w_empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 2 * EPI_WARPS);  // lane 0 of every epilogue warp, both CTAs
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_xh);
+    prefetch_tmap(&tm_xl);
+    prefetch_tmap(&tm_w);
+    if (swiglu) {
+      prefetch_tmap(&tm_zh);
+      prefetch_tmap(&tm_zl);
+    } else {
+      prefetch_tmap(&tm_y);
+    }
+  }
+  if (warp == 1) {  // the same warp in both CTAs allocates the pair's columns
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers are initialised before either signals the other
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // pair tile -> (this CTA's first token, this CTA's first weight row, n tile)
+  auto tile_rows = [&](int tile, int &m0, int &wrow, int &nt) {
+    nt = tile % prm.n_tiles_n;
+    m0 = (tile / prm.n_tiles_n) * (2 * BM) + BM * (int)rank;
+    if (swiglu)
+      wrow = (rank == 0 ? 0 : prm.swiglu_F) + nt * 128;
+    else
+      wrow = nt * BN + 128 * (int)rank;
+  };
+  auto lead = [](const uint64_t *b) { return mapa_shared(smem_u32(b), 0); };
+
+  if (warp < 4) {
+    if (warp == 0 && lane == 0) {
+      // ---------------------------------------------------------- activation producer (both CTAs)
+      uint32_t g = 0;
+      for (int tile = pair; tile < prm.n_tiles && !*abort_flag; tile += npairs) {
+        int m0, wrow, nt;
+        tile_rows(tile, m0, wrow, nt);
+        for (int s = 0; s < S && !*abort_flag; ++s, ++g) {
+          const uint32_t xs = g % PXS;
+          if (g >= PXS && !mbar_wait(&x_empty[xs], ((g / PXS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag))
+            break;
+          if (rank == 0) mbar_arrive_expect_tx(&x_full[xs], 4 * X_TILE);  // hi + lo of both CTAs
+          const uint32_t fb = lead(&x_full[xs]);
+          tma_load_2d_pair(smem + P_OFF_XH + xs * X_TILE, &tm_xh, fb, s * BK, m0);
+          tma_load_2d_pair(smem + P_OFF_XL + xs * X_TILE, &tm_xl, fb, s * BK, m0);
+        }
+      }
+    } else if (warp == 2 && lane == 0) {
+      // ---------------------------------------------------------- raw weight producer (both CTAs)
+      // separate from the activation producer so that raw blocks run ahead
+      // as far as the dequant warps allow, whatever the MMAs are waiting for
+      uint32_t g = 0;
+      for (int tile = pair; tile < prm.n_tiles && !*abort_flag; tile += npairs) {
+        int m0, wrow, nt;
+        tile_rows(tile, m0, wrow, nt);
+        for (int s = 0; s < S && !*abort_flag; ++s, ++g) {
+          const uint32_t rs = g % PRS;
+          if (g >= PRS && !mbar_wait(&raw_empty[rs], ((g / PRS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag))
+            break;
+          const int x = (s * BPB) & ~15;  // aligned window holding block column s
+          mbar_arrive_expect_tx(&raw_full[rs], C::RAW_SLOT);
+          tma_load_2d(smem + P_OFF_RAW + rs * C::RAW_SLOT, &tm_w, &raw_full[rs], x, wrow);
+        }
+      }
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+      // ---------------------------------------------------------- MMA issuer (CTA 0)
+      constexpr uint32_t idesc = idesc_f16_f32(2 * BM, BN);
+      uint32_t g = 0, it = 0;
+      for (int tile = pair; tile < prm.n_tiles && !*abort_flag; tile += npairs, ++it) {
+        if (it >= 1 && !mbar_wait(acc_empty, (it - 1) & 1, prm.err, T0B_DEVERR_WAIT_ACC, abort_flag)) break;
+        tc_fence_after();
+        for (int s = 0; s < S; ++s, ++g) {
+          const uint32_t xs = g % PXS, ws = g % PWS;
+          if (!mbar_wait(&x_full[xs], (g / PXS) & 1, prm.err, T0B_DEVERR_WAIT_X, abort_flag) ||
+              !mbar_wait(&w_full[ws], (g / PWS) & 1, prm.err, T0B_DEVERR_WAIT_DEQ, abort_flag))
+            break;
+          tc_fence_after();
+          const uint32_t xh = base_u32 + P_OFF_XH + xs * X_TILE, xl = base_u32 + P_OFF_XL + xs * X_TILE;
+          const uint32_t wh = base_u32 + P_OFF_WH + ws * PW_TILE, wl = base_u32 + P_OFF_WL + ws * PW_TILE;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint32_t ko = kk * 32;  // 16 f16 along K inside the 64-byte swizzled row
+            const uint32_t acc = (s > 0 || kk > 0) ? 1u : 0u;
+            umma_f16_pair(tmem, sw64_desc(xh + ko), sw64_desc(wh + ko), idesc, acc);
+            umma_f16_pair(tmem + BN, sw64_desc(xh + ko), sw64_desc(wl + ko), idesc, acc);
+            umma_f16_pair(tmem + BN, sw64_desc(xl + ko), sw64_desc(wh + ko), idesc, 1u);
+          }
+          umma_commit_pair_both(&x_empty[xs]);
+          umma_commit_pair_both(&w_empty[ws]);
+        }
+        if (*abort_flag) break;
+        umma_commit_pair_both(acc_full);
+      }
+      // every issued MMA completes before the pair reaches the TMEM release
+      umma_commit_pair(smem_u32(mma_done));
+      mbar_wait(mma_done, 0, prm.err, T0B_DEVERR_WAIT_ACC, nullptr);
+    }
+  } else if (warp < 12) {
+    // ------------------------------------------------------------ dequant (both CTAs)
+    const int grp = (warp - 4) >> 2;            // stages g with g % 2 == grp
+    const int r = (threadIdx.x - 128) & 127;    // tile row 0..127 of this CTA's weight rows
+    uint32_t g = 0;
+    bool ok = true;
+    for (int tile = pair; tile < prm.n_tiles && ok && !*abort_flag; tile += npairs) {
+      for (int s = 0; s < S; ++s, ++g) {
+        if ((int)(g & 1) != grp) continue;
+        const uint32_t ws = g % PWS, rs = g % PRS;
+        bool got = true;
+        if (lane == 0)
+          got = (g < PWS ||
+                 mbar_wait(&w_empty[ws], ((g / PWS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag)) &&
+                mbar_wait(&raw_full[rs], (g / PRS) & 1, prm.err, T0B_DEVERR_WAIT_W, abort_flag);
+        got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+        __syncwarp();
+        if (!got) {
+          ok = false;
+          break;
+        }
+        uint8_t *whs = smem + P_OFF_WH + ws * PW_TILE;
+        uint8_t *wls = smem + P_OFF_WL + ws * PW_TILE;
+        const int off = (s * BPB) & 15;  // block start inside the aligned window
+        const uint8_t *slot = smem + P_OFF_RAW + rs * C::RAW_SLOT;
+        dequant_row_at<QT>(off, slot + r * RAWB, prm.wscale, whs, wls, r);
+        mbar_arrive(&raw_empty[rs]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(lead(&w_full[ws]));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int quarter = (warp - 12) >> 2;
+    const int et = threadIdx.x - 384;
+    const Epi &e = prm.epi;
+    float *sb = epi_s;
+    uint8_t *stg0 = smem + C::OFF_STG + (warp - 12) * STG_N * STG_BYTES;
+    uint32_t ck = 0;  // chunks written by this warp (staging buffer = ck % STG_N)
+    uint32_t it = 0;
+    for (int tile = pair; tile < prm.n_tiles; tile += npairs, ++it) {
+      int m0, wrow, nt;
+      tile_rows(tile, m0, wrow, nt);
+      epi_bar();
+      if (et < BN) {
+        const int c = et;
+        const int f = swiglu ? (c < 128 ? nt * 128 + c : e.F + nt * 128 + (c - 128)) : nt * BN + c;
+        sb[c] = e.bias ? e.bias[f] : 0.0f;
+      }
+      epi_bar();
+      const int row0 = m0 + 32 * q;
+      const int m = row0 + lane;
+      const bool live = m < M;
+      const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
+      const float sc = prm.acc_scale * (live ? 1.0f / epi_row_denom(e, m) : 1.0f);
+      bool have = mbar_wait(acc_full, it & 1, prm.err, T0B_DEVERR_WAIT_ACC, abort_flag) && !*abort_flag;
+      have = __all_sync(0xffffffffu, have);
+      tc_fence_after();
+      bool released = false;
+      auto release = [&] {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(lead(acc_empty));
+        released = true;
+      };
+      auto next_stage_buf = [&]() -> uint8_t * {
+        uint8_t *b = stg0 + (ck % STG_N) * STG_BYTES;
+        ++ck;
+        if (lane == 0) bulk_wait_read<STG_N - 1>();  // the store that last used this buffer has read it
+        __syncwarp();
+        return b;
+      };
+      if (have) {
+        if (swiglu) {
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            const int g0 = 32 * quarter + 16 * c;
+            float gv[16], uv[16];
+            tmem_ld_pair16(trow + g0, gv, sc);
+            tmem_ld_pair16(trow + 128 + g0, uv, sc);
+            if (c == 1) release();
+            uint32_t h[8], l[8];
+#pragma unroll
+            for (int i = 0; i < 16; i += 2) {
+              float z[2];
+#pragma unroll
+              for (int k = 0; k < 2; ++k) {
+                const float gg = gv[i + k] + sb[g0 + i + k];
+                const float uu = uv[i + k] + sb[128 + g0 + i + k];
+                z[k] = gg * __frcp_rn(1.0f + __expf(-gg)) * uu;
+                gv[i + k] = z[k];
+              }
+              __half h0, l0, h1, l1;
+              split_f16(z[0], h0, l0);
+              split_f16(z[1], h1, l1);
+              __half2 hh = __halves2half2(h0, h1), ll = __halves2half2(l0, l1);
+              h[i / 2] = *reinterpret_cast<uint32_t *>(&hh);
+              l[i / 2] = *reinterpret_cast<uint32_t *>(&ll);
+            }
+            uint8_t *stg = next_stage_buf();
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const uint32_t o = lane * 32 + ((j ^ ((lane >> 2) & 1)) << 4);
+              *reinterpret_cast<uint4 *>(stg + o) = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+              *reinterpret_cast<uint4 *>(stg + 1024 + o) =
+                  make_uint4(l[4 * j], l[4 * j + 1], l[4 * j + 2], l[4 * j + 3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tm_zh, stg, nt * 128 + g0, row0);
+              tma_store_2d(&tm_zl, stg + 1024, nt * 128 + g0, row0);
+              bulk_commit();
+            }
+            if (e.z32 && live) store_f32x16(e.z32 + (size_t)m * e.F + (size_t)nt * 128 + g0, gv);
+          }
+        } else {  // EPI_PLAIN
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            const int c0 = 64 * quarter + 16 * c;
+            float v[16];
+            tmem_ld_pair16(trow + c0, v, sc);
+            if (c == 3) release();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] += sb[c0 + i];
+            uint8_t *stg = next_stage_buf();
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              *reinterpret_cast<float4 *>(stg + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                  make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (e.reduce_add)
+                tma_reduce_add_2d(&tm_y, stg, nt * BN + c0, row0);
+              else
+                tma_store_2d(&tm_y, stg, nt * BN + c0, row0);
+              bulk_commit();
+            }
+          }
+        }
+      }
+      if (!released) release();
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA frees the pair's TMEM while the other may still use it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
 // ---------------------------------------------------------------- host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -535,6 +890,27 @@ int sm_count() {
     if (n_sm <= 0) n_sm = 148;
   }
   return n_sm;
+}
+
+// Number of 2-CTA clusters of `kfn` (launched as `cfg`) that fit on the
+// device at once, cached per kernel and device.
+int max_pairs(const void *kfn, const cudaLaunchConfig_t &cfg) {
+  static std::mutex mu;
+  static std::map<std::pair<const void *, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find({kfn, dev});
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t c = cfg;
+  c.gridDim = dim3(2 * sm_count());
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kfn, &c) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    return 0;
+  }
+  cache[{kfn, dev}] = n;
+  return n;
 }
 
 template <int QT>
@@ -580,12 +956,37 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
   prm.acc_scale = ldexpf(1.0f, -wshift);
   prm.epi = epi;
   prm.err = err;
+#if T0B_TC_PAIR
+  (void)sizeof(C);
+  using P = PCfg<QT>;
+  prm.n_tiles = prm.n_tiles_n * ((M + 2 * BM - 1) / (2 * BM));
+  auto kfn = gemm_q_tc_pair_kernel<QT>;
+  cudaError_t e = t0b_smem_limit((const void *)kfn, P::SMEM);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(NTHREADS);
+  cfg.dynamicSmemBytes = P::SMEM;
+  cfg.stream = st;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const int pairs = max_pairs((const void *)kfn, cfg);
+  if (pairs < 1) return cudaErrorInvalidConfiguration;
+  const int np = prm.n_tiles < pairs ? prm.n_tiles : pairs;  // persistent: one CTA pair per SM pair
+  cfg.gridDim = dim3(2 * np);
+  return cudaLaunchKernelEx(&cfg, kfn, txh, txl, tw, ty, tzh, tzl, prm);
+#else
   auto kfn = gemm_q_tc_kernel<QT>;
   cudaError_t e = t0b_smem_limit((const void *)kfn, C::SMEM);
   if (e != cudaSuccess) return e;
   const int grid = prm.n_tiles < sm_count() ? prm.n_tiles : sm_count();  // persistent: one CTA per SM
   kfn<<<grid, NTHREADS, C::SMEM, st>>>(txh, txl, tw, ty, tzh, tzl, prm);
   return cudaGetLastError();
+#endif
 }
 
 }  // namespace

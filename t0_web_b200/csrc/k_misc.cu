@@ -528,186 +528,15 @@ __global__ void __launch_bounds__(128) attn_time_kernel(AttnArgs a) {
   }
 }
 
-// Register-tiled time attention for one (variate row, head), for p <= 131
-// (same semantics as attn_time_kernel).  q, k, v of the row's head are staged
-// in shared memory (q and k normalised and rotated on the way in; q and k
-// rows with their 16-byte units swizzled by row/4 so the tile loads below
-// are bank-conflict free), then
-//   1. S = q k^T / 8 on the causal lower-triangular 4x4 tiles, 16 FMAs per
-//      pair of 16-byte loads;
-//   2. row softmax over the attendable keys [first valid patch, i] (a
-//      whole-padding query row gets 1/p everywhere), probabilities in place;
-//   3. O = P v on 4-query x 4-dim tiles, written as the f16 hi/lo split.
-constexpr int kAttnTiledMaxP = 131;
-
-__global__ void __launch_bounds__(128) attn_time_tiled_kernel(AttnArgs a) {
-  pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
-  extern __shared__ float4 sm4[];
-  float *sm = reinterpret_cast<float *>(sm4);
-  const int r = blockIdx.x, h = blockIdx.y;
-  const int p = a.p, E = a.E;
-  const int PP = (p + 3) & ~3;  // rows padded to whole 4-row tiles
-  const int T = PP / 4;
-  float *Qs = sm;             // [PP][64] swizzled
-  float *Ks = Qs + PP * 64;   // [PP][64] swizzled
-  float *Vs = Ks + PP * 64;   // [PP][64]
-  float *Ss = Vs + PP * 64;   // [PP][PP] scores, then probabilities
-  const size_t tok0 = (size_t)r * p;
-  const float *rope_c = a.use_rope ? a.rope : nullptr;
-  const float *rsc = a.rope + (size_t)2 * p * 64, *rsc_inv = a.rope + (size_t)3 * p * 64;
-  // ---- stage q, k, v: every 16-byte copy issued at once (cp.async), rows
-  // p..PP-1 zero, then QK-norm + RoPE in place (16 threads per token)
-  for (int i = threadIdx.x; i < PP * 16; i += blockDim.x) {
-    const int j = i >> 4, c = i & 15;
-    const int qo = j * 64 + ((((c ^ (j >> 2)) & 7) | (c & 8)) << 2);
-    if (j < p) {
-      const float *row = a.qkv + (tok0 + j) * 3 * E + h * 64 + c * 4;
-      cp_async16(Qs + qo, row);
-      cp_async16(Ks + qo, row + E);
-      cp_async16(Vs + j * 64 + c * 4, row + 2 * E);
-    } else {
-      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-      *reinterpret_cast<float4 *>(Qs + qo) = z;
-      *reinterpret_cast<float4 *>(Ks + qo) = z;
-      *reinterpret_cast<float4 *>(Vs + j * 64 + c * 4) = z;
-    }
-  }
-  cp_async_commit();
-  cp_async_wait<0>();
-  __syncthreads();
-  for (int base = 0; base < p * 16; base += 128) {
-    const int i = base + threadIdx.x;
-    const bool ok = i < p * 16;  // all lanes run every iteration for the half-warp sums
-    const int j = ok ? i >> 4 : 0, c = i & 15, d = c * 4;
-    const int qo = j * 64 + ((((c ^ (j >> 2)) & 7) | (c & 8)) << 2);
-    float4 qv = *reinterpret_cast<const float4 *>(Qs + qo);
-    float4 kv = *reinterpret_cast<const float4 *>(Ks + qo);
-    const float sq = half_warp_sum(qv.x * qv.x + qv.y * qv.y + qv.z * qv.z + qv.w * qv.w);
-    const float sk = half_warp_sum(kv.x * kv.x + kv.y * kv.y + kv.z * kv.z + kv.w * kv.w);
-    if (ok) {
-      *reinterpret_cast<float4 *>(Qs + qo) = qk_norm_rope4(qv, sq, a.qn, d, rope_c, rsc, p, j);
-      *reinterpret_cast<float4 *>(Ks + qo) = qk_norm_rope4(kv, sk, a.kn, d, rope_c, rsc_inv, p, j);
-    }
-  }
-  __syncthreads();
-  const int lo = a.row_first_valid[r];
-  // ---- 1. scores on the lower-triangular 4x4 tiles (qt >= kt)
-  const int n1 = T * (T + 1) / 2;
-  for (int t = threadIdx.x; t < n1; t += blockDim.x) {
-    int qt = (int)((sqrtf(8.0f * t + 1.0f) - 1.0f) * 0.5f);
-    while (qt * (qt + 1) / 2 > t) --qt;
-    while ((qt + 1) * (qt + 2) / 2 <= t) ++qt;
-    const int kt = t - qt * (qt + 1) / 2;
-    float acc[4][4];
-#pragma unroll
-    for (int x = 0; x < 4; ++x)
-#pragma unroll
-      for (int y = 0; y < 4; ++y) acc[x][y] = 0.0f;
-    const float *qb = Qs + qt * 256, *kb = Ks + kt * 256;
-    const int qs = qt & 7, ks = kt & 7;
-#pragma unroll 4
-    for (int c = 0; c < 16; ++c) {
-      const int qc = ((c ^ qs) & 7) | (c & 8), kc = ((c ^ ks) & 7) | (c & 8);
-      float4 q4[4], k4[4];
-#pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        q4[x] = *reinterpret_cast<const float4 *>(qb + x * 64 + qc * 4);
-        k4[x] = *reinterpret_cast<const float4 *>(kb + x * 64 + kc * 4);
-      }
-#pragma unroll
-      for (int x = 0; x < 4; ++x)
-#pragma unroll
-        for (int y = 0; y < 4; ++y) {
-          acc[x][y] = fmaf(q4[x].x, k4[y].x, acc[x][y]);
-          acc[x][y] = fmaf(q4[x].y, k4[y].y, acc[x][y]);
-          acc[x][y] = fmaf(q4[x].z, k4[y].z, acc[x][y]);
-          acc[x][y] = fmaf(q4[x].w, k4[y].w, acc[x][y]);
-        }
-    }
-#pragma unroll
-    for (int x = 0; x < 4; ++x)
-      *reinterpret_cast<float4 *>(Ss + (qt * 4 + x) * PP + kt * 4) =
-          make_float4(acc[x][0] * 0.125f, acc[x][1] * 0.125f, acc[x][2] * 0.125f, acc[x][3] * 0.125f);
-  }
-  __syncthreads();
-  // ---- 2. softmax per query row, probabilities in place (zero elsewhere)
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = warp; i < PP; i += 4) {
-    float *srow = Ss + i * PP;
-    if (i >= p) {
-      for (int j = lane; j < PP; j += 32) srow[j] = 0.0f;
-    } else if (i < lo) {  // whole-padding query: every key blocked -> uniform over all p
-      const float u = 1.0f / (float)p;
-      for (int j = lane; j < PP; j += 32) srow[j] = j < p ? u : 0.0f;
-    } else {
-      float mx = -INFINITY;
-      for (int j = lo + lane; j <= i; j += 32) mx = fmaxf(mx, srow[j]);
-#pragma unroll
-      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      float sum = 0.0f;
-      for (int j = lo + lane; j <= i; j += 32) {
-        const float e = expf(srow[j] - mx);
-        srow[j] = e;
-        sum += e;
-      }
-      sum = warp_sum(sum);
-      __syncwarp();
-      for (int j = lane; j < PP; j += 32) srow[j] = (j >= lo && j <= i) ? srow[j] / sum : 0.0f;
-    }
-  }
-  __syncthreads();
-  // ---- 3. O = P v on 4-query x 4-dim tiles
-  const int n3 = T * 16;
-  for (int t = threadIdx.x; t < n3; t += blockDim.x) {
-    const int qt = t >> 4, dt = t & 15;
-    const int i0 = qt * 4;
-    const bool any_masked = i0 < lo;
-    const int j0 = any_masked ? 0 : lo;
-    const int j1 = any_masked ? p : min(i0 + 4, p);  // exclusive
-    float acc[4][4];
-#pragma unroll
-    for (int x = 0; x < 4; ++x)
-#pragma unroll
-      for (int y = 0; y < 4; ++y) acc[x][y] = 0.0f;
-    const float *pb = Ss + i0 * PP;
-    for (int j = j0; j < j1; ++j) {
-      const float4 v = *reinterpret_cast<const float4 *>(Vs + j * 64 + dt * 4);
-#pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        const float pj = pb[x * PP + j];
-        acc[x][0] = fmaf(pj, v.x, acc[x][0]);
-        acc[x][1] = fmaf(pj, v.y, acc[x][1]);
-        acc[x][2] = fmaf(pj, v.z, acc[x][2]);
-        acc[x][3] = fmaf(pj, v.w, acc[x][3]);
-      }
-    }
-#pragma unroll
-    for (int x = 0; x < 4; ++x) {
-      const int i = i0 + x;
-      if (i >= p) break;
-      const size_t oo = (tok0 + i) * E + h * 64 + dt * 4;
-      __half hh[4], ll[4];
-#pragma unroll
-      for (int y = 0; y < 4; ++y) split_f16(acc[x][y], hh[y], ll[y]);
-      __half2 h01 = __halves2half2(hh[0], hh[1]), h23 = __halves2half2(hh[2], hh[3]);
-      __half2 l01 = __halves2half2(ll[0], ll[1]), l23 = __halves2half2(ll[2], ll[3]);
-      *reinterpret_cast<uint2 *>(a.oh + oo) =
-          make_uint2(*reinterpret_cast<uint32_t *>(&h01), *reinterpret_cast<uint32_t *>(&h23));
-      *reinterpret_cast<uint2 *>(a.ol + oo) =
-          make_uint2(*reinterpret_cast<uint32_t *>(&l01), *reinterpret_cast<uint32_t *>(&l23));
-      if (a.o32) *reinterpret_cast<float4 *>(a.o32 + oo) = make_float4(acc[x][0], acc[x][1], acc[x][2], acc[x][3]);
-    }
-  }
-}
-
 // ---------------------------------------------------------- tensor-core time attention
 // Time attention for one (variate row, head) on mma.sync tensor cores, for
-// p <= 128 (same semantics as attn_time_kernel).  f32-class products from f16
+// p <= 256 (same semantics as attn_time_kernel).  f32-class products from f16
 // MMAs: every operand is split into hi + lo f16 terms and a product is
 // hi.hi + hi.lo + lo.hi with f32 accumulation.
-//   - staging: one thread per key token and tensor loads its k or v row,
-//     applies QK-norm and RoPE to k, and stores k (row-major) and v
-//     (transposed) as f16 hi/lo in shared memory;
+//   - staging: the row's q, k and v tiles arrive by TMA (128-byte swizzled
+//     [p][32] f32 boxes); one thread per key token reads its k or v row,
+//     applies QK-norm and RoPE to k, and stores k and v as f16 hi/lo planes
+//     in shared memory;
 //   - one warp per block of 16 queries keeps its q rows in registers (normed,
 //     rotated, split into mma fragments), walks the key blocks up to the
 //     diagonal with an online softmax on the score fragments, and accumulates
@@ -1790,15 +1619,6 @@ cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
     const int use_tma = t0b_make_tmap_f32_2d(&tm, a.qkv, (uint64_t)3 * a.E, (uint64_t)a.R * a.p,
                                              (uint64_t)3 * a.E * sizeof(float), 32, (uint32_t)a.p, true) ? 1 : 0;
     attn_time_mma_kernel<<<dim3(a.R, a.H), 32 * QB, smem, st>>>(a, tm, use_tma);
-    return cudaGetLastError();
-  }
-  if (a.p <= kAttnTiledMaxP) {
-    const int PP = (a.p + 3) & ~3;
-    const size_t smem = (size_t)(PP * 64 * 3 + PP * PP) * sizeof(float);
-    cudaError_t e =
-        t0b_smem_limit((const void *)attn_time_tiled_kernel, smem);
-    if (e != cudaSuccess) return e;
-    attn_time_tiled_kernel<<<dim3(a.R, a.H), 128, smem, st>>>(a);
     return cudaGetLastError();
   }
   size_t smem = (size_t)(a.p * (65 + 64 + 64) + 4 * a.p) * sizeof(float);
