@@ -10,32 +10,42 @@
 //   t0-alpha-shaped models, and chaining all three terms into one
 //   accumulator triples the tensor core's accumulation error.
 //
-// Persistent kernel: one CTA per SM walks a queue of 128-token x 256-row
-// output tiles (weight-row tiles fastest so the CTAs in flight share their
-// activation tiles in L2).  One 32-value block column of K per pipeline
-// stage; separate rings for the activation tiles (TMA, 64-byte swizzle), the
-// raw weight blocks (TMA) and the dequantized weight tiles.  The two
+// Persistent kernel on CTA pairs (cta_group::2): each 2-CTA cluster (the
+// two SMs of a TPC) walks a queue of 256-token x 256-column output tiles
+// (weight-row tiles fastest so the pairs in flight share their activation
+// tiles in L2).  CTA r of a pair holds tokens 128 r .. 128 r + 127 of the
+// tile and half of its weight rows; one M = 256 MMA issued by CTA 0 reads
+// both CTAs' operand tiles and leaves each CTA's 128 rows x 256 columns in
+// its own TMEM.  One 32-value block column of K per pipeline stage, with
+// rings for the activation tiles (TMA, 64-byte swizzle), the raw weight
+// blocks (TMA) and the dequantized weight tiles.  The main and correction
 // accumulators fill all 512 TMEM columns; the epilogue reads them chunk by
-// chunk and releases TMEM to the next tile's MMAs when done.  Its only
-// global load is the row's RMSNorm sum of squares, fetched before the
-// accumulator is ready (the bias is staged in shared memory), and its
-// global writes are asynchronous TMA stores of swizzled 32-row chunks, so its
-// cost is a short burst of TMEM loads, math and shared-memory stores.
-// Residual adds are TMA reduce-adds of the output tile into the residual
-// stream; QK-norm and RoPE run in the attention kernels.
+// chunk and releases TMEM to the next tile's MMAs after its last load.  Its
+// only global load is the row's RMSNorm sum of squares, fetched before the
+// accumulator is ready (the bias is staged in shared memory); its global
+// writes are asynchronous TMA stores (or TMA reduce-adds into the residual
+// stream) of swizzled 32-row chunks.  QK-norm and RoPE run in the attention
+// kernels.
 //
-// Warp roles (896 threads):
-//   warp 0      TMA producer: Ah/Al tiles and the raw blocks of the tile's
-//               weight rows (16-byte aligned superset window of the 34/18-byte
-//               block), with mbarrier completion.
-//   warp 1      allocates 512 TMEM columns; lane 0 issues tcgen05.mma and
-//               tcgen05.commit.
-//   warps 4-11  dequantize raw blocks (one weight row per thread per stage)
-//               -> Wh/Wl tiles in the canonical K-major SW64 layout (generic
-//               stores + proxy fence).
+// Why pairs: a single CTA per 128 x 256 tile moves ~144 KB through shared
+// memory per K stage (72 KB of it the three MMA terms' operand reads)
+// against 768 MMA cycles and measured exactly shared-memory bound; with the
+// weight half-tiles split across the pair it is ~92 KB per CTA.
+//
+// Warp roles (896 threads per CTA, both CTAs unless noted):
+//   warp 0      TMA producer of the Ah/Al tiles (byte counts of both CTAs
+//               land on CTA 0's barrier).
+//   warp 1      allocates the pair's 512 TMEM columns; in CTA 0 lane 0
+//               issues tcgen05.mma and the commits.
+//   warp 2      TMA producer of the raw blocks of this CTA's weight rows
+//               (16-byte aligned superset window of the 34/18-byte block).
+//   warps 4-11  dequantize raw blocks (one weight row per thread per stage,
+//               two groups of four warps taking alternate stages) -> Wh/Wl
+//               tiles in the canonical K-major SW64 layout (generic stores +
+//               proxy fence).
 //   warps 12-27 epilogue, four warps per TMEM lane quadrant (64 columns
 //               each): bias + RMSNorm row scale (PLAIN) or SwiGLU, staged
-//               in shared memory and written by TMA stores.
+//               in shared memory and written by TMA.
 #include <cuda.h>
 
 #include <map>
@@ -46,25 +56,13 @@
 #include "epilogue.cuh"
 #include "t0b_internal.h"
 
-// 1: CTA-pair kernel (cta_group::2) for every launch; 0: single-CTA kernel
-#ifndef T0B_TC_PAIR
-#define T0B_TC_PAIR 1
-#endif
-
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 32;  // BK: one Q8_0/Q4_0 block column of K per stage
-constexpr int XS = 3, WS = 3, RS = 3;       // ring depths: activation, dequantized weight, raw weight
+constexpr int BM = 128, BN = 256, BK = 32;  // per CTA: 128 tokens; per pair: 256 columns; BK: one block column
 constexpr int NTHREADS = 896;
 constexpr int EPI_WARPS = 16;  // warps 12-27, four per TMEM lane quadrant
 constexpr uint32_t X_TILE = BM * BK * 2;  // 8 KB, one of hi / lo
-constexpr uint32_t W_TILE = BN * BK * 2;  // 16 KB, one of hi / lo
-constexpr uint32_t OFF_XH = 0;
-constexpr uint32_t OFF_XL = OFF_XH + XS * X_TILE;
-constexpr uint32_t OFF_WH = OFF_XL + XS * X_TILE;
-constexpr uint32_t OFF_WL = OFF_WH + WS * W_TILE;
-constexpr uint32_t OFF_RAW = OFF_WL + WS * W_TILE;  // 160 KB
-constexpr uint32_t STG_BYTES = 2048;                // per epilogue warp: one 32-row output chunk
+constexpr uint32_t STG_BYTES = 2048;      // per epilogue warp and buffer: one 32-row output chunk
 
 template <int QT>
 struct TQ;
@@ -77,17 +75,6 @@ struct TQ<4> {
   static constexpr int bpb = 18, rawb = 32;
 };
 
-template <int QT>
-struct Cfg {
-  static constexpr uint32_t RAW_SLOT = (uint32_t)TQ<QT>::rawb * BN;
-  static constexpr uint32_t OFF_EPI = OFF_RAW + RS * RAW_SLOT;  // tile bias for the epilogue
-  // output staging for the TMA stores, 1024-aligned (swizzle pattern period)
-  static constexpr uint32_t OFF_STG = (OFF_EPI + BN * 4 + 1023u) & ~1023u;
-  static constexpr uint32_t OFF_BAR = OFF_STG + EPI_WARPS * STG_BYTES;
-  static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;  // barriers + alignment slack
-  static_assert(SMEM <= 232448, "shared memory over the 227 KB per-block limit");
-};
-
 struct TcParams {
   int M, N, K;
   int swiglu_F;  // > 0: a tile is 128 gate rows + the matching 128 up rows
@@ -98,14 +85,6 @@ struct TcParams {
   Epi epi;
   int *err;
 };
-
-// 16 columns of (main + correction) accumulator for this thread's row.
-T0B_DEV void tmem_ld_pair16(uint32_t taddr, float *v, float scale) {
-  float c[16];
-  tmem_ld16x2(taddr, taddr + BN, v, c);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = (v[i] + c[i]) * scale;
-}
 
 T0B_DEV void store_f32x16(float *dst, const float *v) {
   float4 *d = reinterpret_cast<float4 *>(dst);
@@ -199,308 +178,13 @@ T0B_DEV void dequant_row_at(int off, const uint8_t *src, float wscale, uint8_t *
 
 T0B_DEV void epi_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }  // the 16 epilogue warps only
 
-template <int QT>
-__global__ void __launch_bounds__(NTHREADS, 1)
-    gemm_q_tc_kernel(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
-                     const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_y,
-                     const __grid_constant__ CUtensorMap tm_zh, const __grid_constant__ CUtensorMap tm_zl,
-                     TcParams prm) {
-  using C = Cfg<QT>;
-  constexpr int BPB = TQ<QT>::bpb, RAWB = TQ<QT>::rawb;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t base_u32 = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  uint8_t *smem = smem_raw + (base_u32 - smem_u32(smem_raw));
-
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
-  uint64_t *x_full = bars;              // [XS] TMA -> MMA
-  uint64_t *x_empty = x_full + XS;      // [XS] MMA -> TMA
-  uint64_t *raw_full = x_empty + XS;    // [RS] TMA -> dequant
-  uint64_t *raw_empty = raw_full + RS;  // [RS] dequant -> TMA
-  uint64_t *w_full = raw_empty + RS;    // [WS] dequant -> MMA
-  uint64_t *w_empty = w_full + WS;      // [WS] MMA -> dequant
-  uint64_t *acc_full = w_empty + WS;    // MMA -> epilogue
-  uint64_t *acc_empty = acc_full + 1;   // epilogue -> MMA (TMEM drained)
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 1);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(acc_empty + 2);
-  float *epi_s = reinterpret_cast<float *>(smem + C::OFF_EPI);  // [2][BN]
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int M = prm.M, K = prm.K;
-  const int S = K / BK;
-  const bool swiglu = prm.swiglu_F > 0;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < XS; ++i) {
-      mbar_init(&x_full[i], 1);
-      mbar_init(&x_empty[i], 1);
-    }
-    for (int i = 0; i < RS; ++i) {
-      mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], 256);
-    }
-    for (int i = 0; i < WS; ++i) {
-      mbar_init(&w_full[i], 256);
-      mbar_init(&w_empty[i], 1);
-    }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 32 * EPI_WARPS);
-    *abort_flag = 0;
-    fence_barrier_init();
-    fence_proxy_async_smem();
-  }
-  if (warp == 0 && lane == 0) {
-    prefetch_tmap(&tm_xh);
-    prefetch_tmap(&tm_xl);
-    prefetch_tmap(&tm_w);
-    if (swiglu) {
-      prefetch_tmap(&tm_zh);
-      prefetch_tmap(&tm_zl);
-    } else {
-      prefetch_tmap(&tm_y);
-    }
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  // tile -> (first token, weight rows of the two 128-row halves, n tile)
-  auto tile_rows = [&](int tile, int &m0, int &wr0, int &wr1, int &nt) {
-    nt = tile % prm.n_tiles_n;
-    m0 = (tile / prm.n_tiles_n) * BM;
-    if (swiglu) {
-      wr0 = nt * 128;
-      wr1 = prm.swiglu_F + nt * 128;
-    } else {
-      wr0 = nt * BN;
-      wr1 = wr0 + 128;
-    }
-  };
-
-  if (warp < 4) {
-    if (warp == 0 && lane == 0) {
-      // ---------------------------------------------------------- producer
-      uint32_t g = 0;  // global stage counter across tiles
-      for (int tile = blockIdx.x; tile < prm.n_tiles && !*abort_flag; tile += gridDim.x) {
-        int m0, wr0, wr1, nt;
-        tile_rows(tile, m0, wr0, wr1, nt);
-        for (int s = 0; s < S && !*abort_flag; ++s, ++g) {
-          const uint32_t rs = g % RS;
-          if (g >= RS && !mbar_wait(&raw_empty[rs], ((g / RS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag))
-            break;
-          const int x = (s * BPB) & ~15;  // aligned window holding block column s
-          mbar_arrive_expect_tx(&raw_full[rs], C::RAW_SLOT);
-          uint8_t *dst = smem + OFF_RAW + rs * C::RAW_SLOT;
-          tma_load_2d(dst, &tm_w, &raw_full[rs], x, wr0);
-          tma_load_2d(dst + RAWB * 128, &tm_w, &raw_full[rs], x, wr1);
-          const uint32_t xs = g % XS;
-          if (g >= XS && !mbar_wait(&x_empty[xs], ((g / XS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag))
-            break;
-          mbar_arrive_expect_tx(&x_full[xs], 2 * X_TILE);
-          tma_load_2d(smem + OFF_XH + xs * X_TILE, &tm_xh, &x_full[xs], s * BK, m0);
-          tma_load_2d(smem + OFF_XL + xs * X_TILE, &tm_xl, &x_full[xs], s * BK, m0);
-        }
-      }
-    } else if (warp == 1 && lane == 0) {
-      // ---------------------------------------------------------- MMA issuer
-      constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
-      uint32_t g = 0, it = 0;
-      for (int tile = blockIdx.x; tile < prm.n_tiles && !*abort_flag; tile += gridDim.x, ++it) {
-        if (it >= 1 && !mbar_wait(acc_empty, (it - 1) & 1, prm.err, T0B_DEVERR_WAIT_ACC, abort_flag)) break;
-        tc_fence_after();
-        for (int s = 0; s < S; ++s, ++g) {
-          const uint32_t xs = g % XS, ws = g % WS;
-          if (!mbar_wait(&x_full[xs], (g / XS) & 1, prm.err, T0B_DEVERR_WAIT_X, abort_flag) ||
-              !mbar_wait(&w_full[ws], (g / WS) & 1, prm.err, T0B_DEVERR_WAIT_DEQ, abort_flag))
-            break;
-          tc_fence_after();
-          const uint32_t xh = base_u32 + OFF_XH + xs * X_TILE, xl = base_u32 + OFF_XL + xs * X_TILE;
-          const uint32_t wh = base_u32 + OFF_WH + ws * W_TILE, wl = base_u32 + OFF_WL + ws * W_TILE;
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint32_t ko = kk * 32;  // 16 f16 along K inside the 64-byte swizzled row
-            const uint32_t acc = (s > 0 || kk > 0) ? 1u : 0u;
-            umma_f16(tmem, sw64_desc(xh + ko), sw64_desc(wh + ko), idesc, acc);
-            umma_f16(tmem + BN, sw64_desc(xh + ko), sw64_desc(wl + ko), idesc, acc);
-            umma_f16(tmem + BN, sw64_desc(xl + ko), sw64_desc(wh + ko), idesc, 1u);
-          }
-          umma_commit(&x_empty[xs]);
-          umma_commit(&w_empty[ws]);
-        }
-        umma_commit(acc_full);
-      }
-    }
-  } else if (warp < 12) {
-    // ------------------------------------------------------------ dequant
-    const int r = threadIdx.x - 128;  // tile row 0..255
-    uint32_t g = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < prm.n_tiles && ok && !*abort_flag; tile += gridDim.x) {
-      for (int s = 0; s < S; ++s, ++g) {
-        const uint32_t ws = g % WS, rs = g % RS;
-        if ((g >= WS && !mbar_wait(&w_empty[ws], ((g / WS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag)) ||
-            !mbar_wait(&raw_full[rs], (g / RS) & 1, prm.err, T0B_DEVERR_WAIT_W, abort_flag)) {
-          ok = false;
-          break;
-        }
-        uint8_t *whs = smem + OFF_WH + ws * W_TILE;
-        uint8_t *wls = smem + OFF_WL + ws * W_TILE;
-        const int off = (s * BPB) & 15;  // block start inside the aligned window
-        const uint8_t *slot = smem + OFF_RAW + rs * C::RAW_SLOT;
-        dequant_row_at<QT>(off, slot + r * RAWB, prm.wscale, whs, wls, r);
-        mbar_arrive(&raw_empty[rs]);
-        fence_proxy_async_smem();
-        mbar_arrive(&w_full[ws]);
-      }
-    }
-  } else {
-    // ------------------------------------------------------------ epilogue
-    // Each warp owns 32 rows (its TMEM lane quadrant) x a quarter of the columns.  A
-    // chunk of 16 columns goes TMEM -> registers (bias, row scale, SwiGLU)
-    // -> this warp's swizzled staging buffer -> one TMA store by lane 0, so
-    // global writes are whole rows, asynchronous and clipped at row M.
-    const int q = warp & 3;             // TMEM lane quadrant this warp may access
-    const int quarter = (warp - 12) >> 2;  // which quarter of the tile's columns
-    const int et = threadIdx.x - 384;      // 0..511
-    const Epi &e = prm.epi;
-    float *sb = epi_s;  // tile bias [BN] (SWIGLU: 128 gate then 128 up)
-    uint8_t *stg = smem + C::OFF_STG + (warp - 12) * STG_BYTES;
-    uint32_t it = 0;
-    for (int tile = blockIdx.x; tile < prm.n_tiles; tile += gridDim.x, ++it) {
-      int m0, wr0, wr1, nt;
-      tile_rows(tile, m0, wr0, wr1, nt);
-      epi_bar();  // every epilogue thread is done with the previous tile's bias
-      if (et < BN) {
-        const int c = et;
-        const int f = swiglu ? (c < 128 ? nt * 128 + c : e.F + nt * 128 + (c - 128)) : nt * BN + c;
-        sb[c] = e.bias ? e.bias[f] : 0.0f;
-      }
-      epi_bar();
-      const int row0 = m0 + 32 * q;
-      const int m = row0 + lane;
-      const bool live = m < M;
-      const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
-      // the row scale is fetched while the tile's MMAs are still running
-      const float sc = prm.acc_scale * (live ? 1.0f / epi_row_denom(e, m) : 1.0f);
-      const bool have = mbar_wait(acc_full, it & 1, prm.err, T0B_DEVERR_WAIT_ACC, abort_flag) && !*abort_flag;
-      tc_fence_after();
-      // no early exit: every epilogue thread runs every iteration so the
-      // named barrier above always sees all 512 of them (after an abort the
-      // waits return at once and no work is done)
-      // TMEM is released as soon as this thread's last columns are in
-      // registers, so the next tile's MMAs overlap the last chunk's stores
-      bool released = false;
-      auto release = [&] {
-        tc_fence_before();
-        mbar_arrive(acc_empty);  // TMEM is free for the next tile's MMAs
-        released = true;
-      };
-      if (have) {
-        if (swiglu) {
-#pragma unroll 1
-          for (int c = 0; c < 2; ++c) {  // gate columns 32*quarter + 16c and the matching up columns
-            const int g0 = 32 * quarter + 16 * c;
-            float gv[16], uv[16];
-            tmem_ld_pair16(trow + g0, gv, sc);
-            tmem_ld_pair16(trow + 128 + g0, uv, sc);
-            if (c == 1) release();
-            uint32_t h[8], l[8];
-#pragma unroll
-            for (int i = 0; i < 16; i += 2) {
-              float z[2];
-#pragma unroll
-              for (int k = 0; k < 2; ++k) {
-                const float gg = gv[i + k] + sb[g0 + i + k];
-                const float uu = uv[i + k] + sb[128 + g0 + i + k];
-                z[k] = gg * __frcp_rn(1.0f + __expf(-gg)) * uu;
-                gv[i + k] = z[k];
-              }
-              __half h0, l0, h1, l1;
-              split_f16(z[0], h0, l0);
-              split_f16(z[1], h1, l1);
-              __half2 hh = __halves2half2(h0, h1), ll = __halves2half2(l0, l1);
-              h[i / 2] = *reinterpret_cast<uint32_t *>(&hh);
-              l[i / 2] = *reinterpret_cast<uint32_t *>(&ll);
-            }
-            if (lane == 0) bulk_wait_read0();  // the previous chunk has left the staging buffer
-            __syncwarp();
-            // 32 rows x 32 bytes per half, 32-byte swizzle: 16-byte unit j of row r at r*32 + 16*(j ^ (r>>2 & 1))
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const uint32_t o = lane * 32 + ((j ^ ((lane >> 2) & 1)) << 4);
-              *reinterpret_cast<uint4 *>(stg + o) = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
-              *reinterpret_cast<uint4 *>(stg + 1024 + o) =
-                  make_uint4(l[4 * j], l[4 * j + 1], l[4 * j + 2], l[4 * j + 3]);
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_2d(&tm_zh, stg, nt * 128 + g0, row0);
-              tma_store_2d(&tm_zl, stg + 1024, nt * 128 + g0, row0);
-              bulk_commit();
-            }
-            if (e.z32 && live) store_f32x16(e.z32 + (size_t)m * e.F + (size_t)nt * 128 + g0, gv);
-          }
-        } else {  // EPI_PLAIN
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            const int c0 = 64 * quarter + 16 * c;
-            float v[16];
-            tmem_ld_pair16(trow + c0, v, sc);
-            if (c == 3) release();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] += sb[c0 + i];
-            if (lane == 0) bulk_wait_read0();  // the previous chunk has left the staging buffer
-            __syncwarp();
-            // 32 rows x 64 bytes, 64-byte swizzle: 16-byte unit j of row r at r*64 + 16*(j ^ (r>>1 & 3))
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              *reinterpret_cast<float4 *>(stg + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
-                  make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              if (e.reduce_add)
-                tma_reduce_add_2d(&tm_y, stg, nt * BN + c0, row0);  // y += tile, in L2
-              else
-                tma_store_2d(&tm_y, stg, nt * BN + c0, row0);
-              bulk_commit();
-            }
-          }
-        }
-      }
-      if (!released) release();
-    }
-    if (lane == 0) bulk_wait_all();  // stores complete before the CTA exits
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-// ---------------------------------------------------------------- CTA pairs
-// The same product on CTA pairs (cta_group::2): a 2-CTA cluster owns a
-// 256-token x 256-column output tile.  CTA r holds tokens m0 + 128 r of the
-// activation planes and weight rows 128 r .. 128 r + 127 of the tile (SWIGLU:
-// CTA 0 the 128 gate rows, CTA 1 the matching up rows); one M = 256 MMA
-// issued by CTA 0 reads both CTAs' tiles and writes each CTA's 128 rows x
-// 256 columns into its own TMEM.  Per CTA and K stage this halves the
-// dequantized weight tile, the raw blocks and the weight-operand reads
-// (~92 KB of shared-memory traffic instead of ~144 KB for three MMA terms).
-// Roles are those of the single-CTA kernel; the dequant warps form two
-// groups of four that take alternate stages.  Barriers that the peer CTA
-// feeds live in CTA 0: the activation-full barrier (TMA byte counts of both
-// CTAs), the dequantized-full barrier and the accumulator-empty barrier.
-// CTA 0's MMA thread signals the stage-empty and accumulator-full barriers
-// of both CTAs with one commit each.
+// ---------------------------------------------------------------- the kernel
+// Barriers that the peer CTA feeds live in CTA 0: the activation-full
+// barrier (TMA byte counts of both CTAs), the dequantized-full barrier and
+// the accumulator-empty barrier.  CTA 0's MMA thread signals the
+// stage-empty and accumulator-full barriers of both CTAs with one commit
+// each.  Ring depths and staging buffers per epilogue warp can be set at
+// compile time (defaults measured best; deeper rings did not help).
 #ifndef T0B_PXS
 #define T0B_PXS 4
 #endif
@@ -531,6 +215,14 @@ struct PCfg {
   static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;
   static_assert(SMEM <= 232448, "shared memory over the 227 KB per-block limit");
 };
+
+// 16 columns of (main + correction) accumulator for this thread's row.
+T0B_DEV void tmem_ld_pair16(uint32_t taddr, float *v, float scale) {
+  float c[16];
+  tmem_ld16x2(taddr, taddr + BN, v, c);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = (v[i] + c[i]) * scale;
+}
 
 template <int N>
 T0B_DEV void bulk_wait_read() {
@@ -916,7 +608,6 @@ int max_pairs(const void *kfn, const cudaLaunchConfig_t &cfg) {
 template <int QT>
 cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows, int wshift,
                         const Epi &epi, int *err, cudaStream_t st) {
-  using C = Cfg<QT>;
   CUtensorMap txh, txl, tw;
   const uint64_t rb = (uint64_t)(K / 32) * TQ<QT>::bpb;
   if (!make_tmap_2d(&txh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ah, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BM,
@@ -951,13 +642,10 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
   prm.K = K;
   prm.swiglu_F = epi.kind == EPI_SWIGLU ? epi.F : 0;
   prm.n_tiles_n = epi.kind == EPI_SWIGLU ? epi.F / 128 : epi.N / BN;
-  prm.n_tiles = prm.n_tiles_n * ((M + BM - 1) / BM);
   prm.wscale = ldexpf(1.0f, wshift);
   prm.acc_scale = ldexpf(1.0f, -wshift);
   prm.epi = epi;
   prm.err = err;
-#if T0B_TC_PAIR
-  (void)sizeof(C);
   using P = PCfg<QT>;
   prm.n_tiles = prm.n_tiles_n * ((M + 2 * BM - 1) / (2 * BM));
   auto kfn = gemm_q_tc_pair_kernel<QT>;
@@ -979,14 +667,6 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
   const int np = prm.n_tiles < pairs ? prm.n_tiles : pairs;  // persistent: one CTA pair per SM pair
   cfg.gridDim = dim3(2 * np);
   return cudaLaunchKernelEx(&cfg, kfn, txh, txl, tw, ty, tzh, tzl, prm);
-#else
-  auto kfn = gemm_q_tc_kernel<QT>;
-  cudaError_t e = t0b_smem_limit((const void *)kfn, C::SMEM);
-  if (e != cudaSuccess) return e;
-  const int grid = prm.n_tiles < sm_count() ? prm.n_tiles : sm_count();  // persistent: one CTA per SM
-  kfn<<<grid, NTHREADS, C::SMEM, st>>>(txh, txl, tw, ty, tzh, tzl, prm);
-  return cudaGetLastError();
-#endif
 }
 
 }  // namespace
