@@ -331,7 +331,7 @@ def run_ours(args):
             tok_per_launch = (int(nv_shard.sum()) * config_block(args, nv, world)["patches_per_row"] * n_gemm
                               * args.steps / g["launches"])
             tr = tr["dram_bytes_per_token_per_launch"] * tok_per_launch
-        roofline = {"kernel": "gemm_q_tc_kernel", "bound": "tensor", "achieved": achieved, "peak": peak_tf,
+        roofline = {"kernel": "gemm_q_tc_pair_kernel", "bound": "tensor", "achieved": achieved, "peak": peak_tf,
                     "unit": "TFLOP/s", "frac": achieved / peak_tf,
                     "peak_kind": f"{peak_kind} bf16 sustained (dense cuBLAS)",
                     "traffic": tr, "avg_launch_ms": per_launch_ms,
