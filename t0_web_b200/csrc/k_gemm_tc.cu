@@ -20,7 +20,9 @@
 // rings for the activation tiles (TMA, 64-byte swizzle), the raw weight
 // blocks (TMA) and the dequantized weight tiles.  The main and correction
 // accumulators fill all 512 TMEM columns; the epilogue reads them chunk by
-// chunk and releases TMEM to the next tile's MMAs after its last load.  Its
+// chunk and releases TMEM to the next tile's MMAs after its last load
+// (PLAIN: two 16-column chunks are loaded before the first is stored;
+// SWIGLU: both chunks are computed before either is stored).  Its
 // only global load is the row's RMSNorm sum of squares, fetched before the
 // accumulator is ready (the bias is staged in shared memory); its global
 // writes are asynchronous TMA stores (or TMA reduce-adds into the residual
@@ -461,14 +463,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       };
       if (have) {
         if (swiglu) {
-#pragma unroll 1
+          // both chunks' SwiGLU values are computed (packed as f16 hi / lo)
+          // before TMEM is released; staging and stores come after
+          uint32_t hl[2][16];
+#pragma unroll
           for (int c = 0; c < 2; ++c) {
             const int g0 = 32 * quarter + 16 * c;
             float gv[16], uv[16];
             tmem_ld_pair16(trow + g0, gv, sc);
             tmem_ld_pair16(trow + 128 + g0, uv, sc);
             if (c == 1) release();
-            uint32_t h[8], l[8];
 #pragma unroll
             for (int i = 0; i < 16; i += 2) {
               float z[2];
@@ -483,16 +487,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               split_f16(z[0], h0, l0);
               split_f16(z[1], h1, l1);
               __half2 hh = __halves2half2(h0, h1), ll = __halves2half2(l0, l1);
-              h[i / 2] = *reinterpret_cast<uint32_t *>(&hh);
-              l[i / 2] = *reinterpret_cast<uint32_t *>(&ll);
+              hl[c][i / 2] = *reinterpret_cast<uint32_t *>(&hh);
+              hl[c][8 + i / 2] = *reinterpret_cast<uint32_t *>(&ll);
             }
+            if (e.z32 && live) store_f32x16(e.z32 + (size_t)m * e.F + (size_t)nt * 128 + g0, gv);
+          }
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int g0 = 32 * quarter + 16 * c;
             uint8_t *stg = next_stage_buf();
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
               const uint32_t o = lane * 32 + ((j ^ ((lane >> 2) & 1)) << 4);
-              *reinterpret_cast<uint4 *>(stg + o) = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+              *reinterpret_cast<uint4 *>(stg + o) =
+                  make_uint4(hl[c][4 * j], hl[c][4 * j + 1], hl[c][4 * j + 2], hl[c][4 * j + 3]);
               *reinterpret_cast<uint4 *>(stg + 1024 + o) =
-                  make_uint4(l[4 * j], l[4 * j + 1], l[4 * j + 2], l[4 * j + 3]);
+                  make_uint4(hl[c][8 + 4 * j], hl[c][8 + 4 * j + 1], hl[c][8 + 4 * j + 2], hl[c][8 + 4 * j + 3]);
             }
             fence_proxy_async_smem();
             __syncwarp();
@@ -501,30 +511,38 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               tma_store_2d(&tm_zl, stg + 1024, nt * 128 + g0, row0);
               bulk_commit();
             }
-            if (e.z32 && live) store_f32x16(e.z32 + (size_t)m * e.F + (size_t)nt * 128 + g0, gv);
           }
         } else {  // EPI_PLAIN
+          // two chunks at a time: chunks 0-1 are loaded, staged and stored,
+          // then chunks 2-3 are loaded and TMEM is released
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            const int c0 = 64 * quarter + 16 * c;
-            float v[16];
-            tmem_ld_pair16(trow + c0, v, sc);
-            if (c == 3) release();
+          for (int half = 0; half < 2; ++half) {
+            float v[2][16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] += sb[c0 + i];
-            uint8_t *stg = next_stage_buf();
+            for (int c = 0; c < 2; ++c) {
+              const int c0 = 64 * quarter + 32 * half + 16 * c;
+              tmem_ld_pair16(trow + c0, v[c], sc);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              *reinterpret_cast<float4 *>(stg + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
-                  make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              if (e.reduce_add)
-                tma_reduce_add_2d(&tm_y, stg, nt * BN + c0, row0);
-              else
-                tma_store_2d(&tm_y, stg, nt * BN + c0, row0);
-              bulk_commit();
+              for (int i = 0; i < 16; ++i) v[c][i] += sb[c0 + i];
+            }
+            if (half == 1) release();
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              const int c0 = 64 * quarter + 32 * half + 16 * c;
+              uint8_t *stg = next_stage_buf();
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                *reinterpret_cast<float4 *>(stg + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                    make_float4(v[c][4 * j], v[c][4 * j + 1], v[c][4 * j + 2], v[c][4 * j + 3]);
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                if (e.reduce_add)
+                  tma_reduce_add_2d(&tm_y, stg, nt * BN + c0, row0);
+                else
+                  tma_store_2d(&tm_y, stg, nt * BN + c0, row0);
+                bulk_commit();
+              }
             }
           }
         }
