@@ -1662,7 +1662,12 @@ cudaError_t t0b_launch_dec_head(const float *dec, const float *loc, const float 
 }
 
 // ============================================================== split
+// x -> (hi, lo) f16 planes.  Launched as a programmatic dependent: it lets
+// the next kernel (a small-M GEMM prefetching its weights) start at once,
+// and touches memory only after the previous kernel has completed.
 __global__ void split_f32_kernel(const float *x, __half *h, __half *l, size_t n) {
+  pdl_launch_dependents();
+  pdl_wait();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     __half a, b;
     split_f16(x[i], a, b);
@@ -1672,6 +1677,14 @@ __global__ void split_f32_kernel(const float *x, __half *h, __half *l, size_t n)
 }
 cudaError_t t0b_launch_split_f32(const float *x, __half *xh, __half *xl, size_t n, cudaStream_t st) {
   size_t blocks = std::min<size_t>((n + 255) / 256, 148 * 16);
-  split_f32_kernel<<<(unsigned)std::max<size_t>(blocks, 1), 256, 0, st>>>(x, xh, xl, n);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)std::max<size_t>(blocks, 1));
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, split_f32_kernel, x, xh, xl, n);
 }
