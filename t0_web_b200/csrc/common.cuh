@@ -94,6 +94,14 @@ T0B_DEV void tma_store_2d(const void *tmap, const void *src, int x, int y) {
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
+// 3-D tiled bulk tensor store shared -> global (bulk-group completion); the
+// same rules as tma_store_2d, with z >= 0 too.
+T0B_DEV void tma_store_3d(const void *tmap, const void *src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   (uint64_t)tmap),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
 // 2-D tiled bulk tensor reduction shared -> global: global += the tile
 // (element type from the tensor map; bulk-group completion).  Same
 // coordinate rules as tma_store_2d.

@@ -698,6 +698,23 @@ bool t0b_make_tmap_f32_2d(CUtensorMap *tm, const float *ptr, uint64_t inner, uin
                       swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+// f16 tensor of dims {d0, d1, d2} (innermost first; d1 rows s1 bytes apart,
+// d2 slabs s2 bytes apart), box {b0, b1, b2}, optionally with the 128-byte
+// swizzle: for the attention kernels' TMA stores.
+bool t0b_make_tmap_f16_3d(CUtensorMap *tm, const void *ptr, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+                          uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2, bool swizzle128) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1, s2};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Host entry.  qt: 8 = Q8_0, 4 = Q4_0.  Requires K % 256 == 0, N % 256 == 0
 // (SWIGLU: F % 128 == 0), M >= 1, 16-byte aligned A rows.  `wrows` is the
 // number of rows of W (N, or 2F for SWIGLU); `wshift` the weight prescale

@@ -591,8 +591,16 @@ T0B_DEV uint64_t *attn_bar(__half *base, int PK) {
   return reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(base) + attn_q_off(PK) + (size_t)PK * 256);
 }
 
+// use_tma: bit 0 = q / k / v tiles by TMA loads (tm_qkv); bit 1 (with bit 0)
+// = the output planes by TMA stores (tm_oh / tm_ol: [R][p][E] f16 maps,
+// 64 x 16 x 1 boxes with the 128-byte swizzle), staged in this warp's rows of
+// the q tile, which only this warp reads and only before the k / v barrier.
 __global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a, const __grid_constant__ CUtensorMap tm_qkv,
-                                                               int use_tma) {
+                                                               const __grid_constant__ CUtensorMap tm_oh,
+                                                               const __grid_constant__ CUtensorMap tm_ol,
+                                                               int use_tma_flags) {
+  const bool use_tma = (use_tma_flags & 1) != 0;
+  const bool tma_out = use_tma && (use_tma_flags & 2) != 0;
   pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
   extern __shared__ __align__(128) uint4 smem_u4[];
   const int r = blockIdx.x, h = blockIdx.y;
@@ -864,9 +872,44 @@ __global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a, const
   lb += __shfl_xor_sync(0xffffffffu, lb, 1);
   lb += __shfl_xor_sync(0xffffffffu, lb, 2);
   const float inva = 1.0f / la, invb = 1.0f / lb;
+  if (tma_out) {
+    // this warp's 16 output rows: hi plane in its q-tile rows of dims 0-31,
+    // lo plane in its rows of dims 32-63 (2 KB each, 128-byte swizzle:
+    // 16-byte unit nd of row rr at unit nd ^ (rr & 7)); rows >= p are
+    // clipped by the tensor maps
+    uint8_t *qt = attn_qtile(Kh, PK);
+    uint8_t *sh = qt + (size_t)(qb * 16) * 128, *sl = qt + (size_t)(PK + qb * 16) * 128;
+#pragma unroll
+    for (int nd = 0; nd < 8; ++nd) {
+      uint32_t hw, lw;
+      const uint32_t ua = (uint32_t)g * 128 + (((uint32_t)nd ^ (uint32_t)g) << 4) + 4 * t;
+      split2(o[nd][0] * inva, o[nd][1] * inva, hw, lw);
+      *reinterpret_cast<uint32_t *>(sh + ua) = hw;
+      *reinterpret_cast<uint32_t *>(sl + ua) = lw;
+      split2(o[nd][2] * invb, o[nd][3] * invb, hw, lw);
+      *reinterpret_cast<uint32_t *>(sh + ua + 8 * 128) = hw;
+      *reinterpret_cast<uint32_t *>(sl + ua + 8 * 128) = lw;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(&tm_oh, sh, h * 64, qb * 16, r);
+      tma_store_3d(&tm_ol, sl, h * 64, qb * 16, r);
+      bulk_commit();
+    }
+  }
 #pragma unroll
   for (int nd = 0; nd < 8; ++nd) {
     const int d = nd * 8 + 2 * t;
+    if (tma_out) {  // only the optional f32 copy
+      if (a.o32 && ia < p)
+        *reinterpret_cast<float2 *>(a.o32 + (tok0 + ia) * E + h * 64 + d) =
+            make_float2(o[nd][0] * inva, o[nd][1] * inva);
+      if (a.o32 && ib < p)
+        *reinterpret_cast<float2 *>(a.o32 + (tok0 + ib) * E + h * 64 + d) =
+            make_float2(o[nd][2] * invb, o[nd][3] * invb);
+      continue;
+    }
     if (ia < p) {
       const float x0 = o[nd][0] * inva, x1 = o[nd][1] * inva;
       const size_t oo = (tok0 + ia) * E + h * 64 + d;
@@ -886,6 +929,7 @@ __global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a, const
       if (a.o32) *reinterpret_cast<float2 *>(a.o32 + oo) = make_float2(x0, x1);
     }
   }
+  if (tma_out && lane == 0) bulk_wait_all();  // stores done before the CTA (and its shared memory) ends
 }
 
 // ------------------------------------------------- 128-dim heads (t0-beta)
@@ -1616,9 +1660,16 @@ cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
     // k / v tiles by TMA: a [p][64] f32 box of the [R p][3E] q|k|v tensor
     CUtensorMap tm;
     std::memset(&tm, 0, sizeof(tm));
+    CUtensorMap toh, tol;  // output planes as [R][p][E] f16, 64 x 16 x 1 boxes
+    std::memset(&toh, 0, sizeof(toh));
+    std::memset(&tol, 0, sizeof(tol));
+    const uint64_t rs = (uint64_t)a.E * 2, ss = rs * (uint64_t)a.p;
+    const bool out_ok =
+        t0b_make_tmap_f16_3d(&toh, a.oh, (uint64_t)a.E, (uint64_t)a.p, (uint64_t)a.R, rs, ss, 64, 16, 1, true) &&
+        t0b_make_tmap_f16_3d(&tol, a.ol, (uint64_t)a.E, (uint64_t)a.p, (uint64_t)a.R, rs, ss, 64, 16, 1, true);
     const int use_tma = t0b_make_tmap_f32_2d(&tm, a.qkv, (uint64_t)3 * a.E, (uint64_t)a.R * a.p,
                                              (uint64_t)3 * a.E * sizeof(float), 32, (uint32_t)a.p, true) ? 1 : 0;
-    attn_time_mma_kernel<<<dim3(a.R, a.H), 32 * QB, smem, st>>>(a, tm, use_tma);
+    attn_time_mma_kernel<<<dim3(a.R, a.H), 32 * QB, smem, st>>>(a, tm, toh, tol, use_tma | (use_tma && out_ok ? 2 : 0));
     return cudaGetLastError();
   }
   size_t smem = (size_t)(a.p * (65 + 64 + 64) + 4 * a.p) * sizeof(float);

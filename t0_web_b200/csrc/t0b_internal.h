@@ -65,6 +65,8 @@ struct AttnArgs {
 // rejects the layout (k_gemm_tc.cu).
 bool t0b_make_tmap_f32_2d(CUtensorMap *tm, const float *ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
                           uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+bool t0b_make_tmap_f16_3d(CUtensorMap *tm, const void *ptr, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+                          uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2, bool swizzle128);
 
 // Small-M dequant GEMM (k_gemm_small.cu): thread-block clusters along K,
 // launched as a programmatic dependent of the previous kernel on `st`.
