@@ -112,8 +112,6 @@ T0B_DEV void tma_reduce_add_2d(const void *tmap, const void *src, int x, int y) 
                : "memory");
 }
 T0B_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// Wait until no committed bulk store still reads shared memory.
-T0B_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // Wait until every committed bulk store has completed.
 T0B_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 T0B_DEV void prefetch_tmap(const void *tmap) {
@@ -121,29 +119,6 @@ T0B_DEV void prefetch_tmap(const void *tmap) {
 }
 
 // ---------------------------------------------------------------- tcgen05
-T0B_DEV void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
-               "r"(ncols)
-               : "memory");
-}
-T0B_DEV void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;"); }
-T0B_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-// D[tmem] (+)= A[smem] . B[smem]^T, both K-major, kind::f16 (f16 inputs,
-// f32 accumulate).  Issued by one thread.
-T0B_DEV void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
-          d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrive once on `bar` when all previously issued MMAs of this thread finish.
-T0B_DEV void umma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
 // ------------------------------------------------- CTA pairs (cta_group::2)
 // Two CTAs of a 2-CTA cluster share one MMA: A rows split between the CTAs
 // (each holds its 128 rows), B columns split between them (CTA 0 holds the
@@ -218,35 +193,6 @@ T0B_DEV void umma_commit_pair(uint32_t bar_cl) {
                : "memory");
 }
 
-// 32 lanes x 32 consecutive f32 columns -> 32 registers per thread.
-T0B_DEV void tmem_ld32(uint32_t taddr, float *v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
-      "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// 16 consecutive 32-bit TMEM columns of this thread's lane.
-T0B_DEV void tmem_ld16(uint32_t taddr, float *v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 // Two 16-column loads of this thread's lane with a single wait.
 T0B_DEV void tmem_ld16x2(uint32_t ta, uint32_t tb, float *va, float *vb) {
   uint32_t r[16], q[16];
@@ -265,20 +211,9 @@ T0B_DEV void tmem_ld16x2(uint32_t ta, uint32_t tb, float *va, float *vb) {
   for (int i = 0; i < 16; ++i) va[i] = __uint_as_float(r[i]), vb[i] = __uint_as_float(q[i]);
 }
 
-// Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows of 128 B
-// (64 f16), 8-row atoms of 1024 B stacked at a stride of 1024 B.  The atom
-// base must be 1024-byte aligned.
-T0B_DEV uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
-  d |= (uint64_t)(1024u >> 4) << 32;  // stride byte offset: next 8-row atom
-  d |= (uint64_t)1 << 46;             // descriptor version for tcgen05
-  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
-  return d;
-}
-// Same for a 64-byte swizzle: rows of 64 B (32 f16), 8-row atoms of 512 B
-// stacked at a stride of 512 B.
+// Shared-memory matrix descriptor, K-major, 64-byte swizzle: rows of 64 B
+// (32 f16), 8-row atoms of 512 B stacked at a stride of 512 B.  The atom
+// base must be 512-byte aligned.
 T0B_DEV uint64_t sw64_desc(uint32_t saddr) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
@@ -297,11 +232,6 @@ T0B_DEV uint32_t sw64_offset(uint32_t r, uint32_t k) {
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
   return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
-// Byte offset of element (row r, k) in a K-major SW128 tile of 64-wide rows.
-T0B_DEV uint32_t sw128_offset(uint32_t r, uint32_t k) {
-  return (r >> 3) * 1024u + (r & 7u) * 128u + ((((k >> 3) ^ (r & 7u)) & 7u) << 4) + (k & 7u) * 2u;
-}
-
 // ---------------------------------------------------------------- mma.sync
 T0B_DEV void mma16816(float &d0, float &d1, float &d2, float &d3, uint32_t a0, uint32_t a1, uint32_t a2,
                       uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -384,15 +314,6 @@ T0B_DEV void nib8_to_h2x4(uint32_t w, uint32_t *out) {
     __half2 v = __hsub2(*reinterpret_cast<__half2 *>(&r[i]), k);
     out[i] = *reinterpret_cast<uint32_t *>(&v);
   }
-}
-// Register reconfiguration for warp-specialized kernels (whole warpgroup).
-template <int N>
-T0B_DEV void regs_dealloc() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
-}
-template <int N>
-T0B_DEV void regs_alloc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 // f32 -> (hi, lo) f16 pair with hi + lo == x to about 2^-22 relative.
 T0B_DEV void split_f16(float x, __half &hi, __half &lo) {
