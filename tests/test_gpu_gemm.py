@@ -119,3 +119,46 @@ def test_swiglu_vs_oracle(engine, qtype, M):
     assert np.isfinite(z).all() and np.isfinite(y).all()
     assert _rel(z[rows], zr) <= REL_TIGHT
     assert _rel(y[rows], yr) <= REL_TIGHT
+
+
+@pytest.mark.parametrize("qtype", [Q8_0, Q4_0], ids=["q8_0", "q4_0"])
+@pytest.mark.parametrize("M", [255, 257, 511, 513])
+def test_pair_tile_boundaries(engine, qtype, M):
+    """The tensor-core GEMM runs on CTA pairs that own 256 tokens each (128
+    per CTA): M just below and above one and two pair tiles leaves the second
+    CTA of the last pair partly or wholly past M.  Every row is checked, so
+    rows written by the wrong CTA or left unwritten (NaN-poisoned) fail."""
+    N, K = 512, 512
+    w, x = S.gemm_case(N, K, M, seed=1000 + M)
+    wb = gguf.quantize(w, qtype)
+    bias = (np.random.default_rng(M).standard_normal(N) * 0.02).astype(np.float32)
+    y = _gemm(engine, qtype, wb, N, K, x, bias)
+    ref = O.gemm_q_f64(qtype, wb, N, K, x, bias)
+    assert np.isfinite(y).all()
+    assert _rel(y, ref) <= REL_TIGHT
+
+
+@pytest.mark.parametrize("qtype", [Q8_0, Q4_0], ids=["q8_0", "q4_0"])
+@pytest.mark.parametrize("M", [129, 257])
+def test_pair_swiglu_boundaries(engine, qtype, M):
+    """SwiGLU on CTA pairs (CTA 0 holds the gate rows, CTA 1 the matching up
+    rows) at pair-tile boundaries, every row of z and y checked."""
+    F, K, N2 = 512, 512, 512
+    rng = np.random.default_rng(M + 5)
+    w0 = (rng.standard_normal((2 * F, K), dtype=np.float32) * np.float32(0.02))
+    w2 = (rng.standard_normal((N2, F), dtype=np.float32) * np.float32(0.02))
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    b0, b2 = gguf.quantize(w0, qtype), gguf.quantize(w2, qtype)
+    dev = torch.device("cuda:0")
+    w0d, w2d = torch.from_numpy(b0).to(dev), torch.from_numpy(b2).to(dev)
+    xd = torch.from_numpy(x).to(dev)
+    zd = torch.full((M, F), float("nan"), device=dev)
+    yd = torch.full((M, N2), float("nan"), device=dev)
+    torch.cuda.synchronize()
+    check(lib().t0b_swiglu_q(engine.handle, qtype, ptr(w0d), ptr(w2d), F, K, N2, ptr(xd), M, None, None, ptr(zd),
+                             ptr(yd), None))
+    z, y = zd.cpu().numpy(), yd.cpu().numpy()
+    zr, yr = O.swiglu_q_f64(qtype, b0, F, K, b2, N2, x)
+    assert np.isfinite(z).all() and np.isfinite(y).all()
+    assert _rel(z, zr) <= REL_TIGHT
+    assert _rel(y, yr) <= REL_TIGHT
