@@ -190,6 +190,18 @@ t0b_status t0b_qmatrix_swiglu(t0b_qmatrix *q0, t0b_qmatrix *q2, const float *x_d
 /* Wait for `stream` and report any kernel-side error of q's launches. */
 t0b_status t0b_qmatrix_sync(t0b_qmatrix *q, void *stream);
 
+/* ---- bounded-wait self-test (no reference counterpart; a diagnostic) ----
+ * Every wait of a kernel on an mbarrier (TMA tiles, dequantized tiles,
+ * accumulators) gives up after T0B_WAIT_CYCLES SM cycles (about 2 s), records
+ * a device error code and returns, so a lost arrival becomes T0B_ERR_DEVICE
+ * instead of a hung GPU.  This call exercises that path on the engine's
+ * device: one warp waits with the same bounded wait on a barrier that nothing
+ * arrives on.  Expected result: T0B_ERR_DEVICE after about 2 s, with
+ * *device_code = 1 (the wait's code) and *outcome = 2 (the wait returned and
+ * the kernel finished); the context stays usable.  It starts no TMA, tensor
+ * memory or cluster work. */
+t0b_status t0b_selftest_bounded_wait(t0b_engine *e, int *device_code, int *outcome);
+
 /* ---- no-allocation dequant-GEMM (no reference counterpart) ----
  * The product of t0b_gemm_q, same arguments minus the engine, computed on
  * the calling thread's current device without allocating any device memory:
@@ -205,8 +217,10 @@ t0b_status t0b_qmatrix_sync(t0b_qmatrix *q, void *stream);
  *  - M * K <= T0B_NOALLOC_MAX_X_ELEMENTS, else T0B_ERR_INVALID (nothing runs);
  *    K % 256 == 0 and N % 256 == 0 as for t0b_gemm_q.
  *  - The first call on a device looks up the array's device address
- *    (cudaGetSymbolAddress, with that device current) and caches it; make
- *    that first call before capturing the stream into a graph.
+ *    (cudaGetSymbolAddress, with that device current) and caches it.
+ *  - Every call synchronises `stream` (it reads the kernel error word back
+ *    before returning), so it must not be called while `stream` is being
+ *    captured into a CUDA graph.
  *  - All calls on one device share the array.  Each call clears the two
  *    control words it needs zeroed and overwrites the x copy before reading
  *    it, so no state carries over from one call to the next; but calls that

@@ -23,7 +23,7 @@ EXPORTED = [
     "t0b_qmatrix_create", "t0b_qmatrix_destroy", "t0b_qmatrix_gemm", "t0b_qmatrix_swiglu", "t0b_qmatrix_sync",
     "t0b_gguf_validate",
     "t0b_quantize", "t0b_dequantize", "t0b_row_bytes", "t0b_export_gguf", "t0b_model_profile_enable",
-    "t0b_model_profile_read", "t0b_model_launch_count",
+    "t0b_model_profile_read", "t0b_model_launch_count", "t0b_selftest_bounded_wait",
 ]
 
 
@@ -98,6 +98,7 @@ def lib() -> C.CDLL:
     L.t0b_model_profile_read.argtypes = [vp, C.POINTER(KernelStats), C.c_int, C.POINTER(C.c_int)]
     L.t0b_model_launch_count.argtypes = [vp]
     L.t0b_model_launch_count.restype = C.c_uint64
+    L.t0b_selftest_bounded_wait.argtypes = [vp, C.POINTER(C.c_int), C.POINTER(C.c_int)]
     _lib = L
     return L
 

@@ -591,13 +591,13 @@ bool make_tmap_2d(CUtensorMap *tm, CUtensorMapDataType dt, const void *ptr, uint
   return r == CUDA_SUCCESS;
 }
 
-int sm_count() {
-  static int n_sm = 0;
-  if (!n_sm) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
-    if (n_sm <= 0) n_sm = 148;
+// SM count of device `dev` (callers hold max_pairs' lock or accept a
+// repeated query; nothing is cached here).
+int sm_count(int dev) {
+  int n_sm = 0;
+  if (cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n_sm <= 0) {
+    cudaGetLastError();
+    n_sm = 148;
   }
   return n_sm;
 }
@@ -613,7 +613,7 @@ int max_pairs(const void *kfn, const cudaLaunchConfig_t &cfg) {
   auto it = cache.find({kfn, dev});
   if (it != cache.end()) return it->second;
   cudaLaunchConfig_t c = cfg;
-  c.gridDim = dim3(2 * sm_count());
+  c.gridDim = dim3(2 * sm_count(dev));
   int n = 0;
   if (cudaOccupancyMaxActiveClusters(&n, kfn, &c) != cudaSuccess || n < 1) {
     cudaGetLastError();

@@ -1739,3 +1739,27 @@ cudaError_t t0b_launch_split_f32(const float *x, __half *xh, __half *xl, size_t 
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, split_f32_kernel, x, xh, xl, n);
 }
+
+// ============================================================== bounded-wait self-test
+// One warp initialises an mbarrier with an expected count of one and waits
+// on its first phase with the same bounded wait every pipeline kernel uses
+// (mbar_wait).  Nothing ever arrives, so the wait runs out after
+// T0B_WAIT_CYCLES, records T0B_DEVERR_WAIT_X in the error word and returns
+// false; the kernel then exits normally.  No TMA, tensor memory, cluster or
+// other asynchronous work is started, so nothing is left in flight.
+__global__ void bounded_wait_selftest_kernel(int *err, int *outcome) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  bool got = true;
+  if (threadIdx.x == 0) got = mbar_wait(&bar, 0, err, T0B_DEVERR_WAIT_X, nullptr);
+  got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+  if (threadIdx.x == 0) *outcome = got ? 1 : 2;  // 2: the wait ran out and returned
+}
+cudaError_t t0b_launch_bounded_wait_selftest(int *err, int *outcome, cudaStream_t st) {
+  bounded_wait_selftest_kernel<<<1, 32, 0, st>>>(err, outcome);
+  return cudaGetLastError();
+}

@@ -101,3 +101,6 @@ cudaError_t t0b_launch_dec_gather(const float *x, const float *g, float *xo, int
 cudaError_t t0b_launch_dec_head(const float *dec, const float *loc, const float *scale, float *out, const int *out_row,
                                 int R, int hp, int horizon, int nq, int use_arcsinh, cudaStream_t st);
 cudaError_t t0b_launch_split_f32(const float *x, __half *xh, __half *xl, size_t n, cudaStream_t st);
+// Self-test of the bounded mbarrier wait (k_misc.cu): one warp waits on a
+// barrier nobody arrives on; *outcome = 2 once the wait ran out and returned.
+cudaError_t t0b_launch_bounded_wait_selftest(int *err, int *outcome, cudaStream_t st);

@@ -1539,6 +1539,30 @@ extern "C" t0b_status t0b_qmatrix_sync(t0b_qmatrix *q, void *stream) {
   return T0B_OK;
 }
 
+// ================================================ bounded-wait self-test
+extern "C" t0b_status t0b_selftest_bounded_wait(t0b_engine *e, int *device_code, int *outcome) {
+  if (!e || !device_code || !outcome) return fail(T0B_ERR_INVALID, "t0b_selftest_bounded_wait: NULL argument");
+  CUDA_TRY(cudaSetDevice(e->device));
+  *device_code = 0;
+  *outcome = 0;
+  int *d = nullptr;  // [0] error word, [1] outcome
+  CUDA_TRY(cudaMalloc(&d, 2 * sizeof(int)));
+  std::unique_ptr<int, decltype(&cudaFree)> guard(d, &cudaFree);
+  cudaStream_t st = nullptr;
+  CUDA_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  std::unique_ptr<CUstream_st, decltype(&cudaStreamDestroy)> sguard(st, &cudaStreamDestroy);
+  CUDA_TRY(cudaMemsetAsync(d, 0, 2 * sizeof(int), st));
+  CUDA_TRY(t0b_launch_bounded_wait_selftest(d, d + 1, st));
+  int h[2] = {0, 0};
+  CUDA_TRY(cudaMemcpyAsync(h, d, sizeof(h), cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  *device_code = h[0];
+  *outcome = h[1];
+  if (h[0])
+    return fail(T0B_ERR_DEVICE, "t0b_selftest_bounded_wait: a kernel reported device error code " + std::to_string(h[0]));
+  return T0B_OK;
+}
+
 // ================================================ no-allocation standalone GEMM
 // t0b_gemm_q_noalloc works out of one fixed array that is part of this
 // library's device code, so a call allocates nothing.  Layout:
@@ -1602,16 +1626,6 @@ extern "C" t0b_status t0b_gemm_q_noalloc(int ggml_type, const void *w_dev, int N
   __half *xh = reinterpret_cast<__half *>(base + 256);
   __half *xl = xh + T0B_NOALLOC_MAX_X_ELEMENTS;
   cudaStream_t st = (cudaStream_t)stream;
-  CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
-  CUDA_TRY(t0b_launch_split_f32(x_dev, xh, xl, n_x, st));
-  // weight prescale exponent from the largest block scale (clears `red` first)
-  CUDA_TRY(t0b_launch_absmax_scale((const uint8_t *)w_dev, (size_t)N * K / 32, qt == 8 ? 34 : 18, red, st));
-  unsigned int bits = 0;
-  CUDA_TRY(cudaMemcpyAsync(&bits, red, sizeof(bits), cudaMemcpyDeviceToHost, st));
-  CUDA_TRY(cudaStreamSynchronize(st));
-  float maxd;
-  std::memcpy(&maxd, &bits, 4);
-  const int sh = t0b_weight_shift(maxd, qt);
   Epi ep{};
   ep.kind = EPI_PLAIN;
   ep.M = M;
@@ -1619,13 +1633,27 @@ extern "C" t0b_status t0b_gemm_q_noalloc(int ggml_type, const void *w_dev, int N
   ep.bias = bias_dev;
   ep.y = y_dev;
   ep.ldy = N;
-  if (engine_use_tc(qt, M, K, ep))
+  const bool tc = engine_use_tc(qt, M, K, ep);
+  CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
+  CUDA_TRY(t0b_launch_split_f32(x_dev, xh, xl, n_x, st));
+  if (tc) {
+    // weight prescale exponent from the largest block scale (clears `red`
+    // first); only the tensor-core kernel uses it
+    CUDA_TRY(t0b_launch_absmax_scale((const uint8_t *)w_dev, (size_t)N * K / 32, qt == 8 ? 34 : 18, red, st));
+    unsigned int bits = 0;
+    CUDA_TRY(cudaMemcpyAsync(&bits, red, sizeof(bits), cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    float maxd;
+    std::memcpy(&maxd, &bits, 4);
+    const int sh = t0b_weight_shift(maxd, qt);
     CUDA_TRY(t0b_launch_gemm_tc(qt, xh, xl, M, K, (const uint8_t *)w_dev, N, sh, ep, err, st));
-  else
+  } else {
     CUDA_TRY(t0b_launch_gemm_small(qt, xh, xl, M, K, (const uint8_t *)w_dev, ep, err, st));
-  CUDA_TRY(cudaStreamSynchronize(st));
+  }
+  // the error word is read on the call's own stream (no legacy-stream copy)
   int herr = 0;
-  CUDA_TRY(cudaMemcpy(&herr, err, sizeof(int), cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
   if (herr) return fail(T0B_ERR_DEVICE, "t0b_gemm_q_noalloc: a kernel reported device error code " + std::to_string(herr));
   return T0B_OK;
 }

@@ -7,6 +7,17 @@ quant_blocks.npz   Q8_0 / Q4_0 bytes (and their dequantization) written by
                    bytes).  Inputs: the reference's own test signal
                    sin(0.37 i) * 3 (gguf.rs:410-412), the quant.rs:166-169
                    ramp, seeded normals at three scales and edge blocks.
+reference_contexts.npz
+                   The input contexts of t0-web's own end-to-end fixtures
+                   (fixtures/manifest.json, fixtures/manifest_long.json, made
+                   by tools/make_fixtures.py:124-176): case0_univariate_sine,
+                   case1_trivariate_freqs, case2_masked_gap (NaN steps
+                   [200, 220)) and case_long_rollout (ctx 4096, horizon
+                   1200), with their variate counts and horizons.  Only the
+                   contexts are taken: the fixtures' quantiles come from the
+                   trained checkpoint, which random-init weights cannot
+                   reproduce.  Needs a t0-web checkout:
+                   --reference <path to the t0-web repository>.
 tiny_forecast.npz  End-to-end quantiles of the CPU oracle for the TINY
                    random-init model (seed 0), Q8_0 and Q4_0: one sine
                    context (ctx 77, horizon 30) and three multivariate series
@@ -68,9 +79,30 @@ def make_tiny_forecast():
     np.savez_compressed(os.path.join(HERE, "tiny_forecast.npz"), **out)
 
 
+def make_reference_contexts(ref_root: str):
+    import json
+    fx = os.path.join(ref_root, "fixtures")
+    out = {}
+    names = []
+    for man in ("manifest.json", "manifest_long.json"):
+        m = json.load(open(os.path.join(fx, man)))
+        for c in m["cases"]:
+            ctx = np.fromfile(os.path.join(fx, c["context_file"]), dtype="<f4")
+            v, t = int(c["v"]), int(c["context_len"])
+            assert ctx.size == v * t, (c["name"], ctx.size, v, t)
+            out[c["name"] + "_ctx"] = ctx.reshape(v, t).astype(np.float32)
+            out[c["name"] + "_horizon"] = np.int64(c["horizon"])
+            names.append(c["name"])
+    out["names"] = np.array(names)
+    np.savez_compressed(os.path.join(HERE, "reference_contexts.npz"), **out)
+
+
 if __name__ == "__main__":
-    make_quant_blocks()
-    make_tiny_forecast()
+    if "--reference" in sys.argv:
+        make_reference_contexts(sys.argv[sys.argv.index("--reference") + 1])
+    else:
+        make_quant_blocks()
+        make_tiny_forecast()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

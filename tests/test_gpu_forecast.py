@@ -191,3 +191,58 @@ def test_tiny_model_matches_golden_fixture(engine, quant):
         assert max_abs(got, g[quant + "_multi"]) <= TOL
     finally:
         m.close()
+
+
+@pytest.mark.parametrize("quant", ["q8_0", "q4_0"])
+def test_config4_full_batch_sampled(engine, gpu_model, oracle_model, quant):
+    """The 256-trivariate-series configuration at its full timed size (ctx
+    2048, horizon 96, 51,456 tokens per GEMM, one pass): all 256 series are
+    forecast together on the GPU and 8 series spread over the batch are
+    checked against the oracle."""
+    ctx, nv = S.multiseries(256, 2048, seed=0, n_variates=3)
+    got = t0_fast.forecast_multiseries(engine, gpu_model(quant), ctx, nv, 2048, 96)
+    assert got.shape == (768, 96, 5)
+    assert np.isfinite(got).all()
+    series = [0, 37, 73, 110, 146, 183, 219, 255]
+    rows = np.concatenate([np.arange(3 * s, 3 * s + 3) for s in series])
+    ref = oracle_model(quant).forecast_multiseries(ctx[rows], nv[series], 96, threads=8)
+    assert max_abs(got[rows], ref) <= TOL
+
+
+def _reference_contexts():
+    import os
+    return np.load(os.path.join(os.path.dirname(__file__), "golden", "reference_contexts.npz"))
+
+
+@pytest.mark.parametrize("quant", ["q8_0", "q4_0"])
+@pytest.mark.parametrize("case", ["case0_univariate_sine", "case1_trivariate_freqs", "case2_masked_gap"])
+def test_reference_fixture_contexts(engine, gpu_model, oracle_model, quant, case):
+    """t0-web's own end-to-end fixture inputs (fixtures/manifest.json, made by
+    tools/make_fixtures.py:124-146; committed as tests/golden/
+    reference_contexts.npz): a univariate sine, three variates of different
+    frequencies forecast jointly, and a sine with NaN steps [200, 220).  The
+    fixtures' quantiles come from the trained checkpoint, which is absent, so
+    the GPU is held to the oracle on the same random-init GGUF."""
+    g = _reference_contexts()
+    ctx = g[case + "_ctx"]
+    h = int(g[case + "_horizon"])
+    got = t0_fast.forecast(engine, gpu_model(quant), ctx, ctx.shape[0], ctx.shape[1], h)
+    ref = oracle_model(quant).forecast(ctx, h)
+    assert got.shape == (ctx.shape[0], h, 5)
+    assert np.isfinite(got).all()
+    assert max_abs(got, ref) <= TOL
+
+
+def test_reference_fixture_long_rollout(engine, gpu_model, oracle_model):
+    """fixtures/manifest_long.json's case_long_rollout (tools/
+    make_fixtures.py:150-176): ctx 4096, horizon 1200, so one 1024-step block
+    and one autoregressive block over the trained levels."""
+    g = _reference_contexts()
+    ctx = g["case_long_rollout_ctx"]
+    h = int(g["case_long_rollout_horizon"])
+    levels = [0.1, 0.25, 0.5, 0.75, 0.9]
+    got = t0_fast.forecast_rollout(engine, gpu_model("q8_0"), ctx[0], ctx.shape[1], h, levels)
+    ref = oracle_model("q8_0").forecast_rollout(ctx[0], h, levels)
+    assert got.shape == (h, 5)
+    assert np.isfinite(got).all()
+    assert max_abs(got, ref) <= TOL

@@ -162,3 +162,61 @@ def test_pair_swiglu_boundaries(engine, qtype, M):
     assert np.isfinite(z).all() and np.isfinite(y).all()
     assert _rel(z, zr) <= REL_TIGHT
     assert _rel(y, yr) <= REL_TIGHT
+
+
+def _sampled_rows(M, n=96, seed=0):
+    """First and last rows, both sides of every 256-token pair tile near the
+    ends, and a seeded spread in between."""
+    fixed = [0, 1, 127, 128, 255, 256, M - 257, M - 256, M - 129, M - 128, M - 2, M - 1]
+    rest = np.random.default_rng(seed).choice(M, n - len(fixed), replace=False)
+    return np.unique(np.clip(np.concatenate([fixed, rest]), 0, M - 1))
+
+
+@pytest.mark.parametrize("qtype", [Q8_0, Q4_0], ids=["q8_0", "q4_0"])
+def test_gemm_config2_full_size(engine, qtype):
+    """The standalone Q8_0 GEMM configuration at its largest timed size,
+    N = 3072, K = 1024, M = 65,536 (805 MB of output): ~96 sampled rows
+    against the f64 oracle, every output checked finite."""
+    N, K, M = 3072, 1024, 65536
+    w, x = S.gemm_case(N, K, M, seed=65536)
+    wb = gguf.quantize(w, qtype)
+    dev = torch.device("cuda:0")
+    wd = torch.from_numpy(wb.copy()).to(dev)
+    xd = torch.from_numpy(x).to(dev)
+    yd = torch.full((M, N), float("nan"), device=dev)
+    torch.cuda.synchronize()
+    check(lib().t0b_gemm_q(engine.handle, qtype, ptr(wd), N, K, ptr(xd), M, None, ptr(yd), None))
+    rows = _sampled_rows(M)
+    assert bool(torch.isfinite(yd).all())
+    y = yd[torch.from_numpy(rows).to(dev)].cpu().numpy()
+    ref = O.gemm_q_f64(qtype, wb, N, K, x[rows])
+    assert _rel(y, ref) <= REL_TIGHT
+
+
+@pytest.mark.parametrize("qtype,M", [(Q4_0, 1024), (Q8_0, 1024), (Q4_0, 65536)],
+                         ids=["q4_0-1024", "q8_0-1024", "q4_0-65536"])
+def test_swiglu_config3_timed_sizes(engine, qtype, M):
+    """The standalone SwiGLU configuration (F = 4096, K = 1024, N2 = 1024) at
+    the timed token counts 1,024 and 65,536: z and y of ~96 sampled rows
+    against the f64 oracle, every output checked finite."""
+    F, K, N2 = 4096, 1024, 1024
+    rng = np.random.default_rng(M + 11)
+    w0 = (rng.standard_normal((2 * F, K), dtype=np.float32) * np.float32(0.02))
+    w2 = (rng.standard_normal((N2, F), dtype=np.float32) * np.float32(0.02))
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    b0, b2 = gguf.quantize(w0, qtype), gguf.quantize(w2, qtype)
+    dev = torch.device("cuda:0")
+    w0d, w2d = torch.from_numpy(b0).to(dev), torch.from_numpy(b2).to(dev)
+    xd = torch.from_numpy(x).to(dev)
+    zd = torch.full((M, F), float("nan"), device=dev)
+    yd = torch.full((M, N2), float("nan"), device=dev)
+    torch.cuda.synchronize()
+    check(lib().t0b_swiglu_q(engine.handle, qtype, ptr(w0d), ptr(w2d), F, K, N2, ptr(xd), M, None, None, ptr(zd),
+                             ptr(yd), None))
+    assert bool(torch.isfinite(zd).all()) and bool(torch.isfinite(yd).all())
+    rows = _sampled_rows(M)
+    idx = torch.from_numpy(rows).to(dev)
+    z, y = zd[idx].cpu().numpy(), yd[idx].cpu().numpy()
+    zr, yr = O.swiglu_q_f64(qtype, b0, F, K, b2, N2, x[rows])
+    assert _rel(z, zr) <= REL_TIGHT
+    assert _rel(y, yr) <= REL_TIGHT
