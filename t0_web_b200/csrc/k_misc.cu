@@ -933,12 +933,18 @@ __global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a, const
 }
 
 // ------------------------------------------------- 128-dim heads (t0-beta)
-// Time attention for heads of HD = 128 dims, p <= 192, with the arithmetic
+// Time attention for heads of HD = 128 dims, p <= 256, with the arithmetic
 // of attn_time_mma_kernel (split-f16 QK^T and PV on mma.sync, online
 // softmax).  At most 8 warps, each taking query blocks warp, warp + 8, ...;
 // k / v rows are staged in 64-dim halves after a sum-of-squares pass, so no
-// thread holds a whole row.
-constexpr int kAttnWideMaxP = 192;  // 4 f16 planes of [192][136]: 209 KB of shared memory
+// thread holds a whole row.  VSPLIT = 1 stages all of V (p <= 192: 4 f16
+// planes of [192][136], 209 KB of shared memory); VSPLIT = 2 stages K whole
+// and V one 64-dim half at a time (p <= 256: 139 + 74 KB), running the
+// queries once per half: the scores and softmax of the second run repeat
+// the first bit for bit (same operations in the same order), and each run
+// writes its half of the output dims.
+constexpr int kAttnWideMaxP = 256;
+constexpr int kAttnWideOnePassMaxP = 192;
 
 // RoPE on dims 16cg .. 16cg + 15 from a compact table row [2 HD]
 // (cos[HD/2], sin[HD/2] per pair, scale[HD/2], 1/scale[HD/2] per dim mod
@@ -966,12 +972,16 @@ T0B_DEV void rope_pair_hd(float &x0, float &x1, const float *tab, int i, bool ks
   x1 = a1 * c * s1 + a0 * sn * s1;
 }
 
-template <int HD>
+template <int HD, int VSPLIT>
 __global__ void __launch_bounds__(256, 1) attn_time_wide_kernel(AttnArgs a) {
   pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
   constexpr int PITCH = HD + 8;  // halves: conflict-free ldmatrix rows
+  constexpr int VD = HD / VSPLIT;  // V dims staged (and output dims written) per run
+  constexpr int VPITCH = VD + 8;
   constexpr int NKC = HD / 16;   // 16-dim chunks of a head
-  constexpr int NDT = HD / 8;    // n8 tiles of the output
+  constexpr int NVC = VD / 16;   // 16-dim chunks of V per run
+  constexpr int NDT = VD / 8;    // n8 tiles of the output per run
+  static_assert(VD % 64 == 0, "V is staged in 64-dim halves");
   extern __shared__ uint4 smem_u4[];
   const int r = blockIdx.x, h = blockIdx.y;
   const int p = a.p, E = a.E;
@@ -980,14 +990,18 @@ __global__ void __launch_bounds__(256, 1) attn_time_wide_kernel(AttnArgs a) {
   __half *Kh = reinterpret_cast<__half *>(smem_u4);
   __half *Kl = Kh + PK * PITCH;
   __half *Vh = Kl + PK * PITCH;
-  __half *Vl = Vh + PK * PITCH;
+  __half *Vl = Vh + PK * VPITCH;
   const size_t tok0 = (size_t)r * p;
   const bool rope = a.use_rope != 0;
   const int lo = a.row_first_valid[r];
   const float qk_scale = 1.0f / sqrtf((float)HD);
 
-  // ---- staging: rows [0, PK) are v rows, [PK, 2 PK) k rows (rows >= p zero)
-  for (int row = threadIdx.x; row < 2 * PK; row += blockDim.x) {
+#pragma unroll 1
+  for (int vp = 0; vp < VSPLIT; ++vp) {
+  // ---- staging: rows [0, PK) are v rows (dims [vp VD, vp VD + VD)), [PK, 2 PK)
+  // k rows (all dims, first run only); rows >= p are zero
+  if (vp > 0) __syncthreads();  // the previous run has finished reading V
+  for (int row = threadIdx.x; row < (vp == 0 ? 2 * PK : PK); row += blockDim.x) {
     const bool is_k = row >= PK;
     const int j = is_k ? row - PK : row;
     const float *src = a.qkv + (tok0 + (j < p ? j : 0)) * 3 * E + (is_k ? E : 2 * E) + h * HD;
@@ -1004,9 +1018,11 @@ __global__ void __launch_bounds__(256, 1) attn_time_wide_kernel(AttnArgs a) {
       }
       rdn = 1.0f / sqrtf(ss / (float)HD + 1e-8f);
     }
-    __half *dh = (is_k ? Kh : Vh) + j * PITCH, *dl = (is_k ? Kl : Vl) + j * PITCH;
+    __half *dh = is_k ? Kh + j * PITCH : Vh + j * VPITCH, *dl = is_k ? Kl + j * PITCH : Vl + j * VPITCH;
+    const int hf0 = is_k ? 0 : vp * (VD / 64), nhf = is_k ? HD / 64 : VD / 64;
 #pragma unroll 1
-    for (int hf = 0; hf < HD / 64; ++hf) {
+    for (int hx = 0; hx < nhf; ++hx) {
+      const int hf = hf0 + hx;  // 64-dim half of the head read here
       float xv[64];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
@@ -1028,8 +1044,8 @@ __global__ void __launch_bounds__(256, 1) attn_time_wide_kernel(AttnArgs a) {
         uint32_t hw[4], lw[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) split2(xv[8 * u + 2 * e], xv[8 * u + 2 * e + 1], hw[e], lw[e]);
-        *reinterpret_cast<uint4 *>(dh + 64 * hf + 8 * u) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4 *>(dl + 64 * hf + 8 * u) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        *reinterpret_cast<uint4 *>(dh + 64 * hx + 8 * u) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4 *>(dl + 64 * hx + 8 * u) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
     }
   }
@@ -1161,9 +1177,9 @@ __global__ void __launch_bounds__(256, 1) attn_time_wide_kernel(AttnArgs a) {
       split2(sc[1][0], sc[1][1], ph[2], pl[2]);
       split2(sc[1][2], sc[1][3], ph[3], pl[3]);
       // transposed ldmatrix rows: matrix m -> keys (m % 2) * 8 + (lane % 8), dims (m / 2) * 8
-      const int voff = (kb * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * PITCH + ((lane >> 4) << 3);
+      const int voff = (kb * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * VPITCH + ((lane >> 4) << 3);
   #pragma unroll
-      for (int n2 = 0; n2 < NKC; ++n2) {  // dims 16 n2 .. 16 n2 + 15 = n8 blocks 2 n2, 2 n2 + 1
+      for (int n2 = 0; n2 < NVC; ++n2) {  // dims 16 n2 .. 16 n2 + 15 = n8 blocks 2 n2, 2 n2 + 1
         uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
         ldsm_x4_trans(Vh + voff + 16 * n2, h0, h1, h2, h3);
         ldsm_x4_trans(Vl + voff + 16 * n2, l0, l1, l2, l3);
@@ -1183,7 +1199,7 @@ __global__ void __launch_bounds__(256, 1) attn_time_wide_kernel(AttnArgs a) {
     const float inva = 1.0f / la, invb = 1.0f / lb;
 #pragma unroll
     for (int nd = 0; nd < NDT; ++nd) {
-      const int d = nd * 8 + 2 * t;
+      const int d = vp * VD + nd * 8 + 2 * t;
       if (ia < p) {
         const float x0 = o[nd][0] * inva, x1 = o[nd][1] * inva;
         const size_t oo = (tok0 + ia) * E + h * HD + d;
@@ -1204,6 +1220,7 @@ __global__ void __launch_bounds__(256, 1) attn_time_wide_kernel(AttnArgs a) {
       }
     }
   }
+  }  // vp
 }
 
 // Group attention for one (series, patch): every head (one warp each) over
@@ -1645,10 +1662,18 @@ cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
   if (a.E / a.H == 128) {
     if (a.p > kAttnWideMaxP) return cudaErrorInvalidValue;
     const int QB = (a.p + 15) / 16, PK = 16 * QB;
-    const size_t smem = (size_t)(4 * PK * (128 + 8)) * sizeof(__half);
-    cudaError_t e = t0b_smem_limit((const void *)attn_time_wide_kernel<128>, smem);
-    if (e != cudaSuccess) return e;
-    attn_time_wide_kernel<128><<<dim3(a.R, a.H), 32 * (QB < 8 ? QB : 8), smem, st>>>(a);
+    const unsigned nthr = 32 * (QB < 8 ? QB : 8);
+    if (a.p <= kAttnWideOnePassMaxP) {
+      const size_t smem = (size_t)(4 * PK * (128 + 8)) * sizeof(__half);
+      cudaError_t e = t0b_smem_limit((const void *)attn_time_wide_kernel<128, 1>, smem);
+      if (e != cudaSuccess) return e;
+      attn_time_wide_kernel<128, 1><<<dim3(a.R, a.H), nthr, smem, st>>>(a);
+    } else {
+      const size_t smem = (size_t)(2 * PK * (128 + 8) + 2 * PK * (64 + 8)) * sizeof(__half);
+      cudaError_t e = t0b_smem_limit((const void *)attn_time_wide_kernel<128, 2>, smem);
+      if (e != cudaSuccess) return e;
+      attn_time_wide_kernel<128, 2><<<dim3(a.R, a.H), nthr, smem, st>>>(a);
+    }
     return cudaGetLastError();
   }
   if (a.E / a.H != 64) return cudaErrorInvalidValue;

@@ -899,8 +899,8 @@ t0b_status run_series(t0b_model *m, const float *ctx_dev, const std::vector<RowS
                       size_t max_rows_hint) {
   const int hpad = (horizon + 31) / 32 * 32;
   const int p = (ctx_w + hpad) / 32, hp = hpad / 32;
-  if (m->E / m->H == 128 && p > 192)
-    return fail(T0B_ERR_UNSUPPORTED, "t0b: 128-dim heads run at most 192 patches per row (context + horizon)");
+  if (m->E / m->H == 128 && p > 256)
+    return fail(T0B_ERR_UNSUPPORTED, "t0b: 128-dim heads run at most 256 patches per row (context + horizon)");
   size_t max_rows = std::max<size_t>(1, m->max_tokens / (size_t)p);
   if (max_rows_hint) max_rows = std::min(max_rows, max_rows_hint);
   size_t s = 0, row = 0;

@@ -2,9 +2,10 @@
 128), 21 quantile levels, `std_clamp` scaler (eps 0.01), on a 3-layer model
 of t0-beta's widths (TIME, TIME, GROUP) with random-init weights.
 
-Covers the 128-dim attention kernels (`attn_time_wide_kernel`, the group
-kernels instantiated for 128 dims), both GEMM paths at K = 1024 and the
-decoder with 21 quantiles.
+Covers the 128-dim attention kernels (`attn_time_wide_kernel`, one run up
+to 192 patches and split-V runs up to 256, the group kernels instantiated
+for 128 dims), both GEMM paths at K = 1024 and the decoder with 21
+quantiles, plus one forecast of the full 24-layer depth at small M.
 
 Tolerance: with random-init weights and 21 levels the cumulative softplus
 head drives the upper quantiles to ~1e6-1e7 (sinh of a running sum near
@@ -66,7 +67,49 @@ def test_beta_long_context(engine, beta):
     assert err(got, ref) <= TOL
 
 
-def test_beta_beyond_192_patches_is_unsupported(engine, beta):
+def test_beta_250_patches_v_split(engine, beta):
+    """p = 250 patches per row (ctx 7904, horizon 96): beyond 192 patches the
+    128-dim time attention stages K whole and V one 64-dim half at a time
+    and runs the queries once per half (t0-fast's windows reach 256
+    patches: shaders/attention.wgsl:21 MAX_SEQ = 256)."""
+    gm, om = beta
+    ctx, nv = S.multiseries(1, 7904, seed=4, n_variates=2)
+    got = t0_fast.forecast_multiseries(engine, gm, ctx, nv, 7904, 96)
+    ref = om.forecast_multiseries(ctx, nv, 96, threads=8)
+    assert np.isfinite(got).all()
+    assert err(got, ref) <= TOL
+
+
+def test_beta_193_and_256_patches(engine, beta):
+    """The two ends of the split-V range: p = 193 (ctx 6080 + horizon 96,
+    16-row key blocks padded to 208) and p = 256 (ctx 8096 + horizon 96)."""
+    gm, om = beta
+    for t_ctx in (6080, 8096):
+        ctx = S.sine_context(t_ctx, seed=t_ctx)
+        got = t0_fast.forecast(engine, gm, ctx, 1, t_ctx, 96)
+        ref = om.forecast(ctx, 96)
+        assert np.isfinite(got).all()
+        assert err(got, ref) <= TOL, t_ctx
+
+
+def test_beta_beyond_256_patches_is_unsupported(engine, beta):
     gm, _ = beta
     with pytest.raises(T0bError):
-        t0_fast.forecast(engine, gm, S.sine_context(6200), 1, 6200, 96)
+        t0_fast.forecast(engine, gm, S.sine_context(8192), 1, 8192, 96)
+
+
+def test_beta_full_24_layers_small_m(engine):
+    """The full t0-beta depth (24 layers: TIME, TIME, GROUP x 8, embed_dim
+    1024) at small M: one sine context (ctx 512, horizon 96, 19 tokens per
+    GEMM), Q8_0, against the oracle on the same GGUF."""
+    g = gguf.export_gguf(S.random_weights(S.BETA, seed=2), S.BETA, "q8_0")
+    gm = t0_fast.load_model_from_gguf(engine, g)
+    try:
+        ctx = S.sine_context(512, seed=0)
+        got = t0_fast.forecast(engine, gm, ctx, 1, 512, 96)
+        ref = O.OracleModel(g).forecast(ctx, 96)
+        assert got.shape == (1, 96, 21)
+        assert np.isfinite(got).all()
+        assert err(got, ref) <= TOL
+    finally:
+        gm.close()
