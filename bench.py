@@ -508,7 +508,7 @@ def run_single(args, engine=None, model=None, emit=True):
             out.append((time.perf_counter() - t0) * 1e3)
         return out
 
-    nsteps = max(args.steps, 20)
+    nsteps = max(args.steps, 400)  # about 0.3 s, so the 200 ms clock sampler sees it
     sampler = ClockSampler([gpu_uuid(0)], [0]).start()
     times = timed(nsteps)                 # default: passes replayed from CUDA graphs
     clocks = sampler.stop()

@@ -86,6 +86,16 @@ T0B_DEV void tma_load_2d(void *dst, const void *tmap, uint64_t *bar, int x, int 
       "l"((uint64_t)tmap), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
+// 3-D tiled bulk tensor load global -> shared (same rules as tma_load_2d;
+// box rows outside the tensor are filled with zeros and still counted in the
+// completed bytes).
+T0B_DEV void tma_load_3d(void *dst, const void *tmap, uint64_t *bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"((uint64_t)tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 // 2-D tiled bulk tensor store shared -> global (bulk-group completion).
 // Rows or columns outside the tensor are not written.  x * element size
 // must be a multiple of 16 bytes and x, y >= 0 (callers guarantee both).

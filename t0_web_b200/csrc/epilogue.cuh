@@ -10,7 +10,7 @@
 
 #include "common.cuh"
 
-enum : int { EPI_PLAIN = 0, EPI_RESID = 2, EPI_SWIGLU = 3 };
+enum : int { EPI_PLAIN = 0, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_QKV = 4 };
 
 struct Epi {
   int kind;
@@ -38,7 +38,56 @@ struct Epi {
   int F;
   __half *zh, *zl;
   float *z32;
+  // EPI_QKV (tensor-core kernel, head_dim 64, TIME layers): the wQKV output
+  // y (q | k | v, E columns each) leaves as f16 (hi, lo) planes in zh / zl
+  // [M][F = 3E] with q and k already multiplied by their QK-norm gains
+  // (qn / kn) and rotated by the xpos RoPE of the token's patch position
+  // (m mod p, transposed compact table rope_t [128][p]); v is only split.  The QK-norm
+  // itself, 1/sqrt(mean(y^2) + 1e-8) of each (token, head) of q and k, is a
+  // per-row scale of the attention scores: the sums of squares of y go to
+  // ssq_qk[m * 2H + h] (q) and ssq_qk[m * 2H + H + h] (k).  RoPE is linear,
+  // so rope(g * y * s) == s * rope(g * y) (ops.rs:132-142, 175-177).
+  const float *qn, *kn, *rope_t;
+  float *ssq_qk;
+  int p, E, H;
 };
+
+// RoPE on 16 consecutive dims 16cg..16cg+15 (8 pairs) of a 64-dim head with
+// 16-byte loads from the compact table row `tab` [128]: cos[32], sin[32] per
+// rotated pair, scale[32] (q side), 1/scale[32] (k side) per dim mod 32
+// (ops.rs:132-142: x0' = (x0 c - x1 s) scale, x1' = (x1 c + x0 s) scale).
+T0B_DEV void rope16(float *x, const float *tab, int cg, bool kside) {
+  const float4 *t4 = reinterpret_cast<const float4 *>(tab);
+  const float4 c0 = t4[2 * cg], c1 = t4[2 * cg + 1], n0 = t4[8 + 2 * cg], n1 = t4[8 + 2 * cg + 1];
+  const float4 *sp = t4 + (kside ? 24 : 16) + ((16 * cg) & 31) / 4;
+  const float4 s0 = sp[0], s1 = sp[1], s2 = sp[2], s3 = sp[3];
+  const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  const float sn[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+  const float sv[16] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w,
+                        s2.x, s2.y, s2.z, s2.w, s3.x, s3.y, s3.z, s3.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float a0 = x[2 * i], a1 = x[2 * i + 1];
+    x[2 * i] = a0 * cs[i] * sv[2 * i] + (-a1) * sn[i] * sv[2 * i];
+    x[2 * i + 1] = a1 * cs[i] * sv[2 * i + 1] + a0 * sn[i] * sv[2 * i + 1];
+  }
+}
+
+// The same rotation with the table transposed, rope_t [128][p] (entry j of
+// position pos at j * p + pos): the lanes of a warp hold consecutive tokens,
+// so each entry is one coalesced load across the warp.
+T0B_DEV void rope16_t(float *x, const float *tabt, int p, int pos, int cg, bool kside) {
+  const float *ct = tabt + (size_t)(8 * cg) * p + pos, *st = ct + (size_t)32 * p;
+  const float *sv = tabt + (size_t)((kside ? 96 : 64) + ((16 * cg) & 31)) * p + pos;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float c = ct[(size_t)i * p], sn = st[(size_t)i * p];
+    const float s0 = sv[(size_t)(2 * i) * p], s1 = sv[(size_t)(2 * i + 1) * p];
+    const float a0 = x[2 * i], a1 = x[2 * i + 1];
+    x[2 * i] = a0 * c * s0 + (-a1) * sn * s0;
+    x[2 * i + 1] = a1 * c * s1 + a0 * sn * s1;
+  }
+}
 
 T0B_DEV float epi_row_denom(const Epi &e, int m) {
   if (!e.ssq_in) return 1.0f;

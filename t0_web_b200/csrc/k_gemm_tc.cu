@@ -212,7 +212,7 @@ template <int QT>
 struct PCfg {
   static constexpr uint32_t RAW_SLOT = (uint32_t)TQ<QT>::rawb * 128;
   static constexpr uint32_t OFF_EPI = P_OFF_RAW + PRS * RAW_SLOT;
-  static constexpr uint32_t OFF_STG = (OFF_EPI + BN * 4 + 1023u) & ~1023u;
+  static constexpr uint32_t OFF_STG = (OFF_EPI + 2 * BN * 4 + 1023u) & ~1023u;  // bias [BN] + QKV gains [BN]
   static constexpr uint32_t OFF_BAR = OFF_STG + STG_N * EPI_WARPS * STG_BYTES;
   static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;
   static_assert(SMEM <= 232448, "shared memory over the 227 KB per-block limit");
@@ -231,7 +231,7 @@ T0B_DEV void bulk_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
-template <int QT>
+template <int QT, int EK>  // EK: the epilogue kind (EPI_PLAIN, EPI_SWIGLU or EPI_QKV)
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_q_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
                           const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_y,
@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int M = prm.M, K = prm.K;
   const int S = K / BK;
-  const bool swiglu = prm.swiglu_F > 0;
+  constexpr bool swiglu = EK == EPI_SWIGLU;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
@@ -437,6 +437,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int c = et;
         const int f = swiglu ? (c < 128 ? nt * 128 + c : e.F + nt * 128 + (c - 128)) : nt * BN + c;
         sb[c] = e.bias ? e.bias[f] : 0.0f;
+        if constexpr (EK == EPI_QKV) {  // QK-norm gains of the tile's columns (1 for v)
+          const int seg = f / e.E;
+          sb[BN + c] = seg == 0 ? e.qn[c & 63] : (seg == 1 ? e.kn[c & 63] : 1.0f);
+        }
       }
       epi_bar();
       const int row0 = m0 + 32 * q;
@@ -462,7 +466,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         return b;
       };
       if (have) {
-        if (swiglu) {
+        if constexpr (swiglu) {
           // both chunks' SwiGLU values are computed (packed as f16 hi / lo)
           // before TMEM is released; staging and stores come after
           uint32_t hl[2][16];
@@ -512,6 +516,80 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               bulk_commit();
             }
           }
+        } else if constexpr (EK == EPI_QKV) {
+          // this warp's 64 columns are one head of q, k or v: bias, then for
+          // q and k the sum of squares of y (their QK-norm, applied to the
+          // attention scores), the norm gain and the RoPE of the token's
+          // patch position; each 16-column chunk is split into f16 hi / lo.
+          // Chunks 0-1 are staged, chunk 2 kept in registers and chunk 3
+          // loaded before TMEM is released; the TMA stores (as for the SwiGLU
+          // output) are all issued after the release.
+          const int col0 = nt * BN + 64 * quarter;  // first column of the head
+          const int seg = col0 / e.E;               // 0: q, 1: k, 2: v
+          const int pos = live ? m % e.p : 0;  // patch position of this thread's token
+          float ss = 0.0f;
+          uint8_t *stg_a[2];
+          uint32_t hk[16];  // chunk 2, split
+          auto make = [&](int ch, float *v, uint32_t *hl) {
+            const int c0 = 64 * quarter + 16 * ch;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] += sb[c0 + i];
+            if (seg < 2) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                ss += v[i] * v[i];
+                v[i] *= sb[BN + c0 + i];
+              }
+              rope16_t(v, e.rope_t, e.p, pos, ch, seg == 1);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) split2(v[2 * i], v[2 * i + 1], hl[i], hl[8 + i]);
+          };
+          auto stage = [&](const uint32_t *hl) -> uint8_t * {
+            uint8_t *stg = next_stage_buf();
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const uint32_t o = lane * 32 + ((j ^ ((lane >> 2) & 1)) << 4);
+              *reinterpret_cast<uint4 *>(stg + o) = make_uint4(hl[4 * j], hl[4 * j + 1], hl[4 * j + 2], hl[4 * j + 3]);
+              *reinterpret_cast<uint4 *>(stg + 1024 + o) =
+                  make_uint4(hl[8 + 4 * j], hl[8 + 4 * j + 1], hl[8 + 4 * j + 2], hl[8 + 4 * j + 3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            return stg;
+          };
+          auto store = [&](const uint8_t *stg, int ch) {
+            if (lane == 0) {
+              tma_store_2d(&tm_zh, stg, col0 + 16 * ch, row0);
+              tma_store_2d(&tm_zl, stg + 1024, col0 + 16 * ch, row0);
+              bulk_commit();
+            }
+          };
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch) {
+            float v[16];
+            uint32_t hl[16];
+            tmem_ld_pair16(trow + 64 * quarter + 16 * ch, v, sc);
+            make(ch, v, hl);
+            stg_a[ch] = stage(hl);
+          }
+          {
+            float v[16];
+            tmem_ld_pair16(trow + 64 * quarter + 32, v, sc);
+            make(2, v, hk);
+          }
+          float v3[16];
+          tmem_ld_pair16(trow + 64 * quarter + 48, v3, sc);
+          release();
+          store(stg_a[0], 0);
+          store(stg_a[1], 1);
+          store(stage(hk), 2);
+          {
+            uint32_t hl[16];
+            make(3, v3, hl);
+            store(stage(hl), 3);
+          }
+          if (seg < 2 && live) e.ssq_qk[(size_t)m * 2 * e.H + seg * e.H + ((col0 - seg * e.E) >> 6)] = ss;
         } else {  // EPI_PLAIN
           // two chunks at a time: chunks 0-1 are loaded, staged and stored,
           // then chunks 2-3 are loaded and TMEM is released
@@ -623,50 +701,11 @@ int max_pairs(const void *kfn, const cudaLaunchConfig_t &cfg) {
   return n;
 }
 
-template <int QT>
-cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows, int wshift,
-                        const Epi &epi, int *err, cudaStream_t st) {
-  CUtensorMap txh, txl, tw;
-  const uint64_t rb = (uint64_t)(K / 32) * TQ<QT>::bpb;
-  if (!make_tmap_2d(&txh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ah, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BM,
-                    CU_TENSOR_MAP_SWIZZLE_64B) ||
-      !make_tmap_2d(&txl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, al, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BM,
-                    CU_TENSOR_MAP_SWIZZLE_64B) ||
-      !make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, rb, (uint64_t)wrows, rb, TQ<QT>::rawb, 128,
-                    CU_TENSOR_MAP_SWIZZLE_NONE))
-    return cudaErrorInvalidValue;
-  if (epi.kind != EPI_PLAIN && epi.kind != EPI_SWIGLU) return cudaErrorInvalidValue;
-  // output maps for the epilogue's TMA stores (the unused kind's maps repeat
-  // a valid one; the kernel never touches them)
-  CUtensorMap ty, tzh, tzl;
-  if (epi.kind == EPI_PLAIN) {
-    if (!epi.y || epi.ldy < epi.N || epi.ldy % 4 ||
-        !make_tmap_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, epi.y, (uint64_t)epi.N, (uint64_t)M,
-                      (uint64_t)epi.ldy * 4, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B))
-      return cudaErrorInvalidValue;
-    tzh = tzl = ty;
-  } else {
-    if (!epi.zh || !epi.zl ||
-        !make_tmap_2d(&tzh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, epi.zh, (uint64_t)epi.F, (uint64_t)M,
-                      (uint64_t)epi.F * 2, 16, 32, CU_TENSOR_MAP_SWIZZLE_32B) ||
-        !make_tmap_2d(&tzl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, epi.zl, (uint64_t)epi.F, (uint64_t)M,
-                      (uint64_t)epi.F * 2, 16, 32, CU_TENSOR_MAP_SWIZZLE_32B))
-      return cudaErrorInvalidValue;
-    ty = tzh;
-  }
-  TcParams prm;
-  prm.M = M;
-  prm.N = epi.N;
-  prm.K = K;
-  prm.swiglu_F = epi.kind == EPI_SWIGLU ? epi.F : 0;
-  prm.n_tiles_n = epi.kind == EPI_SWIGLU ? epi.F / 128 : epi.N / BN;
-  prm.wscale = ldexpf(1.0f, wshift);
-  prm.acc_scale = ldexpf(1.0f, -wshift);
-  prm.epi = epi;
-  prm.err = err;
+template <int QT, int EK>
+cudaError_t launch_tc_k(const CUtensorMap &txh, const CUtensorMap &txl, const CUtensorMap &tw, const CUtensorMap &ty,
+                        const CUtensorMap &tzh, const CUtensorMap &tzl, const TcParams &prm, cudaStream_t st) {
   using P = PCfg<QT>;
-  prm.n_tiles = prm.n_tiles_n * ((M + 2 * BM - 1) / (2 * BM));
-  auto kfn = gemm_q_tc_pair_kernel<QT>;
+  auto kfn = gemm_q_tc_pair_kernel<QT, EK>;
   cudaError_t e = t0b_smem_limit((const void *)kfn, P::SMEM);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
@@ -685,6 +724,57 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
   const int np = prm.n_tiles < pairs ? prm.n_tiles : pairs;  // persistent: one CTA pair per SM pair
   cfg.gridDim = dim3(2 * np);
   return cudaLaunchKernelEx(&cfg, kfn, txh, txl, tw, ty, tzh, tzl, prm);
+}
+
+template <int QT>
+cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows, int wshift,
+                        const Epi &epi, int *err, cudaStream_t st) {
+  CUtensorMap txh, txl, tw;
+  const uint64_t rb = (uint64_t)(K / 32) * TQ<QT>::bpb;
+  if (!make_tmap_2d(&txh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ah, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BM,
+                    CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !make_tmap_2d(&txl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, al, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BM,
+                    CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, rb, (uint64_t)wrows, rb, TQ<QT>::rawb, 128,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  if (epi.kind != EPI_PLAIN && epi.kind != EPI_SWIGLU && epi.kind != EPI_QKV) return cudaErrorInvalidValue;
+  if (epi.kind == EPI_QKV &&
+      (epi.F != 3 * epi.E || epi.N != epi.F || epi.E % 64 || epi.E / 64 != epi.H || !epi.qn || !epi.kn ||
+       !epi.rope_t || !epi.ssq_qk || epi.p < 1))
+    return cudaErrorInvalidValue;
+  // output maps for the epilogue's TMA stores (the unused kind's maps repeat
+  // a valid one; the kernel never touches them)
+  CUtensorMap ty, tzh, tzl;
+  if (epi.kind == EPI_PLAIN) {
+    if (!epi.y || epi.ldy < epi.N || epi.ldy % 4 ||
+        !make_tmap_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, epi.y, (uint64_t)epi.N, (uint64_t)M,
+                      (uint64_t)epi.ldy * 4, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return cudaErrorInvalidValue;
+    tzh = tzl = ty;
+  } else {  // SWIGLU and QKV: f16 (hi, lo) planes of F columns
+    if (!epi.zh || !epi.zl ||
+        !make_tmap_2d(&tzh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, epi.zh, (uint64_t)epi.F, (uint64_t)M,
+                      (uint64_t)epi.F * 2, 16, 32, CU_TENSOR_MAP_SWIZZLE_32B) ||
+        !make_tmap_2d(&tzl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, epi.zl, (uint64_t)epi.F, (uint64_t)M,
+                      (uint64_t)epi.F * 2, 16, 32, CU_TENSOR_MAP_SWIZZLE_32B))
+      return cudaErrorInvalidValue;
+    ty = tzh;
+  }
+  TcParams prm;
+  prm.M = M;
+  prm.N = epi.N;
+  prm.K = K;
+  prm.swiglu_F = epi.kind == EPI_SWIGLU ? epi.F : 0;
+  prm.n_tiles_n = epi.kind == EPI_SWIGLU ? epi.F / 128 : epi.N / BN;
+  prm.wscale = ldexpf(1.0f, wshift);
+  prm.acc_scale = ldexpf(1.0f, -wshift);
+  prm.epi = epi;
+  prm.err = err;
+  prm.n_tiles = prm.n_tiles_n * ((M + 2 * BM - 1) / (2 * BM));
+  if (epi.kind == EPI_SWIGLU) return launch_tc_k<QT, EPI_SWIGLU>(txh, txl, tw, ty, tzh, tzl, prm, st);
+  if (epi.kind == EPI_QKV) return launch_tc_k<QT, EPI_QKV>(txh, txl, tw, ty, tzh, tzl, prm, st);
+  return launch_tc_k<QT, EPI_PLAIN>(txh, txl, tw, ty, tzh, tzl, prm, st);
 }
 
 }  // namespace
@@ -720,7 +810,8 @@ bool t0b_make_tmap_f16_3d(CUtensorMap *tm, const void *ptr, uint64_t d0, uint64_
 // number of rows of W (N, or 2F for SWIGLU); `wshift` the weight prescale
 // exponent from t0b_weight_shift.  Epilogue kinds: PLAIN (bias + optional
 // RMSNorm row scale; with reduce_add the tile is added into y by TMA
-// reduce-adds) and SWIGLU; others are rejected (cudaErrorInvalidValue).
+// reduce-adds), SWIGLU and QKV (N = F = 3E, 64-dim heads); others are
+// rejected (cudaErrorInvalidValue).
 cudaError_t t0b_launch_gemm_tc(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
                                int wshift, const Epi &epi, int *err, cudaStream_t st) {
   if (qt == 8) return launch_tc_t<8>(ah, al, M, K, W, wrows, wshift, epi, err, st);

@@ -561,25 +561,6 @@ T0B_DEV uint32_t pack_h2(__half lo_elem, __half hi_elem) {
 }
 
 
-// RoPE on 16 consecutive dims 16cg..16cg+15 (8 pairs) with 16-byte table
-// loads; same arithmetic as rope_pair.
-T0B_DEV void rope16(float *x, const float *tab, int cg, bool kside) {
-  const float4 *t4 = reinterpret_cast<const float4 *>(tab);
-  const float4 c0 = t4[2 * cg], c1 = t4[2 * cg + 1], n0 = t4[8 + 2 * cg], n1 = t4[8 + 2 * cg + 1];
-  const float4 *sp = t4 + (kside ? 24 : 16) + ((16 * cg) & 31) / 4;
-  const float4 s0 = sp[0], s1 = sp[1], s2 = sp[2], s3 = sp[3];
-  const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-  const float sn[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
-  const float sv[16] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w,
-                        s2.x, s2.y, s2.z, s2.w, s3.x, s3.y, s3.z, s3.w};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float a0 = x[2 * i], a1 = x[2 * i + 1];
-    x[2 * i] = a0 * cs[i] * sv[2 * i] + (-a1) * sn[i] * sv[2 * i];
-    x[2 * i + 1] = a1 * cs[i] * sv[2 * i + 1] + a0 * sn[i] * sv[2 * i + 1];
-  }
-}
-
 // Shared-memory layout of attn_time_mma_kernel past its 1024-byte aligned
 // base: the four f16 planes [4][PK][72] (the k / v TMA tiles alias their
 // start), the q tile [2][PK][32] f32 (1024-byte aligned), the mbarrier.
@@ -930,6 +911,242 @@ __global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a, const
     }
   }
   if (tma_out && lane == 0) bulk_wait_all();  // stores done before the CTA (and its shared memory) ends
+}
+
+// --------------------------------------- time attention on f16 planes
+// Time attention for one (variate row, head) of 64 dims when the wQKV GEMM
+// has written q, k and v as f16 (hi, lo) planes (its EPI_QKV epilogue): q
+// and k arrive multiplied by their QK-norm gains and rotated by RoPE, and
+// their QK-norm, 1/sqrt(mean(y^2) + 1e-8) per (token, head), enters here as
+// a per-query and per-key scale of the scores (RoPE is linear, so this is
+// the same product as norm-then-rotate, ops.rs:132-142, 175-190).  The six
+// [PK][64] tiles (q, k, v; hi and lo) come in by one TMA load each with the
+// 128-byte swizzle, straight into the layout the ldmatrix fragment loads
+// read (16-byte unit u of row r at unit u ^ (r & 7)); rows p .. PK-1 lie
+// outside the [R][p][3E] tensor map and arrive as zeros.  There is no
+// per-row conversion: each warp takes one block of 16 queries through
+// split-f16 QK^T and PV on mma.sync with an online softmax and the masks of
+// attn_time_mma_kernel, and writes its 16 output rows as f16 planes by TMA
+// stores staged in its own (already consumed) q rows.
+__host__ __device__ constexpr size_t attn_pl_smem_bytes(int PK) {
+  return (size_t)6 * PK * 128 + (size_t)2 * PK * 4 + 16 + 1024;  // tiles, norm factors, mbarrier, alignment
+}
+// Byte offset of 16-byte unit u of row r in a 128-byte-swizzled [rows][64] f16 tile.
+T0B_DEV uint32_t sw128_unit(int r, int u) { return (uint32_t)r * 128u + ((uint32_t)(u ^ (r & 7)) << 4); }
+
+__global__ void __launch_bounds__(512, 1) attn_time_pl_kernel(AttnArgs a, const __grid_constant__ CUtensorMap tm_h,
+                                                              const __grid_constant__ CUtensorMap tm_l,
+                                                              const __grid_constant__ CUtensorMap tm_oh,
+                                                              const __grid_constant__ CUtensorMap tm_ol) {
+  pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
+  extern __shared__ __align__(128) uint4 smem_u4[];
+  uint8_t *base = reinterpret_cast<uint8_t *>(smem_u4) + ((1024u - (smem_u32(smem_u4) & 1023u)) & 1023u);
+  const int r = blockIdx.x, h = blockIdx.y;
+  const int p = a.p, E = a.E, H = a.H;
+  const int QB = (p + 15) >> 4;  // blocks of 16 queries (= keys), one per warp
+  const int PK = QB * 16;
+  const uint32_t tile = (uint32_t)PK * 128u;
+  uint8_t *Qh = base, *Ql = base + tile, *Kh = base + 2 * tile, *Kl = base + 3 * tile;
+  uint8_t *Vh = base + 4 * tile, *Vl = base + 5 * tile;
+  float *rq = reinterpret_cast<float *>(base + 6 * tile);
+  float *rk = rq + PK;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(rk + PK);
+  const size_t tok0 = (size_t)r * p;
+  const int lo = a.row_first_valid[r];
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  for (int j = threadIdx.x; j < PK; j += blockDim.x) {  // QK-norm factors (rows >= p unused)
+    float fq = 0.0f, fk = 0.0f;
+    if (j < p) {
+      const float *ss = a.ssq_qk + (tok0 + j) * 2 * H;
+      fq = 1.0f / sqrtf(ss[h] / 64.0f + 1e-8f);
+      fk = 1.0f / sqrtf(ss[H + h] / 64.0f + 1e-8f);
+    }
+    rq[j] = fq;
+    rk[j] = fk;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(bar, 6 * tile);
+#pragma unroll
+    for (int sg = 0; sg < 3; ++sg) {  // q, k, v
+      tma_load_3d(base + (2 * sg) * tile, &tm_h, bar, sg * E + h * 64, 0, r);
+      tma_load_3d(base + (2 * sg + 1) * tile, &tm_l, bar, sg * E + h * 64, 0, r);
+    }
+  }
+  mbar_wait(bar, 0, a.err, T0B_DEVERR_WAIT_ATTN, nullptr);
+
+  const int qb = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int ia = qb * 16 + g, ib = ia + 8;  // this thread's two query rows
+  // q fragments of the block: ldmatrix matrix m = lane / 8 -> rows (m % 2) * 8 + lane % 8, dims (m / 2) * 8
+  uint32_t qh[4][4], ql[4][4];
+  {
+    const int row = qb * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {
+      const uint32_t off = sw128_unit(row, 2 * kc + (lane >> 4));
+      ldsm_x4(Qh + off, qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3]);
+      ldsm_x4(Ql + off, ql[kc][0], ql[kc][1], ql[kc][2], ql[kc][3]);
+    }
+  }
+  const float fa = rq[ia] * 0.125f, fb = rq[ib] * 0.125f;  // QK-norm of the two query rows x 1/sqrt(64)
+
+  const bool any_masked = qb * 16 < lo;  // a whole-padding query in this block
+  const int kb0 = any_masked ? 0 : (lo >> 4), kb1 = any_masked ? QB - 1 : qb;
+  float o[8][4];
+#pragma unroll
+  for (int nd = 0; nd < 8; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.0f;
+  float ma = -INFINITY, mb = -INFINITY, la = 0.0f, lb = 0.0f;
+  for (int kb = kb0; kb <= kb1; ++kb) {
+    float sc[2][4];
+#pragma unroll
+    for (int nh = 0; nh < 2; ++nh) sc[nh][0] = sc[nh][1] = sc[nh][2] = sc[nh][3] = 0.0f;
+    // ldmatrix rows: matrix m = lane / 8 -> keys (m / 2) * 8 + (lane % 8), dims (m % 2) * 8
+    const int krow = kb * 16 + ((lane >> 4) << 3) + (lane & 7);
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {
+      uint32_t h00, h01, h10, h11, l00, l01, l10, l11;  // [key half][dim half]
+      const uint32_t off = sw128_unit(krow, 2 * kc + ((lane >> 3) & 1));
+      ldsm_x4(Kh + off, h00, h01, h10, h11);
+      ldsm_x4(Kl + off, l00, l01, l10, l11);
+      mma16816(sc[0][0], sc[0][1], sc[0][2], sc[0][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], h00, h01);
+      mma16816(sc[1][0], sc[1][1], sc[1][2], sc[1][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], h10, h11);
+      mma16816(sc[0][0], sc[0][1], sc[0][2], sc[0][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], l00, l01);
+      mma16816(sc[1][0], sc[1][1], sc[1][2], sc[1][3], qh[kc][0], qh[kc][1], qh[kc][2], qh[kc][3], l10, l11);
+      mma16816(sc[0][0], sc[0][1], sc[0][2], sc[0][3], ql[kc][0], ql[kc][1], ql[kc][2], ql[kc][3], h00, h01);
+      mma16816(sc[1][0], sc[1][1], sc[1][2], sc[1][3], ql[kc][0], ql[kc][1], ql[kc][2], ql[kc][3], h10, h11);
+    }
+    // QK-norm scales + masks; e = 0,1: row ia, e = 2,3: row ib
+    float bma = -INFINITY, bmb = -INFINITY;
+#pragma unroll
+    for (int nh = 0; nh < 2; ++nh) {
+      const int k0 = kb * 16 + nh * 8 + 2 * t;
+      const float2 fk = *reinterpret_cast<const float2 *>(rk + k0);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = e < 2 ? ia : ib;
+        const int key = k0 + (e & 1);
+        float s = sc[nh][e] * (e < 2 ? fa : fb) * ((e & 1) ? fk.y : fk.x);
+        if (row >= p || row < lo)  // padding row / whole-padding query: uniform over the p keys
+          s = key < p ? -1.0e9f : -INFINITY;
+        else if (key < lo || key > row)
+          s = -INFINITY;
+        sc[nh][e] = s;
+        if (e < 2) bma = fmaxf(bma, s); else bmb = fmaxf(bmb, s);
+      }
+    }
+    bma = fmaxf(bma, __shfl_xor_sync(0xffffffffu, bma, 1));
+    bma = fmaxf(bma, __shfl_xor_sync(0xffffffffu, bma, 2));
+    bmb = fmaxf(bmb, __shfl_xor_sync(0xffffffffu, bmb, 1));
+    bmb = fmaxf(bmb, __shfl_xor_sync(0xffffffffu, bmb, 2));
+    const float na = fmaxf(ma, bma), nb = fmaxf(mb, bmb);
+    const float ua = na == -INFINITY ? 0.0f : na, ub = nb == -INFINITY ? 0.0f : nb;
+    const float ca = expf(ma - ua), cb = expf(mb - ub);  // rescale of what came before (0 at the start)
+    ma = na;
+    mb = nb;
+    la *= ca;
+    lb *= cb;
+#pragma unroll
+    for (int nd = 0; nd < 8; ++nd) {
+      o[nd][0] *= ca, o[nd][1] *= ca;
+      o[nd][2] *= cb, o[nd][3] *= cb;
+    }
+#pragma unroll
+    for (int nh = 0; nh < 2; ++nh)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float pe = expf(sc[nh][e] - (e < 2 ? ua : ub));
+        sc[nh][e] = pe;
+        if (e < 2) la += pe; else lb += pe;
+      }
+    // P as the A operand (16 queries x 16 keys of this block), split hi/lo
+    uint32_t ph[4], pl[4];
+    split2(sc[0][0], sc[0][1], ph[0], pl[0]);
+    split2(sc[0][2], sc[0][3], ph[1], pl[1]);
+    split2(sc[1][0], sc[1][1], ph[2], pl[2]);
+    split2(sc[1][2], sc[1][3], ph[3], pl[3]);
+    // transposed ldmatrix rows: matrix m -> keys (m % 2) * 8 + (lane % 8), dims (m / 2) * 8
+    const int vrow = kb * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+    for (int n2 = 0; n2 < 4; ++n2) {  // dims 16 n2 .. 16 n2 + 15 = n8 blocks 2 n2, 2 n2 + 1
+      uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+      const uint32_t off = sw128_unit(vrow, 2 * n2 + (lane >> 4));
+      ldsm_x4_trans(Vh + off, h0, h1, h2, h3);
+      ldsm_x4_trans(Vl + off, l0, l1, l2, l3);
+      float *oa = o[2 * n2], *ob = o[2 * n2 + 1];
+      mma16816(oa[0], oa[1], oa[2], oa[3], ph[0], ph[1], ph[2], ph[3], h0, h1);
+      mma16816(ob[0], ob[1], ob[2], ob[3], ph[0], ph[1], ph[2], ph[3], h2, h3);
+      mma16816(oa[0], oa[1], oa[2], oa[3], ph[0], ph[1], ph[2], ph[3], l0, l1);
+      mma16816(ob[0], ob[1], ob[2], ob[3], ph[0], ph[1], ph[2], ph[3], l2, l3);
+      mma16816(oa[0], oa[1], oa[2], oa[3], pl[0], pl[1], pl[2], pl[3], h0, h1);
+      mma16816(ob[0], ob[1], ob[2], ob[3], pl[0], pl[1], pl[2], pl[3], h2, h3);
+    }
+  }
+  la += __shfl_xor_sync(0xffffffffu, la, 1);
+  la += __shfl_xor_sync(0xffffffffu, la, 2);
+  lb += __shfl_xor_sync(0xffffffffu, lb, 1);
+  lb += __shfl_xor_sync(0xffffffffu, lb, 2);
+  const float inva = 1.0f / la, invb = 1.0f / lb;
+  // this warp's 16 output rows: hi plane in its q-tile rows of the hi tile, lo
+  // plane in its rows of the lo tile (2 KB each, 128-byte swizzle); rows >= p
+  // are clipped by the tensor maps
+  uint8_t *sh = Qh + (size_t)(qb * 16) * 128, *sl = Ql + (size_t)(qb * 16) * 128;
+#pragma unroll
+  for (int nd = 0; nd < 8; ++nd) {
+    uint32_t hw, lw;
+    const uint32_t ua = (uint32_t)g * 128 + (((uint32_t)nd ^ (uint32_t)g) << 4) + 4 * t;
+    split2(o[nd][0] * inva, o[nd][1] * inva, hw, lw);
+    *reinterpret_cast<uint32_t *>(sh + ua) = hw;
+    *reinterpret_cast<uint32_t *>(sl + ua) = lw;
+    split2(o[nd][2] * invb, o[nd][3] * invb, hw, lw);
+    *reinterpret_cast<uint32_t *>(sh + ua + 8 * 128) = hw;
+    *reinterpret_cast<uint32_t *>(sl + ua + 8 * 128) = lw;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_3d(&tm_oh, sh, h * 64, qb * 16, r);
+    tma_store_3d(&tm_ol, sl, h * 64, qb * 16, r);
+    bulk_commit();
+    bulk_wait_all();  // stores done before the CTA (and its shared memory) ends
+  }
+  if (a.o32) {  // optional f32 copy of the output
+#pragma unroll
+    for (int nd = 0; nd < 8; ++nd) {
+      const int d = nd * 8 + 2 * t;
+      if (ia < p)
+        *reinterpret_cast<float2 *>(a.o32 + (tok0 + ia) * E + h * 64 + d) = make_float2(o[nd][0] * inva, o[nd][1] * inva);
+      if (ib < p)
+        *reinterpret_cast<float2 *>(a.o32 + (tok0 + ib) * E + h * 64 + d) = make_float2(o[nd][2] * invb, o[nd][3] * invb);
+    }
+  }
+}
+
+cudaError_t t0b_launch_attn_time_planes(const AttnArgs &a, cudaStream_t st) {
+  if (a.E / a.H != 64 || a.E % 64 || a.p < 1 || a.p > 256 || !a.qkv_h || !a.qkv_l || !a.ssq_qk || !a.oh || !a.ol)
+    return cudaErrorInvalidValue;
+  const int QB = (a.p + 15) / 16, PK = 16 * QB;
+  const size_t smem = attn_pl_smem_bytes(PK);
+  cudaError_t e = t0b_smem_limit((const void *)attn_time_pl_kernel, smem);
+  if (e != cudaSuccess) return e;
+  // q | k | v planes as [R][p][3E] f16 with [1][PK][64] boxes (rows >= p zero);
+  // output planes as [R][p][E] f16 with [1][16][64] boxes (rows >= p clipped)
+  CUtensorMap th, tl, toh, tol;
+  const uint64_t rs = (uint64_t)3 * a.E * 2, ss = rs * (uint64_t)a.p;
+  const uint64_t ors = (uint64_t)a.E * 2, oss = ors * (uint64_t)a.p;
+  if (!t0b_make_tmap_f16_3d(&th, a.qkv_h, (uint64_t)3 * a.E, (uint64_t)a.p, (uint64_t)a.R, rs, ss, 64, (uint32_t)PK, 1,
+                            true) ||
+      !t0b_make_tmap_f16_3d(&tl, a.qkv_l, (uint64_t)3 * a.E, (uint64_t)a.p, (uint64_t)a.R, rs, ss, 64, (uint32_t)PK, 1,
+                            true) ||
+      !t0b_make_tmap_f16_3d(&toh, a.oh, (uint64_t)a.E, (uint64_t)a.p, (uint64_t)a.R, ors, oss, 64, 16, 1, true) ||
+      !t0b_make_tmap_f16_3d(&tol, a.ol, (uint64_t)a.E, (uint64_t)a.p, (uint64_t)a.R, ors, oss, 64, 16, 1, true))
+    return cudaErrorInvalidValue;
+  attn_time_pl_kernel<<<dim3(a.R, a.H), 32 * QB, smem, st>>>(a, th, tl, toh, tol);
+  return cudaGetLastError();
 }
 
 // ------------------------------------------------- 128-dim heads (t0-beta)

@@ -57,6 +57,11 @@ struct AttnArgs {
   int R, p, E, H, n_series;
   int max_nrows;  // largest series_nrows entry (host-side bound for the group kernel)
   int *err;       // device error word (a bounded wait that ran out)
+  // time attention on f16 planes (t0b_launch_attn_time_planes): q | k | v as
+  // (hi, lo) planes [R p][3E] written by the wQKV GEMM's EPI_QKV epilogue,
+  // and the per-(token, head) sums of squares of q and k [R p][2H]
+  const __half *qkv_h, *qkv_l;
+  const float *ssq_qk;
 };
 
 // Tensor map of an f32 row-major [outer][inner] tensor with rows row_bytes
@@ -95,6 +100,9 @@ cudaError_t t0b_launch_sgemm(const SgemmArgs &a, cudaStream_t st);
 cudaError_t t0b_launch_rownorm_split(const float *x, const float *g, __half *xh, __half *xl, float *ssq, int M, int E,
                                      cudaStream_t st);
 cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st);
+// Time attention for 64-dim heads on the planes of the EPI_QKV epilogue
+// (qkv_h, qkv_l, ssq_qk), p <= 256.
+cudaError_t t0b_launch_attn_time_planes(const AttnArgs &a, cudaStream_t st);
 cudaError_t t0b_launch_attn_group(const AttnArgs &a, cudaStream_t st);
 cudaError_t t0b_launch_dec_gather(const float *x, const float *g, float *xo, int R, int p, int hp, int E,
                                   cudaStream_t st);

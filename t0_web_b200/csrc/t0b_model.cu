@@ -113,6 +113,7 @@ struct t0b_model {
   std::map<int, float *> rope;  // p -> [4][p][hd] device tables: cos, sin, scale, 1/scale
   // workspace
   DBuf x, qkv, feat, ssq, xo, dhid, dout, loc, scl;
+  DBuf ssqk;  // per-(token, head) sums of squares of q and k (TIME layers on the tensor-core path)
   DBuf xh, xl, ah, al, hh, hl;
   DBuf meta;  // row/series metadata
   HBuf hmeta;
@@ -436,8 +437,10 @@ t0b_status rope_tables(t0b_model *m, int p, const float **out) {
     return T0B_OK;
   }
   const int hd = m->E / m->H, half = hd / 2;
-  // [4][p][hd] full tables, then the [p][2 hd] compact copy
-  std::vector<float> h((size_t)4 * p * hd + (size_t)p * 2 * hd);
+  // [4][p][hd] full tables, then the [p][2 hd] compact copy, then the same
+  // compact table transposed, [2 hd][p] (entry-major: a warp of consecutive
+  // tokens reads one entry of consecutive positions in one coalesced access)
+  std::vector<float> h((size_t)4 * p * hd + (size_t)2 * p * 2 * hd);
   float *cs = h.data(), *sn = cs + (size_t)p * hd, *sc = sn + (size_t)p * hd, *si = sc + (size_t)p * hd;
   const double theta = 10000.0, base512 = 512.0;
   const double max_half = std::floor((double)(p - 1) / 2.0);
@@ -462,6 +465,9 @@ t0b_status rope_tables(t0b_model *m, int p, const float **out) {
       cc[pos * 2 * hd + 2 * half + j] = sc[pos * hd + j];
       cc[pos * 2 * hd + 3 * half + j] = si[pos * hd + j];
     }
+  float *ct = cc + (size_t)p * 2 * hd;
+  for (int pos = 0; pos < p; ++pos)
+    for (int j = 0; j < 2 * hd; ++j) ct[(size_t)j * p + pos] = cc[pos * 2 * hd + j];
   float *d = nullptr;
   if (cudaMalloc(&d, h.size() * 4) != cudaSuccess) return fail(T0B_ERR_OOM, "t0b: out of device memory");
   CUDA_TRY(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
@@ -591,6 +597,7 @@ t0b_status ensure_ws(t0b_model *m, size_t T, size_t R, size_t nout) {
   CUDA_TRY(m->qkv.reserve(T * 3 * E * 4));
   CUDA_TRY(m->feat.reserve(T * 96 * 4));
   CUDA_TRY(m->ssq.reserve(T * std::max<size_t>(16, E / 32) * 4));
+  CUDA_TRY(m->ssqk.reserve(T * 2 * (size_t)m->H * 4));
   CUDA_TRY(m->xh.reserve(T * E * 2));
   CUDA_TRY(m->xl.reserve(T * E * 2));
   CUDA_TRY(m->ah.reserve(T * E * 2));
@@ -654,8 +661,8 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
     // a workspace buffer that was reallocated invalidates every cached graph
     // (a graph may hold its old allocation, even at an address reused since)
     std::vector<uint64_t> sig{(uint64_t)(uintptr_t)m->hmeta.p, (uint64_t)m->hmeta.bytes};
-    for (const DBuf *b : {&m->x, &m->qkv, &m->feat, &m->ssq, &m->xo, &m->dhid, &m->dout, &m->loc, &m->scl, &m->xh,
-                          &m->xl, &m->ah, &m->al, &m->hh, &m->hl, &m->meta, &m->ctx_stage, &m->out_stage}) {
+    for (const DBuf *b : {&m->x, &m->qkv, &m->feat, &m->ssq, &m->ssqk, &m->xo, &m->dhid, &m->dout, &m->loc, &m->scl,
+                          &m->xh, &m->xl, &m->ah, &m->al, &m->hh, &m->hl, &m->meta, &m->ctx_stage, &m->out_stage}) {
       sig.push_back((uint64_t)(uintptr_t)b->p);
       sig.push_back((uint64_t)b->bytes);
     }
@@ -668,8 +675,8 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
            (uint64_t)(uintptr_t)rope, (uint64_t)m->tc_min_tokens,
            // the group-attention kernel variant depends on the largest series
            (uint64_t)(ps.s_nrows.empty() ? 0 : *std::max_element(ps.s_nrows.begin(), ps.s_nrows.end()))};
-    for (const DBuf *b : {&m->x, &m->qkv, &m->feat, &m->ssq, &m->xo, &m->dhid, &m->dout, &m->loc, &m->scl, &m->xh,
-                          &m->xl, &m->ah, &m->al, &m->hh, &m->hl, &m->meta})
+    for (const DBuf *b : {&m->x, &m->qkv, &m->feat, &m->ssq, &m->ssqk, &m->xo, &m->dhid, &m->dout, &m->loc, &m->scl,
+                          &m->xh, &m->xl, &m->ah, &m->al, &m->hh, &m->hl, &m->meta})
       key.push_back((uint64_t)(uintptr_t)b->p);
     auto it = m->graphs.find(key);
     if (it != m->graphs.end()) {
@@ -756,13 +763,22 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   const int M = (int)T;
   aa.rope = rope;
   aa.rope_c = rope + (size_t)4 * p * (E / m->H);  // after the [4][p][hd] full tables
+  // TIME layers on the tensor-core path with 64-dim heads: the wQKV epilogue
+  // writes gain-scaled, rotated q / k and v as f16 planes (the qkv buffer's
+  // bytes) plus the QK-norm sums of squares, and the time attention reads the
+  // planes by TMA without a conversion pass
+  const bool qkv_planes = E / m->H == 64 && p <= 256 && use_tc(m, M);
+  aa.qkv_h = m->qkv.as<__half>();
+  aa.qkv_l = aa.qkv_h + T * 3 * E;
+  aa.ssq_qk = m->ssqk.as<float>();
 
   for (int l = 0; l < m->L; ++l) {
     const LayerW &w = m->layers[l];
     // q | k | v = rmsnorm(x) . wQKV^T + b; QK-norm and RoPE happen in the
-    // attention kernels as q and k are read
+    // attention kernels as q and k are read, or in the epilogue (planes)
+    const bool planes = qkv_planes && !w.group;
     Epi e{};
-    e.kind = EPI_PLAIN;
+    e.kind = planes ? EPI_QKV : EPI_PLAIN;
     e.M = M;
     e.N = 3 * E;
     e.bias = w.bqkv;
@@ -771,6 +787,18 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
     e.ssq_dim = E;
     e.y = m->qkv.as<float>();
     e.ldy = 3 * E;
+    if (planes) {
+      e.F = 3 * E;
+      e.zh = m->qkv.as<__half>();
+      e.zl = e.zh + T * 3 * E;
+      e.qn = w.qn;
+      e.kn = w.kn;
+      e.rope_t = aa.rope_c + (size_t)p * 2 * (E / m->H);  // the transposed compact table
+      e.ssq_qk = m->ssqk.as<float>();
+      e.p = p;
+      e.E = E;
+      e.H = m->H;
+    }
     LAUNCH(qgemm(m, m->xh.as<__half>(), m->xl.as<__half>(), M, E, w.wqkv, 3 * E, w.sh_qkv, e));
     aa.qn = w.qn;
     aa.kn = w.kn;
@@ -780,7 +808,9 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
     } else {
       // causal pairs per row: p(p+1)/2, each 2*hd flops for q.k and 2*hd for p.v, per head
       const double fl = (double)R * m->H * (p * (p + 1) / 2.0) * 4.0 * (E / m->H);
-      LAUNCH(launch(m, KC_ATTN_TIME, fl, T * (3.0 * E * 4 + E * 4.0), [&] { return t0b_launch_attn_time(aa, m->stream); }));
+      LAUNCH(launch(m, KC_ATTN_TIME, fl, T * (3.0 * E * 4 + E * 4.0), [&] {
+        return planes ? t0b_launch_attn_time_planes(aa, m->stream) : t0b_launch_attn_time(aa, m->stream);
+      }));
     }
     LAUNCH(resid_gemm(m, m->ah.as<__half>(), m->al.as<__half>(), M, E, w.wo, w.sh_o, w.bo, x, w.g_mlp, &ssq_nt));
 
