@@ -242,6 +242,18 @@ T0B_DEV uint32_t sw64_offset(uint32_t r, uint32_t k) {
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
   return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
+// Per-warpgroup register budget (all 4 warps of a warpgroup execute it):
+// dec gives registers back to the CTA's pool, inc waits until the pool has
+// them.  The budgets of all warpgroups must fit the registers the kernel was
+// launched with.
+template <uint32_t N>
+T0B_DEV void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+T0B_DEV void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
 // ---------------------------------------------------------------- mma.sync
 T0B_DEV void mma16816(float &d0, float &d1, float &d2, float &d3, uint32_t a0, uint32_t a1, uint32_t a2,
                       uint32_t a3, uint32_t b0, uint32_t b1) {

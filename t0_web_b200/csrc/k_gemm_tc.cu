@@ -95,13 +95,16 @@ T0B_DEV void store_f32x16(float *dst, const float *v) {
 }
 
 // Dequantize one 32-value block of one weight row (raw window `src`, block
-// starting OFF bytes in) into 16 f16x2 hi words and 16 lo words:
-// hi = f16(2^s d q), lo = f16(2^s d q - hi).  OFF is a compile-time
-// constant (the block start inside the 16-byte aligned window is 34 s mod 16
-// or 18 s mod 16, always even), so every word index and shift is static and
-// the window stays in registers.
+// starting OFF bytes in) into tile row r of the Wh / Wl tiles:
+// hi = f16(2^s d q), lo = f16(2^s d q - hi), in the canonical K-major SW64
+// layout (16-byte unit c of row r at sw64_offset(r, 8c)).  OFF is a
+// compile-time constant (the block start inside the 16-byte aligned window
+// is 34 s mod 16 or 18 s mod 16, always even), so every word index and shift
+// is static and the window stays in registers; each 16-byte unit is stored
+// as soon as its 8 values are made, which keeps the dequant warps within
+// their register share.
 template <int QT, int OFF>
-T0B_DEV void dequant_block(const uint8_t *src, float wscale, uint32_t *hv, uint32_t *lv) {
+T0B_DEV void dequant_row(const uint8_t *src, float wscale, uint8_t *whs, uint8_t *wls, int r) {
   constexpr int RAWB = TQ<QT>::rawb;
   constexpr int NW = QT == 8 ? 8 : 4;  // 32-bit words of quants in a block
   uint32_t wv[RAWB / 4 + 1];
@@ -122,45 +125,48 @@ T0B_DEV void dequant_block(const uint8_t *src, float wscale, uint32_t *hv, uint3
   };
   const __half dh = __float2half_rn(__half2float(__ushort_as_half((unsigned short)dbits)) * wscale);  // exact
   const __half2 d2 = __halves2half2(dh, dh);
-  auto emit = [&](uint32_t qv, int pair) {
+  auto emit = [&](uint32_t qv, uint32_t &hv, uint32_t &lv) {
     __half2 h = __hmul2(d2, *reinterpret_cast<__half2 *>(&qv));
     __half2 l = __hfma2(d2, *reinterpret_cast<__half2 *>(&qv), __hneg2(h));  // exact residual, rounded once
-    hv[pair] = *reinterpret_cast<uint32_t *>(&h);
-    lv[pair] = *reinterpret_cast<uint32_t *>(&l);
+    hv = *reinterpret_cast<uint32_t *>(&h);
+    lv = *reinterpret_cast<uint32_t *>(&l);
+  };
+  auto put = [&](int c, const uint32_t *hv, const uint32_t *lv) {  // 16-byte unit c = values 8c .. 8c + 7
+    const uint32_t o = sw64_offset(r, 8 * c);
+    *reinterpret_cast<uint4 *>(whs + o) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+    *reinterpret_cast<uint4 *>(wls + o) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
   };
   if (QT == 8) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      uint32_t a, b;
-      i8x4_to_h2x2(word_q(i), a, b);  // int8 values 4i..4i+3
-      emit(a, 2 * i);
-      emit(b, 2 * i + 1);
+    for (int c = 0; c < 4; ++c) {
+      uint32_t hv[4], lv[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        uint32_t a, b;
+        i8x4_to_h2x2(word_q(2 * c + j), a, b);  // int8 values 8c + 4j .. 8c + 4j + 3
+        emit(a, hv[2 * j], lv[2 * j]);
+        emit(b, hv[2 * j + 1], lv[2 * j + 1]);
+      }
+      put(c, hv, lv);
     }
   } else {
-    // byte b holds value b (low nibble) and value b+16 (high nibble)
+    // byte b holds value b (low nibble) and value b+16 (high nibble): words
+    // 2 hf and 2 hf + 1 make units hf (values 8 hf ..) and 2 + hf (16 + 8 hf ..)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint32_t r[4];
-      nib8_to_h2x4(word_q(i), r);
-      emit(r[0], 2 * i);          // values 4i, 4i+1
-      emit(r[1], 2 * i + 1);      // values 4i+2, 4i+3
-      emit(r[2], 8 + 2 * i);      // values 16+4i, 16+4i+1
-      emit(r[3], 8 + 2 * i + 1);  // values 16+4i+2, 16+4i+3
+    for (int hf = 0; hf < 2; ++hf) {
+      uint32_t h0[4], l0[4], h1[4], l1[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        uint32_t rr[4];
+        nib8_to_h2x4(word_q(2 * hf + j), rr);
+        emit(rr[0], h0[2 * j], l0[2 * j]);          // values 8hf + 4j, +1
+        emit(rr[1], h0[2 * j + 1], l0[2 * j + 1]);  // values 8hf + 4j + 2, +3
+        emit(rr[2], h1[2 * j], l1[2 * j]);          // values 16 + 8hf + 4j, +1
+        emit(rr[3], h1[2 * j + 1], l1[2 * j + 1]);  // values 16 + 8hf + 4j + 2, +3
+      }
+      put(hf, h0, l0);
+      put(2 + hf, h1, l1);
     }
-  }
-}
-
-// Dequantize tile row r of one stage into the Wh / Wl tiles (canonical
-// K-major SW64 layout: 16-byte unit c of row r at sw64_offset(r, 8c)).
-template <int QT, int OFF>
-T0B_DEV void dequant_row(const uint8_t *src, float wscale, uint8_t *whs, uint8_t *wls, int r) {
-  uint32_t hv[16], lv[16];
-  dequant_block<QT, OFF>(src, wscale, hv, lv);
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const uint32_t o = sw64_offset(r, 8 * c);
-    *reinterpret_cast<uint4 *>(whs + o) = make_uint4(hv[4 * c], hv[4 * c + 1], hv[4 * c + 2], hv[4 * c + 3]);
-    *reinterpret_cast<uint4 *>(wls + o) = make_uint4(lv[4 * c], lv[4 * c + 1], lv[4 * c + 2], lv[4 * c + 3]);
   }
 }
 
@@ -201,6 +207,21 @@ T0B_DEV void epi_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }  // th
 #endif
 constexpr int PXS = T0B_PXS, PWS = T0B_PWS, PRS = T0B_PRS;  // ring depths per CTA
 constexpr int STG_N = T0B_STG_N;                             // staging buffers per epilogue warp
+// The activation and dequantized-weight slots of a stage are freed together
+// by one commit per stage (a second commit per stage measured 3.4 % slower),
+// so both rings have the same depth; the QKV epilogue stages two chunks
+// before it stores either.
+static_assert(PXS == PWS, "one stage-empty barrier frees both rings");
+static_assert(STG_N >= 2, "the epilogues use two staging buffers per warp");
+// Register split between the warpgroups (setmaxnreg), out of the 72 per
+// thread the kernel is launched with (896 x 72 = 64,512 of the SM's 65,536):
+// producers / MMA 32, dequant 40, epilogue 96, so that an epilogue warp
+// holds its whole 64-column slice of the accumulator in registers and
+// releases tensor memory before any staging or store.  The host checks the
+// kernel's launch register count before every launch (a split above the
+// launch pool would wait forever).
+constexpr int REG_LAUNCH = 72, REG_WG0 = 32, REG_DEQ = 40, REG_EPI = 96;
+static_assert(REG_WG0 * 128 + REG_DEQ * 256 + REG_EPI * 512 <= REG_LAUNCH * NTHREADS, "register split over the pool");
 constexpr uint32_t PW_TILE = 128 * BK * 2;    // 8 KB: one of hi / lo for this CTA's 128 weight rows
 constexpr uint32_t P_OFF_XH = 0;
 constexpr uint32_t P_OFF_XL = P_OFF_XH + PXS * X_TILE;
@@ -250,12 +271,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
   uint64_t *x_full = bars;               // [PXS] TMA bytes of both CTAs -> MMA (CTA 0's)
-  uint64_t *x_empty = x_full + PXS;      // [PXS] MMA -> TMA (each CTA's)
+  uint64_t *x_empty = x_full + PXS;      // [PXS] MMA -> TMA and dequant: the stage's slots are free (each CTA's)
   uint64_t *raw_full = x_empty + PXS;    // [PRS] TMA -> dequant
   uint64_t *raw_empty = raw_full + PRS;  // [PRS] dequant -> TMA
   uint64_t *w_full = raw_empty + PRS;    // [PWS] dequant warps of both CTAs -> MMA (CTA 0's)
-  uint64_t *w_empty = w_full + PWS;      // [PWS] MMA -> dequant (each CTA's)
-  uint64_t *acc_full = w_empty + PWS;    // MMA -> epilogue (each CTA's)
+  uint64_t *acc_full = w_full + PWS;     // MMA -> epilogue (each CTA's)
   uint64_t *acc_empty = acc_full + 1;    // epilogue warps of both CTAs -> MMA (CTA 0's)
   uint64_t *mma_done = acc_empty + 1;    // every issued MMA has completed (CTA 0)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
@@ -279,7 +299,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int i = 0; i < PWS; ++i) {
       mbar_init(&w_full[i], 8);  // lane 0 of the 4 dequant warps of a stage, in both CTAs
-      mbar_init(&w_empty[i], 1);
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 2 * EPI_WARPS);  // lane 0 of every epilogue warp, both CTAs
@@ -321,6 +340,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   auto lead = [](const uint64_t *b) { return mapa_shared(smem_u32(b), 0); };
 
   if (warp < 4) {
+    setmaxnreg_dec<REG_WG0>();
     if (warp == 0 && lane == 0) {
       // ---------------------------------------------------------- activation producer (both CTAs)
       uint32_t g = 0;
@@ -377,8 +397,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             umma_f16_pair(tmem + BN, sw64_desc(xh + ko), sw64_desc(wl + ko), idesc, acc);
             umma_f16_pair(tmem + BN, sw64_desc(xl + ko), sw64_desc(wh + ko), idesc, 1u);
           }
-          umma_commit_pair_both(&x_empty[xs]);
-          umma_commit_pair_both(&w_empty[ws]);
+          umma_commit_pair_both(&x_empty[xs]);  // frees the stage's activation and weight slots
         }
         if (*abort_flag) break;
         umma_commit_pair_both(acc_full);
@@ -389,6 +408,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else if (warp < 12) {
     // ------------------------------------------------------------ dequant (both CTAs)
+    setmaxnreg_dec<REG_DEQ>();
     const int grp = (warp - 4) >> 2;            // stages g with g % 2 == grp
     const int r = (threadIdx.x - 128) & 127;    // tile row 0..127 of this CTA's weight rows
     uint32_t g = 0;
@@ -400,7 +420,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         bool got = true;
         if (lane == 0)
           got = (g < PWS ||
-                 mbar_wait(&w_empty[ws], ((g / PWS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag)) &&
+                 mbar_wait(&x_empty[ws], ((g / PWS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag)) &&
                 mbar_wait(&raw_full[rs], (g / PRS) & 1, prm.err, T0B_DEVERR_WAIT_W, abort_flag);
         got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
         __syncwarp();
@@ -421,6 +441,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
+    setmaxnreg_inc<REG_EPI>();
     const int q = warp & 3;
     const int quarter = (warp - 12) >> 2;
     const int et = threadIdx.x - 384;
@@ -466,161 +487,107 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         return b;
       };
       if (have) {
+        // every epilogue kind loads its whole slice of the accumulator (64
+        // values per thread: main + correction summed, scaled) and releases
+        // tensor memory before it computes, stages or stores anything
+        float v[4][16];
         if constexpr (swiglu) {
-          // both chunks' SwiGLU values are computed (packed as f16 hi / lo)
-          // before TMEM is released; staging and stores come after
-          uint32_t hl[2][16];
+          // gate columns 32 quarter .. + 31 and the matching up columns
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld_pair16(trow + 32 * quarter + 16 * c, v[c], sc);
+            tmem_ld_pair16(trow + 128 + 32 * quarter + 16 * c, v[2 + c], sc);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tmem_ld_pair16(trow + 64 * quarter + 16 * c, v[c], sc);
+        }
+        release();
+        // one 16-column chunk split in place (word 2i: f16x2 hi of values
+        // 2i, 2i+1; word 2i+1: their lo) -> staged -> two TMA stores
+        auto store_hl = [&](const uint32_t *w, int x) {
+          uint8_t *stg = next_stage_buf();
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const uint32_t o = lane * 32 + ((j ^ ((lane >> 2) & 1)) << 4);
+            *reinterpret_cast<uint4 *>(stg + o) = make_uint4(w[8 * j], w[8 * j + 2], w[8 * j + 4], w[8 * j + 6]);
+            *reinterpret_cast<uint4 *>(stg + 1024 + o) =
+                make_uint4(w[8 * j + 1], w[8 * j + 3], w[8 * j + 5], w[8 * j + 7]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tm_zh, stg, x, row0);
+            tma_store_2d(&tm_zl, stg + 1024, x, row0);
+            bulk_commit();
+          }
+        };
+        if constexpr (swiglu) {
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const int g0 = 32 * quarter + 16 * c;
-            float gv[16], uv[16];
-            tmem_ld_pair16(trow + g0, gv, sc);
-            tmem_ld_pair16(trow + 128 + g0, uv, sc);
-            if (c == 1) release();
+            float *gv = v[c], *uv = v[2 + c];
 #pragma unroll
-            for (int i = 0; i < 16; i += 2) {
-              float z[2];
-#pragma unroll
-              for (int k = 0; k < 2; ++k) {
-                const float gg = gv[i + k] + sb[g0 + i + k];
-                const float uu = uv[i + k] + sb[128 + g0 + i + k];
-                z[k] = gg * __frcp_rn(1.0f + __expf(-gg)) * uu;
-                gv[i + k] = z[k];
-              }
-              __half h0, l0, h1, l1;
-              split_f16(z[0], h0, l0);
-              split_f16(z[1], h1, l1);
-              __half2 hh = __halves2half2(h0, h1), ll = __halves2half2(l0, l1);
-              hl[c][i / 2] = *reinterpret_cast<uint32_t *>(&hh);
-              hl[c][8 + i / 2] = *reinterpret_cast<uint32_t *>(&ll);
+            for (int i = 0; i < 16; ++i) {
+              const float gg = gv[i] + sb[g0 + i];
+              const float uu = uv[i] + sb[128 + g0 + i];
+              gv[i] = gg * __frcp_rn(1.0f + __expf(-gg)) * uu;
             }
             if (e.z32 && live) store_f32x16(e.z32 + (size_t)m * e.F + (size_t)nt * 128 + g0, gv);
-          }
+            uint32_t *w = reinterpret_cast<uint32_t *>(gv);
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const int g0 = 32 * quarter + 16 * c;
-            uint8_t *stg = next_stage_buf();
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const uint32_t o = lane * 32 + ((j ^ ((lane >> 2) & 1)) << 4);
-              *reinterpret_cast<uint4 *>(stg + o) =
-                  make_uint4(hl[c][4 * j], hl[c][4 * j + 1], hl[c][4 * j + 2], hl[c][4 * j + 3]);
-              *reinterpret_cast<uint4 *>(stg + 1024 + o) =
-                  make_uint4(hl[c][8 + 4 * j], hl[c][8 + 4 * j + 1], hl[c][8 + 4 * j + 2], hl[c][8 + 4 * j + 3]);
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_2d(&tm_zh, stg, nt * 128 + g0, row0);
-              tma_store_2d(&tm_zl, stg + 1024, nt * 128 + g0, row0);
-              bulk_commit();
-            }
+            for (int i = 0; i < 8; ++i) split2(gv[2 * i], gv[2 * i + 1], w[2 * i], w[2 * i + 1]);
+            store_hl(w, nt * 128 + g0);
           }
         } else if constexpr (EK == EPI_QKV) {
           // this warp's 64 columns are one head of q, k or v: bias, then for
           // q and k the sum of squares of y (their QK-norm, applied to the
           // attention scores), the norm gain and the RoPE of the token's
-          // patch position; each 16-column chunk is split into f16 hi / lo.
-          // Chunks 0-1 are staged, chunk 2 kept in registers and chunk 3
-          // loaded before TMEM is released; the TMA stores (as for the SwiGLU
-          // output) are all issued after the release.
+          // patch position; each 16-column chunk is split into f16 hi / lo
+          // and written by TMA stores like the SwiGLU output
           const int col0 = nt * BN + 64 * quarter;  // first column of the head
           const int seg = col0 / e.E;               // 0: q, 1: k, 2: v
-          const int pos = live ? m % e.p : 0;  // patch position of this thread's token
+          const int pos = live ? m % e.p : 0;       // patch position of this thread's token
           float ss = 0.0f;
-          uint8_t *stg_a[2];
-          uint32_t hk[16];  // chunk 2, split
-          auto make = [&](int ch, float *v, uint32_t *hl) {
-            const int c0 = 64 * quarter + 16 * ch;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] += sb[c0 + i];
+          for (int ch = 0; ch < 4; ++ch) {
+            const int c0 = 64 * quarter + 16 * ch;
+            float *x = v[ch];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) x[i] += sb[c0 + i];
             if (seg < 2) {
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
-                ss += v[i] * v[i];
-                v[i] *= sb[BN + c0 + i];
+                ss += x[i] * x[i];
+                x[i] *= sb[BN + c0 + i];
               }
-              rope16_t(v, e.rope_t, e.p, pos, ch, seg == 1);
+              rope16_t(x, e.rope_t, e.p, pos, ch, seg == 1);
             }
+            uint32_t *w = reinterpret_cast<uint32_t *>(x);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) split2(v[2 * i], v[2 * i + 1], hl[i], hl[8 + i]);
-          };
-          auto stage = [&](const uint32_t *hl) -> uint8_t * {
-            uint8_t *stg = next_stage_buf();
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const uint32_t o = lane * 32 + ((j ^ ((lane >> 2) & 1)) << 4);
-              *reinterpret_cast<uint4 *>(stg + o) = make_uint4(hl[4 * j], hl[4 * j + 1], hl[4 * j + 2], hl[4 * j + 3]);
-              *reinterpret_cast<uint4 *>(stg + 1024 + o) =
-                  make_uint4(hl[8 + 4 * j], hl[8 + 4 * j + 1], hl[8 + 4 * j + 2], hl[8 + 4 * j + 3]);
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            return stg;
-          };
-          auto store = [&](const uint8_t *stg, int ch) {
-            if (lane == 0) {
-              tma_store_2d(&tm_zh, stg, col0 + 16 * ch, row0);
-              tma_store_2d(&tm_zl, stg + 1024, col0 + 16 * ch, row0);
-              bulk_commit();
-            }
-          };
-#pragma unroll
-          for (int ch = 0; ch < 2; ++ch) {
-            float v[16];
-            uint32_t hl[16];
-            tmem_ld_pair16(trow + 64 * quarter + 16 * ch, v, sc);
-            make(ch, v, hl);
-            stg_a[ch] = stage(hl);
-          }
-          {
-            float v[16];
-            tmem_ld_pair16(trow + 64 * quarter + 32, v, sc);
-            make(2, v, hk);
-          }
-          float v3[16];
-          tmem_ld_pair16(trow + 64 * quarter + 48, v3, sc);
-          release();
-          store(stg_a[0], 0);
-          store(stg_a[1], 1);
-          store(stage(hk), 2);
-          {
-            uint32_t hl[16];
-            make(3, v3, hl);
-            store(stage(hl), 3);
+            for (int i = 0; i < 8; ++i) split2(x[2 * i], x[2 * i + 1], w[2 * i], w[2 * i + 1]);
+            store_hl(w, col0 + 16 * ch);
           }
           if (seg < 2 && live) e.ssq_qk[(size_t)m * 2 * e.H + seg * e.H + ((col0 - seg * e.E) >> 6)] = ss;
-        } else {  // EPI_PLAIN
-          // two chunks at a time: chunks 0-1 are loaded, staged and stored,
-          // then chunks 2-3 are loaded and TMEM is released
-#pragma unroll 1
-          for (int half = 0; half < 2; ++half) {
-            float v[2][16];
+        } else {  // EPI_PLAIN: bias, then f32 chunks stored (or reduce-added) by TMA
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              const int c0 = 64 * quarter + 32 * half + 16 * c;
-              tmem_ld_pair16(trow + c0, v[c], sc);
+          for (int c = 0; c < 4; ++c) {
+            const int c0 = 64 * quarter + 16 * c;
 #pragma unroll
-              for (int i = 0; i < 16; ++i) v[c][i] += sb[c0 + i];
-            }
-            if (half == 1) release();
+            for (int i = 0; i < 16; ++i) v[c][i] += sb[c0 + i];
+            uint8_t *stg = next_stage_buf();
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              const int c0 = 64 * quarter + 32 * half + 16 * c;
-              uint8_t *stg = next_stage_buf();
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                *reinterpret_cast<float4 *>(stg + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
-                    make_float4(v[c][4 * j], v[c][4 * j + 1], v[c][4 * j + 2], v[c][4 * j + 3]);
-              fence_proxy_async_smem();
-              __syncwarp();
-              if (lane == 0) {
-                if (e.reduce_add)
-                  tma_reduce_add_2d(&tm_y, stg, nt * BN + c0, row0);
-                else
-                  tma_store_2d(&tm_y, stg, nt * BN + c0, row0);
-                bulk_commit();
-              }
+            for (int j = 0; j < 4; ++j)
+              *reinterpret_cast<float4 *>(stg + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                  make_float4(v[c][4 * j], v[c][4 * j + 1], v[c][4 * j + 2], v[c][4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (e.reduce_add)
+                tma_reduce_add_2d(&tm_y, stg, nt * BN + c0, row0);
+              else
+                tma_store_2d(&tm_y, stg, nt * BN + c0, row0);
+              bulk_commit();
             }
           }
         }
@@ -706,6 +673,13 @@ cudaError_t launch_tc_k(const CUtensorMap &txh, const CUtensorMap &txl, const CU
                         const CUtensorMap &tzh, const CUtensorMap &tzl, const TcParams &prm, cudaStream_t st) {
   using P = PCfg<QT>;
   auto kfn = gemm_q_tc_pair_kernel<QT, EK>;
+  // the warpgroups' register split (setmaxnreg) is sized for a launch with
+  // REG_LAUNCH registers per thread; any other count is refused, never run
+  static const int launch_regs = [&] {
+    cudaFuncAttributes fa{};
+    return cudaFuncGetAttributes(&fa, (const void *)kfn) == cudaSuccess ? fa.numRegs : -1;
+  }();
+  if (launch_regs != REG_LAUNCH) return cudaErrorInvalidConfiguration;
   cudaError_t e = t0b_smem_limit((const void *)kfn, P::SMEM);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};

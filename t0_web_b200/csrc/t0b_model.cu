@@ -933,6 +933,14 @@ t0b_status run_series(t0b_model *m, const float *ctx_dev, const std::vector<RowS
     return fail(T0B_ERR_UNSUPPORTED, "t0b: 128-dim heads run at most 256 patches per row (context + horizon)");
   size_t max_rows = std::max<size_t>(1, m->max_tokens / (size_t)p);
   if (max_rows_hint) max_rows = std::min(max_rows, max_rows_hint);
+  {
+    // balanced passes: as many as the token budget needs, of near-equal size
+    // (whole series per pass), instead of full passes and a small remainder
+    const size_t total = rows.size();
+    const size_t npass = (total + max_rows - 1) / max_rows;
+    const int maxnv = series_nrows.empty() ? 1 : *std::max_element(series_nrows.begin(), series_nrows.end());
+    if (npass > 1) max_rows = std::min(max_rows, (total + npass - 1) / npass + (size_t)maxnv - 1);
+  }
   size_t s = 0, row = 0;
   while (s < series_nrows.size()) {
     Pass ps;
