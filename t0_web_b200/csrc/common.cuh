@@ -221,6 +221,29 @@ T0B_DEV void tmem_ld16x2(uint32_t ta, uint32_t tb, float *va, float *vb) {
   for (int i = 0; i < 16; ++i) va[i] = __uint_as_float(r[i]), vb[i] = __uint_as_float(q[i]);
 }
 
+// Four 16-column loads of this thread's lane with a single wait.
+T0B_DEV void tmem_ld16x4(uint32_t ta, uint32_t tb, uint32_t tc, uint32_t td, float *va, float *vb, float *vc,
+                         float *vd) {
+  uint32_t r[4][16];
+  const uint32_t addr[4] = {ta, tb, tc, td};
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[k][0]), "=r"(r[k][1]), "=r"(r[k][2]), "=r"(r[k][3]), "=r"(r[k][4]), "=r"(r[k][5]), "=r"(r[k][6]),
+          "=r"(r[k][7]), "=r"(r[k][8]), "=r"(r[k][9]), "=r"(r[k][10]), "=r"(r[k][11]), "=r"(r[k][12]),
+          "=r"(r[k][13]), "=r"(r[k][14]), "=r"(r[k][15])
+        : "r"(addr[k]));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    va[i] = __uint_as_float(r[0][i]);
+    vb[i] = __uint_as_float(r[1][i]);
+    vc[i] = __uint_as_float(r[2][i]);
+    vd[i] = __uint_as_float(r[3][i]);
+  }
+}
+
 // Shared-memory matrix descriptor, K-major, 64-byte swizzle: rows of 64 B
 // (32 f16), 8-row atoms of 512 B stacked at a stride of 512 B.  The atom
 // base must be 512-byte aligned.

@@ -208,11 +208,12 @@ T0B_DEV void epi_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }  // th
 constexpr int PXS = T0B_PXS, PWS = T0B_PWS, PRS = T0B_PRS;  // ring depths per CTA
 constexpr int STG_N = T0B_STG_N;                             // staging buffers per epilogue warp
 // The activation and dequantized-weight slots of a stage are freed together
-// by one commit per stage (a second commit per stage measured 3.4 % slower),
-// so both rings have the same depth; the QKV epilogue stages two chunks
-// before it stores either.
-static_assert(PXS == PWS, "one stage-empty barrier frees both rings");
-static_assert(STG_N >= 2, "the epilogues use two staging buffers per warp");
+// by one commit per stage on the stage-empty barrier of the activation slot
+// (a second commit per stage measured 3.4 % slower): the activation ring is
+// at least as deep as the weight ring, and the weight slot of stage g waits
+// on the barrier of stage g - PWS.
+static_assert(PXS >= PWS, "one stage-empty barrier per activation slot frees both rings");
+static_assert(STG_N >= 1, "at least one staging buffer per epilogue warp");
 // Register split between the warpgroups (setmaxnreg), out of the 72 per
 // thread the kernel is launched with (896 x 72 = 64,512 of the SM's 65,536):
 // producers / MMA 32, dequant 40, epilogue 96, so that an epilogue warp
@@ -245,6 +246,16 @@ T0B_DEV void tmem_ld_pair16(uint32_t taddr, float *v, float scale) {
   tmem_ld16x2(taddr, taddr + BN, v, c);
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = (v[i] + c[i]) * scale;
+}
+// The same for two 16-column chunks at once (one wait for four loads).
+T0B_DEV void tmem_ld_pair16x2(uint32_t ta, uint32_t tb, float *va, float *vb, float scale) {
+  float ca[16], cb[16];
+  tmem_ld16x4(ta, ta + BN, tb, tb + BN, va, ca, vb, cb);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    va[i] = (va[i] + ca[i]) * scale;
+    vb[i] = (vb[i] + cb[i]) * scale;
+  }
 }
 
 template <int N>
@@ -420,7 +431,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         bool got = true;
         if (lane == 0)
           got = (g < PWS ||
-                 mbar_wait(&x_empty[ws], ((g / PWS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag)) &&
+                 mbar_wait(&x_empty[(g - PWS) % PXS], ((g - PWS) / PXS) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY,
+                           abort_flag)) &&
                 mbar_wait(&raw_full[rs], (g / PRS) & 1, prm.err, T0B_DEVERR_WAIT_W, abort_flag);
         got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
         __syncwarp();
@@ -491,16 +503,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // values per thread: main + correction summed, scaled) and releases
         // tensor memory before it computes, stages or stores anything
         float v[4][16];
+        // three load round trips: two chunks, then one, then one
         if constexpr (swiglu) {
           // gate columns 32 quarter .. + 31 and the matching up columns
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            tmem_ld_pair16(trow + 32 * quarter + 16 * c, v[c], sc);
-            tmem_ld_pair16(trow + 128 + 32 * quarter + 16 * c, v[2 + c], sc);
-          }
+          tmem_ld_pair16x2(trow + 32 * quarter, trow + 128 + 32 * quarter, v[0], v[2], sc);
+          tmem_ld_pair16(trow + 32 * quarter + 16, v[1], sc);
+          tmem_ld_pair16(trow + 128 + 32 * quarter + 16, v[3], sc);
         } else {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) tmem_ld_pair16(trow + 64 * quarter + 16 * c, v[c], sc);
+          tmem_ld_pair16x2(trow + 64 * quarter, trow + 64 * quarter + 16, v[0], v[1], sc);
+          tmem_ld_pair16(trow + 64 * quarter + 32, v[2], sc);
+          tmem_ld_pair16(trow + 64 * quarter + 48, v[3], sc);
         }
         release();
         // one 16-column chunk split in place (word 2i: f16x2 hi of values
