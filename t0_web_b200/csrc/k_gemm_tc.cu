@@ -263,7 +263,7 @@ T0B_DEV void bulk_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
-template <int QT, int EK>  // EK: the epilogue kind (EPI_PLAIN, EPI_SWIGLU or EPI_QKV)
+template <int QT, int EK>  // EK: the epilogue kind (EPI_PLAIN, EPI_SWIGLU, EPI_QKV or EPI_RESID)
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_q_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
                           const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_y,
@@ -322,12 +322,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     prefetch_tmap(&tm_xh);
     prefetch_tmap(&tm_xl);
     prefetch_tmap(&tm_w);
-    if (swiglu) {
-      prefetch_tmap(&tm_zh);
-      prefetch_tmap(&tm_zl);
-    } else {
-      prefetch_tmap(&tm_y);
-    }
+    prefetch_tmap(&tm_y);  // the unused kinds' maps repeat a valid one
+    prefetch_tmap(&tm_zh);
+    prefetch_tmap(&tm_zl);
   }
   if (warp == 1) {  // the same warp in both CTAs allocates the pair's columns
     tmem_alloc_pair(tmem_slot, 512);
@@ -470,6 +467,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int c = et;
         const int f = swiglu ? (c < 128 ? nt * 128 + c : e.F + nt * 128 + (c - 128)) : nt * BN + c;
         sb[c] = e.bias ? e.bias[f] : 0.0f;
+        if constexpr (EK == EPI_RESID) sb[BN + c] = e.gnext[f];  // the next RMSNorm's gains
         if constexpr (EK == EPI_QKV) {  // QK-norm gains of the tile's columns (1 for v)
           const int seg = f / e.E;
           sb[BN + c] = seg == 0 ? e.qn[c & 63] : (seg == 1 ? e.kn[c & 63] : 1.0f);
@@ -581,6 +579,49 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             store_hl(w, col0 + 16 * ch);
           }
           if (seg < 2 && live) e.ssq_qk[(size_t)m * 2 * e.H + seg * e.H + ((col0 - seg * e.E) >> 6)] = ss;
+        } else if constexpr (EK == EPI_RESID) {
+          // residual branch output (wO, mlp.2): x[m, n] += y + bias; the new
+          // x is stored back (each element belongs to one tile), x * gnext is
+          // split into the f16 planes of the next RMSNorm-fused GEMM, and the
+          // sum of x^2 over this warp's 64 columns goes to its slot of the
+          // row's partial sums (the next GEMM's row scale adds the N / 64 slots)
+          const int col0 = nt * BN + 64 * quarter;
+          float ss = 0.0f;
+          const float4 *xo = reinterpret_cast<const float4 *>(e.x + (size_t)(live ? m : 0) * e.N + col0);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int c0 = 64 * quarter + 16 * c;
+            float *xv = v[c];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {  // x + (branch + bias), the order of the reduce-add path
+              const float4 o = live ? xo[4 * c + i] : make_float4(0.f, 0.f, 0.f, 0.f);
+              xv[4 * i] = o.x + (xv[4 * i] + sb[c0 + 4 * i]);
+              xv[4 * i + 1] = o.y + (xv[4 * i + 1] + sb[c0 + 4 * i + 1]);
+              xv[4 * i + 2] = o.z + (xv[4 * i + 2] + sb[c0 + 4 * i + 2]);
+              xv[4 * i + 3] = o.w + (xv[4 * i + 3] + sb[c0 + 4 * i + 3]);
+            }
+            uint8_t *stg = next_stage_buf();
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              *reinterpret_cast<float4 *>(stg + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                  make_float4(xv[4 * j], xv[4 * j + 1], xv[4 * j + 2], xv[4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tm_y, stg, col0 + 16 * c, row0);
+              bulk_commit();
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              ss += xv[i] * xv[i];
+              xv[i] *= sb[BN + c0 + i];
+            }
+            uint32_t *w = reinterpret_cast<uint32_t *>(xv);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) split2(xv[2 * i], xv[2 * i + 1], w[2 * i], w[2 * i + 1]);
+            store_hl(w, col0 + 16 * c);
+          }
+          if (live) e.ssq_out[(size_t)m * e.ssq_out_nt + (col0 >> 6)] = ss;
         } else {  // EPI_PLAIN: bias, then f32 chunks stored (or reduce-added) by TMA
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -724,7 +765,12 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
       !make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, rb, (uint64_t)wrows, rb, TQ<QT>::rawb, 128,
                     CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
-  if (epi.kind != EPI_PLAIN && epi.kind != EPI_SWIGLU && epi.kind != EPI_QKV) return cudaErrorInvalidValue;
+  if (epi.kind != EPI_PLAIN && epi.kind != EPI_SWIGLU && epi.kind != EPI_QKV && epi.kind != EPI_RESID)
+    return cudaErrorInvalidValue;
+  if (epi.kind == EPI_RESID &&
+      (!epi.x || !epi.gnext || !epi.ssq_out || epi.ssq_out_nt != epi.N / 64 || epi.F != epi.N || epi.zh != epi.xh ||
+       epi.zl != epi.xl || epi.y != epi.x || epi.ldy != epi.N))
+    return cudaErrorInvalidValue;
   if (epi.kind == EPI_QKV &&
       (epi.F != 3 * epi.E || epi.N != epi.F || epi.E % 64 || epi.E / 64 != epi.H || !epi.qn || !epi.kn ||
        !epi.rope_t || !epi.ssq_qk || epi.p < 1))
@@ -732,7 +778,15 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
   // output maps for the epilogue's TMA stores (the unused kind's maps repeat
   // a valid one; the kernel never touches them)
   CUtensorMap ty, tzh, tzl;
-  if (epi.kind == EPI_PLAIN) {
+  if (epi.kind == EPI_RESID) {  // x (f32) and the split planes of x * gnext
+    if (!make_tmap_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, epi.y, (uint64_t)epi.N, (uint64_t)M,
+                      (uint64_t)epi.ldy * 4, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_tmap_2d(&tzh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, epi.zh, (uint64_t)epi.F, (uint64_t)M,
+                      (uint64_t)epi.F * 2, 16, 32, CU_TENSOR_MAP_SWIZZLE_32B) ||
+        !make_tmap_2d(&tzl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, epi.zl, (uint64_t)epi.F, (uint64_t)M,
+                      (uint64_t)epi.F * 2, 16, 32, CU_TENSOR_MAP_SWIZZLE_32B))
+      return cudaErrorInvalidValue;
+  } else if (epi.kind == EPI_PLAIN) {
     if (!epi.y || epi.ldy < epi.N || epi.ldy % 4 ||
         !make_tmap_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, epi.y, (uint64_t)epi.N, (uint64_t)M,
                       (uint64_t)epi.ldy * 4, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B))
@@ -760,6 +814,7 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
   prm.n_tiles = prm.n_tiles_n * ((M + 2 * BM - 1) / (2 * BM));
   if (epi.kind == EPI_SWIGLU) return launch_tc_k<QT, EPI_SWIGLU>(txh, txl, tw, ty, tzh, tzl, prm, st);
   if (epi.kind == EPI_QKV) return launch_tc_k<QT, EPI_QKV>(txh, txl, tw, ty, tzh, tzl, prm, st);
+  if (epi.kind == EPI_RESID) return launch_tc_k<QT, EPI_RESID>(txh, txl, tw, ty, tzh, tzl, prm, st);
   return launch_tc_k<QT, EPI_PLAIN>(txh, txl, tw, ty, tzh, tzl, prm, st);
 }
 

@@ -555,10 +555,12 @@ cudaError_t qgemm(t0b_model *m, const __half *ah, const __half *al, int M, int K
 }
 
 // Residual branch output GEMM (wO or mlp.2): x += A . W^T + bias, then the
-// split of x * gnext and its sums of squares for the next RMSNorm-fused GEMM.
-// The tensor-core path adds into x with TMA reduce-adds from its epilogue and
-// a row kernel does the split; the small-M path fuses everything into its
-// epilogue.  Sets *ssq_nt to the number of partial sums of squares per row.
+// split of x * gnext and its sums of squares for the next RMSNorm-fused GEMM,
+// all in the GEMM's epilogue (EPI_RESID) on both paths: the tensor-core
+// epilogue reads its x tile, stores the new x and the split planes by TMA and
+// writes one partial sum of squares per 64 columns (N / 64 per row); the
+// small-M epilogue one per 32 columns.  Sets *ssq_nt to the number of partial
+// sums per row.
 cudaError_t resid_gemm(t0b_model *m, const __half *ah, const __half *al, int M, int K, const uint8_t *W,
                        int wshift, const float *bias, float *x, const float *gnext, int *ssq_nt) {
   const int E = m->E;
@@ -566,27 +568,22 @@ cudaError_t resid_gemm(t0b_model *m, const __half *ah, const __half *al, int M, 
   r.M = M;
   r.N = E;
   r.bias = bias;
-  if (use_tc(m, M, K, r)) {
-    // the epilogue adds the branch output into x with TMA reduce-adds (in
-    // L2), then a row kernel makes x * gnext's split and sum of squares
-    r.kind = EPI_PLAIN;
-    r.y = x;
-    r.ldy = E;
-    r.reduce_add = 1;
-    cudaError_t e = qgemm(m, ah, al, M, K, W, E, wshift, r);
-    if (e != cudaSuccess) return e;
-    *ssq_nt = 1;
-    return launch(m, KC_OTHER, 0.0, (double)M * E * 8.0, [&] {
-      return t0b_launch_rownorm_split(x, gnext, m->xh.as<__half>(), m->xl.as<__half>(), m->ssq.as<float>(), M, E,
-                                      m->stream);
-    });
-  }
   r.kind = EPI_RESID;
   r.x = x;
   r.gnext = gnext;
   r.xh = m->xh.as<__half>();
   r.xl = m->xl.as<__half>();
   r.ssq_out = m->ssq.as<float>();
+  if (use_tc(m, M, K, r)) {
+    r.y = x;
+    r.ldy = E;
+    r.F = E;
+    r.zh = r.xh;
+    r.zl = r.xl;
+    r.ssq_out_nt = E / 64;
+    *ssq_nt = E / 64;
+    return qgemm(m, ah, al, M, K, W, E, wshift, r);
+  }
   *ssq_nt = E / 32;
   return qgemm(m, ah, al, M, K, W, E, wshift, r);
 }
