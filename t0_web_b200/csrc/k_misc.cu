@@ -1525,7 +1525,7 @@ __global__ void __launch_bounds__(256) attn_group_kernel(AttnArgs a) {
 // (f32-class), the softmax runs on the score fragments.  Semantics as
 // attn_group_kernel (mask.rs:69-82).
 template <int NT>  // key / query tiles of 8 rows: 1 (up to 8 variates) or 2 (up to 16)
-__global__ void __launch_bounds__(256, NT == 1 ? 3 : 2) attn_group_mma_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(256, NT == 1 ? 4 : 2) attn_group_mma_kernel(AttnArgs a) {
   pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
   __shared__ __align__(16) __half vs[8][2][16 * 72];  // per warp: v rows as f16 hi / lo planes
   const int s = blockIdx.x, patch = blockIdx.y;
