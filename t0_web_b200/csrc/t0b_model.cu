@@ -118,6 +118,10 @@ struct t0b_model {
   DBuf meta;  // row/series metadata
   HBuf hmeta;
   DBuf ctx_stage, out_stage;
+  // host-buffer forecasts: a copy stream and events that overlap each pass's
+  // context upload and the previous pass's quantile download with compute
+  cudaStream_t io_stream = nullptr;
+  cudaEvent_t io_in[2] = {nullptr, nullptr}, io_done[2] = {nullptr, nullptr};
   // measurement
   uint64_t launches = 0;
   bool prof = false;
@@ -153,6 +157,11 @@ struct t0b_model {
     for (auto &kv : rope) cudaFree(kv.second);
     for (void *p : allocs) cudaFree(p);
     if (own_stream && stream) cudaStreamDestroy(stream);
+    if (io_stream) cudaStreamDestroy(io_stream);
+    for (int i = 0; i < 2; ++i) {
+      if (io_in[i]) cudaEventDestroy(io_in[i]);
+      if (io_done[i]) cudaEventDestroy(io_done[i]);
+    }
     if (d_err) cudaFree(d_err);
   }
 };
@@ -921,9 +930,16 @@ struct RowSpec {
   int len;
 };
 
+// Host buffers behind a device forecast: the contexts at the same offsets as
+// ctx_dev, the quantiles at the same offsets as out_dev.
+struct HostIO {
+  const float *ctx;
+  float *out;
+};
+
 t0b_status run_series(t0b_model *m, const float *ctx_dev, const std::vector<RowSpec> &rows,
                       const std::vector<int> &series_nrows, int ctx_w, int horizon, float *out_dev,
-                      size_t max_rows_hint) {
+                      size_t max_rows_hint, const HostIO *hio = nullptr) {
   const int hpad = (horizon + 31) / 32 * 32;
   const int p = (ctx_w + hpad) / 32, hp = hpad / 32;
   if (m->E / m->H == 128 && p > 256)
@@ -939,6 +955,8 @@ t0b_status run_series(t0b_model *m, const float *ctx_dev, const std::vector<RowS
     if (npass > 1) max_rows = std::min(max_rows, (total + npass - 1) / npass + (size_t)maxnv - 1);
   }
   size_t s = 0, row = 0;
+  std::vector<Pass> passes;
+  std::vector<std::pair<size_t, size_t>> pass_rows;  // [row0, row1) of each pass
   while (s < series_nrows.size()) {
     Pass ps;
     ps.p = p;
@@ -963,10 +981,50 @@ t0b_status run_series(t0b_model *m, const float *ctx_dev, const std::vector<RowS
       ++s;
     }
     ps.out = out_dev + row0 * (size_t)horizon * m->nq;
-    t0b_status st = run_pass(m, ps);
-    if (st != T0B_OK) return st;
+    pass_rows.push_back({row0, row});
+    passes.push_back(std::move(ps));
   }
-  return T0B_OK;
+  if (!hio) {
+    for (const Pass &ps : passes) {
+      t0b_status st = run_pass(m, ps);
+      if (st != T0B_OK) return st;
+    }
+    return T0B_OK;
+  }
+  // host buffers: pass i's contexts go up on the copy stream while pass i-1
+  // computes, and pass i-1's quantiles come down while pass i computes
+  if (!m->io_stream) CUDA_TRY(cudaStreamCreateWithFlags(&m->io_stream, cudaStreamNonBlocking));
+  for (int i = 0; i < 2; ++i) {
+    if (!m->io_in[i]) CUDA_TRY(cudaEventCreateWithFlags(&m->io_in[i], cudaEventDisableTiming));
+    if (!m->io_done[i]) CUDA_TRY(cudaEventCreateWithFlags(&m->io_done[i], cudaEventDisableTiming));
+  }
+  const size_t per_row_out = (size_t)horizon * m->nq;
+  auto h2d = [&](size_t i) -> t0b_status {
+    const RowSpec &a = rows[pass_rows[i].first], &b = rows[pass_rows[i].second - 1];
+    const size_t n = (size_t)(b.off + b.len - a.off);
+    CUDA_TRY(cudaMemcpyAsync(const_cast<float *>(ctx_dev) + a.off, hio->ctx + a.off, n * 4, cudaMemcpyHostToDevice,
+                             m->io_stream));
+    CUDA_TRY(cudaEventRecord(m->io_in[i & 1], m->io_stream));
+    return T0B_OK;
+  };
+  auto d2h = [&](size_t i) -> t0b_status {
+    const size_t r0 = pass_rows[i].first, r1 = pass_rows[i].second;
+    CUDA_TRY(cudaStreamWaitEvent(m->io_stream, m->io_done[i & 1], 0));
+    CUDA_TRY(cudaMemcpyAsync(hio->out + r0 * per_row_out, out_dev + r0 * per_row_out, (r1 - r0) * per_row_out * 4,
+                             cudaMemcpyDeviceToHost, m->io_stream));
+    return T0B_OK;
+  };
+  t0b_status st = passes.empty() ? T0B_OK : h2d(0);
+  for (size_t i = 0; i < passes.size() && st == T0B_OK; ++i) {
+    CUDA_TRY(cudaStreamWaitEvent(m->stream, m->io_in[i & 1], 0));
+    if ((st = run_pass(m, passes[i])) != T0B_OK) break;
+    CUDA_TRY(cudaEventRecord(m->io_done[i & 1], m->stream));
+    if (i + 1 < passes.size() && (st = h2d(i + 1)) != T0B_OK) break;
+    if (i >= 1) st = d2h(i - 1);
+  }
+  if (st == T0B_OK && !passes.empty()) st = d2h(passes.size() - 1);
+  CUDA_TRY(cudaStreamSynchronize(m->io_stream));
+  return st;
 }
 
 struct Staged {
@@ -1118,12 +1176,26 @@ extern "C" t0b_status t0b_forecast_multiseries(t0b_model *m, const float *ctx, c
   size_t rows = 0;
   for (size_t i = 0; i < n_series; ++i) rows += (size_t)std::max(n_variates[i], 0);
   CUDA_TRY(cudaSetDevice(m->eng->device));
-  Staged sg;
-  t0b_status s = stage_io(m, ctx, rows * t_ctx, rows * horizon * m->nq, &sg);
+  t0b_status s = check_horizon(horizon);
   if (s != T0B_OK) return s;
-  s = t0b_forecast_multiseries_device(m, sg.ctx, n_variates, n_series, t_ctx, horizon, sg.out);
+  if (t_ctx == 0) return fail(T0B_ERR_INVALID, "t0b: context length must be >= 1");
+  CUDA_TRY(m->ctx_stage.reserve(std::max<size_t>(rows * t_ctx, 1) * 4));
+  CUDA_TRY(m->out_stage.reserve(std::max<size_t>(rows * horizon * m->nq, 1) * 4));
+  const int pad_left = (int)((32 - t_ctx % 32) % 32);  // data.rs:112
+  std::vector<RowSpec> rs;
+  std::vector<int> nr;
+  int64_t off = 0;
+  for (size_t i = 0; i < n_series; ++i) {
+    if (n_variates[i] < 1) return fail(T0B_ERR_INVALID, "t0b: every series needs >= 1 variate");
+    nr.push_back(n_variates[i]);
+    for (int v = 0; v < n_variates[i]; ++v, off += (int64_t)t_ctx) rs.push_back({off, (int)t_ctx});
+  }
+  // contexts up and quantiles down per pass, overlapped with the other passes
+  const HostIO hio{ctx, out};
+  s = run_series(m, m->ctx_stage.as<float>(), rs, nr, (int)t_ctx + pad_left, (int)horizon, m->out_stage.as<float>(), 0,
+                 &hio);
   if (s != T0B_OK) return s;
-  return finish_io(m, sg, out, rows * horizon * m->nq);
+  return sync_model(m);
 }
 
 extern "C" t0b_status t0b_forecast(t0b_model *m, const float *ctx, size_t v, size_t t_ctx, size_t horizon,
@@ -1140,14 +1212,17 @@ extern "C" t0b_status t0b_forecast_batch(t0b_model *m, const float *ctx, size_t 
   if (s != T0B_OK) return s;
   if (t_ctx == 0) return fail(T0B_ERR_INVALID, "t0b: context length must be >= 1");
   CUDA_TRY(cudaSetDevice(m->eng->device));
-  Staged sg;
-  if ((s = stage_io(m, ctx, n * t_ctx, n * horizon * m->nq, &sg)) != T0B_OK) return s;
+  CUDA_TRY(m->ctx_stage.reserve(std::max<size_t>(n * t_ctx, 1) * 4));
+  CUDA_TRY(m->out_stage.reserve(std::max<size_t>(n * horizon * m->nq, 1) * 4));
   const int pad_left = (int)((32 - t_ctx % 32) % 32);
   std::vector<RowSpec> rows(n);
   std::vector<int> nr(n, 1);  // data.rs:96-105: a distinct group per signal
   for (size_t i = 0; i < n; ++i) rows[i] = {(int64_t)(i * t_ctx), (int)t_ctx};
-  if ((s = run_series(m, sg.ctx, rows, nr, (int)t_ctx + pad_left, (int)horizon, sg.out, chunk)) != T0B_OK) return s;
-  return finish_io(m, sg, out, n * horizon * m->nq);
+  const HostIO hio{ctx, out};
+  if ((s = run_series(m, m->ctx_stage.as<float>(), rows, nr, (int)t_ctx + pad_left, (int)horizon,
+                      m->out_stage.as<float>(), chunk, &hio)) != T0B_OK)
+    return s;
+  return sync_model(m);
 }
 
 extern "C" t0b_status t0b_forecast_batch_rows(t0b_model *m, const float *ctx, const size_t *lengths, size_t n,
