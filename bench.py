@@ -16,8 +16,8 @@ forecast of the whole batch.
 The default run also checks the timed step's output against the CPU oracle
 on a sample of series (`parity`; the run exits non-zero when it is off),
 times the oracle on the host cores (`cpu_baseline`, all threads and one
-thread) and, on one GPU, adds the single-forecast latency and the two
-standalone small-M GEMM configurations as `secondary` (each with its own
+thread) and, on one GPU, adds the single-forecast latency and every size
+of the two standalone GEMM configurations as `secondary` (each with its own
 clock record).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--quant q8_0|q4_0]
@@ -66,7 +66,7 @@ def parse():
                     help="(default) split one fixed set of series across the ranks, NCCL all-gather of the quantiles")
     ap.add_argument("--weak", action="store_true", help="every rank forecasts its own series, no collective")
     ap.add_argument("--no-secondary", action="store_true",
-                    help="skip the single-forecast latency and standalone small-M GEMM lines of the default run")
+                    help="skip the single-forecast latency and standalone GEMM lines of the default run")
     ap.add_argument("--parity-series", type=int, default=0,
                     help="series checked against the oracle (0 = the CPU-baseline sample, at least 8)")
     ap.add_argument("--workload", default="forecast", choices=["forecast", "single", "gemm", "swiglu"],
@@ -315,8 +315,9 @@ def run_ours(args):
     secondary = None
     if rank == 0 and world == 1 and not args.no_secondary and args.model == "alpha":
         secondary = {"single_forecast": run_single(args, engine=engine, model=model, emit=False)}
-        for wl in ("gemm", "swiglu"):
-            secondary[f"{wl}_M16"] = run_standalone(args, workload=wl, cases=[16], engine=engine, emit=False)[0]
+        for wl in ("gemm", "swiglu"):  # every size of the standalone configurations
+            for line in run_standalone(args, workload=wl, engine=engine, emit=False):
+                secondary[f"{wl}_M{line['config_M']}"] = line
 
     for _ in range(args.warmup):
         step()
@@ -659,7 +660,7 @@ def run_standalone(args, workload=None, cases=None, engine=None, emit=True):
                  "peak_kind": f"{kind} HBM copy"} if small else
                 {"bound": "tensor", "achieved": tf, "peak": peak_tf, "unit": "TFLOP/s", "frac": tf / peak_tf,
                  "peak_kind": f"{kind} bf16 (sustained)"})
-        line = {"metric": f"{name}, M={M}", "value": tf, "unit": "TFLOP/s (useful)", "ms_per_call": ms,
+        line = {"metric": f"{name}, M={M}", "config_M": M, "value": tf, "unit": "TFLOP/s (useful)", "ms_per_call": ms,
                 "achieved_GBps": gbs, "algorithmic_bytes": nbytes, "higher_is_better": True, "n_gpus": 1,
                 "dtype": "f32-class (split-f16)", "data": "synthetic N(0,0.02) weights, N(0,1) activations",
                 "roofline": roof, "path": "tcgen05" if not small else "mma.sync small-M", "clocks": clocks,

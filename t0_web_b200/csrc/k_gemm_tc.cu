@@ -81,6 +81,10 @@ struct TcParams {
   int M, N, K;
   int swiglu_F;  // > 0: a tile is 128 gate rows + the matching 128 up rows
   int n_tiles_n, n_tiles;
+  // split-K (PLAIN only): each (m, n) tile is k_split work items over
+  // consecutive K ranges whose partial tiles the epilogue reduce-adds into a
+  // zeroed y; only the first split adds the bias
+  int k_split;
   // power-of-two weight prescale: W is split as (2^s d q) = Wh + Wl so that Wl
   // stays a normal f16; the accumulator is multiplied by 2^-s (both exact)
   float wscale, acc_scale;
@@ -296,6 +300,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int M = prm.M, K = prm.K;
   const int S = K / BK;
+  const int SK = S / prm.k_split;  // K stages per work item
   constexpr bool swiglu = EK == EPI_SWIGLU;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
 
@@ -336,10 +341,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // work item -> its first K stage (items of one tile are adjacent K splits)
+  auto tile_s0 = [&](int tile) { return ((tile / prm.n_tiles_n) % prm.k_split) * SK; };
   // pair tile -> (this CTA's first token, this CTA's first weight row, n tile)
   auto tile_rows = [&](int tile, int &m0, int &wrow, int &nt) {
     nt = tile % prm.n_tiles_n;
-    m0 = (tile / prm.n_tiles_n) * (2 * BM) + BM * (int)rank;
+    m0 = (tile / prm.n_tiles_n / prm.k_split) * (2 * BM) + BM * (int)rank;
     if (swiglu)
       wrow = (rank == 0 ? 0 : prm.swiglu_F) + nt * 128;
     else
@@ -355,7 +362,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int tile = pair; tile < prm.n_tiles && !*abort_flag; tile += npairs) {
         int m0, wrow, nt;
         tile_rows(tile, m0, wrow, nt);
-        for (int s = 0; s < S && !*abort_flag; ++s, ++g) {
+        const int s0 = tile_s0(tile);
+        for (int s = s0; s < s0 + SK && !*abort_flag; ++s, ++g) {
           const uint32_t xs = g % PXS;
           if (g >= PXS && !mbar_wait(&x_empty[xs], ((g / PXS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag))
             break;
@@ -373,7 +381,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int tile = pair; tile < prm.n_tiles && !*abort_flag; tile += npairs) {
         int m0, wrow, nt;
         tile_rows(tile, m0, wrow, nt);
-        for (int s = 0; s < S && !*abort_flag; ++s, ++g) {
+        const int s0 = tile_s0(tile);
+        for (int s = s0; s < s0 + SK && !*abort_flag; ++s, ++g) {
           const uint32_t rs = g % PRS;
           if (g >= PRS && !mbar_wait(&raw_empty[rs], ((g / PRS) - 1) & 1, prm.err, T0B_DEVERR_WAIT_EMPTY, abort_flag))
             break;
@@ -389,7 +398,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int tile = pair; tile < prm.n_tiles && !*abort_flag; tile += npairs, ++it) {
         if (it >= 1 && !mbar_wait(acc_empty, (it - 1) & 1, prm.err, T0B_DEVERR_WAIT_ACC, abort_flag)) break;
         tc_fence_after();
-        for (int s = 0; s < S; ++s, ++g) {
+        const int s0 = tile_s0(tile);
+        for (int s = s0; s < s0 + SK; ++s, ++g) {
           const uint32_t xs = g % PXS, ws = g % PWS;
           if (!mbar_wait(&x_full[xs], (g / PXS) & 1, prm.err, T0B_DEVERR_WAIT_X, abort_flag) ||
               !mbar_wait(&w_full[ws], (g / PWS) & 1, prm.err, T0B_DEVERR_WAIT_DEQ, abort_flag))
@@ -400,7 +410,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint32_t ko = kk * 32;  // 16 f16 along K inside the 64-byte swizzled row
-            const uint32_t acc = (s > 0 || kk > 0) ? 1u : 0u;
+            const uint32_t acc = (s > s0 || kk > 0) ? 1u : 0u;
             umma_f16_pair(tmem, sw64_desc(xh + ko), sw64_desc(wh + ko), idesc, acc);
             umma_f16_pair(tmem + BN, sw64_desc(xh + ko), sw64_desc(wl + ko), idesc, acc);
             umma_f16_pair(tmem + BN, sw64_desc(xl + ko), sw64_desc(wh + ko), idesc, 1u);
@@ -422,7 +432,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint32_t g = 0;
     bool ok = true;
     for (int tile = pair; tile < prm.n_tiles && ok && !*abort_flag; tile += npairs) {
-      for (int s = 0; s < S; ++s, ++g) {
+      const int s0 = tile_s0(tile);
+      for (int s = s0; s < s0 + SK; ++s, ++g) {
         if ((int)(g & 1) != grp) continue;
         const uint32_t ws = g % PWS, rs = g % PRS;
         bool got = true;
@@ -466,7 +477,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (et < BN) {
         const int c = et;
         const int f = swiglu ? (c < 128 ? nt * 128 + c : e.F + nt * 128 + (c - 128)) : nt * BN + c;
-        sb[c] = e.bias ? e.bias[f] : 0.0f;
+        sb[c] = (e.bias && tile_s0(tile) == 0) ? e.bias[f] : 0.0f;
         if constexpr (EK == EPI_RESID) sb[BN + c] = e.gnext[f];  // the next RMSNorm's gains
         if constexpr (EK == EPI_QKV) {  // QK-norm gains of the tile's columns (1 for v)
           const int seg = f / e.E;
@@ -807,11 +818,29 @@ cudaError_t launch_tc_t(const __half *ah, const __half *al, int M, int K, const 
   prm.K = K;
   prm.swiglu_F = epi.kind == EPI_SWIGLU ? epi.F : 0;
   prm.n_tiles_n = epi.kind == EPI_SWIGLU ? epi.F / 128 : epi.N / BN;
+  prm.k_split = 1;
   prm.wscale = ldexpf(1.0f, wshift);
   prm.acc_scale = ldexpf(1.0f, -wshift);
   prm.epi = epi;
   prm.err = err;
   prm.n_tiles = prm.n_tiles_n * ((M + 2 * BM - 1) / (2 * BM));
+  {
+    // few tiles for the SMs (the standalone shapes at a few hundred tokens):
+    // split K in two, the partial tiles reduce-added into a zeroed y.  Two
+    // addends into zero give the same sum in either order, so the result
+    // stays deterministic.
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int pairs_est = sm_count(dev) / 2, S = K / BK;
+    if (epi.kind == EPI_PLAIN && !epi.reduce_add && 2 * prm.n_tiles <= pairs_est && S % 2 == 0 && S / 2 >= 8) {
+      cudaError_t ze = epi.ldy == epi.N ? cudaMemsetAsync(epi.y, 0, (size_t)M * epi.N * 4, st)
+                                        : cudaMemset2DAsync(epi.y, (size_t)epi.ldy * 4, 0, (size_t)epi.N * 4, M, st);
+      if (ze != cudaSuccess) return ze;
+      prm.k_split = 2;
+      prm.n_tiles *= 2;
+      prm.epi.reduce_add = 1;
+    }
+  }
   if (epi.kind == EPI_SWIGLU) return launch_tc_k<QT, EPI_SWIGLU>(txh, txl, tw, ty, tzh, tzl, prm, st);
   if (epi.kind == EPI_QKV) return launch_tc_k<QT, EPI_QKV>(txh, txl, tw, ty, tzh, tzl, prm, st);
   if (epi.kind == EPI_RESID) return launch_tc_k<QT, EPI_RESID>(txh, txl, tw, ty, tzh, tzl, prm, st);
