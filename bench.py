@@ -421,7 +421,10 @@ def run_ours(args):
                     "share_of_step": g["total_ms"] / max(total_ms, 1e-9),
                     "issued_frac": 3.0 * achieved / peak_tf,
                     "issued_note": "f32-class accuracy takes 3 f16 MMAs per useful multiply-add (Ah.Wh + Ah.Wl + "
-                                   "Al.Wh); issued_frac counts them, frac counts useful flops only"}
+                                   "Al.Wh); issued_frac counts them, frac counts useful flops only",
+                    "epilogue_note": "the launches also do the residual add + split of x*g + row sums of squares "
+                                     "(wO, mlp.2), QK-norm gains + RoPE + split planes (TIME-layer wQKV) and SwiGLU "
+                                     "(mlp.0); only the GEMM flops are counted"}
     breakdown = {k: {"launches": v["launches"], "ms": round(v["total_ms"], 3)} for k, v in prof.items()
                  if v["launches"]}
 
