@@ -73,7 +73,7 @@ t0b_status t0b_model_info_get(const t0b_model *m, t0b_model_info *out);
 t0b_status t0b_model_set_stream(t0b_model *m, void *stream);
 void *t0b_model_stream(const t0b_model *m);
 /* Upper bound on tokens (rows x patches) per device pass; larger requests are
- * split into passes.  Default 262144. */
+ * split into passes.  Default 393216 (about 8 GB of workspace for t0-alpha). */
 t0b_status t0b_model_set_max_tokens(t0b_model *m, size_t max_tokens);
 /* Replay each forecast pass from a CUDA graph (default on).  A pass's launch
  * sequence is captured the first time its shape, input/output pointers and

@@ -108,7 +108,7 @@ struct t0b_model {
   cudaStream_t stream = nullptr;
   bool own_stream = false;
   int *d_err = nullptr;
-  size_t max_tokens = 262144;
+  size_t max_tokens = 393216;
   int tc_min_tokens = 128;
   std::map<int, float *> rope;  // p -> [4][p][hd] device tables: cos, sin, scale, 1/scale
   // workspace

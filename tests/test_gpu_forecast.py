@@ -109,7 +109,7 @@ def test_chunking_is_invisible(engine, gpu_model):
     try:
         many = t0_fast.forecast_multiseries(engine, m, ctx, nv, 512, 96)
     finally:
-        m.set_max_tokens(262144)
+        m.set_max_tokens(393216)
     assert max_abs(one, many) <= TOL
 
 
