@@ -774,6 +774,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   // bytes) plus the QK-norm sums of squares, and the time attention reads the
   // planes by TMA without a conversion pass
   const bool qkv_planes = E / m->H == 64 && p <= 256 && use_tc(m, M);
+  const bool univariate = ns == R;  // one variate row per series
   aa.qkv_h = m->qkv.as<__half>();
   aa.qkv_l = aa.qkv_h + T * 3 * E;
   aa.ssq_qk = m->ssqk.as<float>();
@@ -805,6 +806,25 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
       e.E = E;
       e.H = m->H;
     }
+    if (w.group && univariate) {
+      // every series has one variate: the group attention of a token is a
+      // softmax over its own key alone, exactly 1, so its output is exactly
+      // v (mask.rs:69-82 makes a lone whole-padding query average the same
+      // single v).  Only the v third of wQKV is computed, then split into
+      // the wO GEMM's f16 planes.
+      const size_t rb = (size_t)(E / 32) * (m->qt == 8 ? 34 : 18);  // bytes per weight row
+      Epi ev = e;
+      ev.kind = EPI_PLAIN;
+      ev.N = E;
+      ev.bias = w.bqkv + 2 * E;
+      ev.ldy = E;
+      LAUNCH(qgemm(m, m->xh.as<__half>(), m->xl.as<__half>(), M, E, w.wqkv + 2 * (size_t)E * rb, E, w.sh_qkv, ev));
+      LAUNCH(launch(m, KC_OTHER, 0.0, T * E * 8.0, [&] {
+        return t0b_launch_split_f32(m->qkv.as<float>(), m->ah.as<__half>(), m->al.as<__half>(), T * (size_t)E,
+                                    m->stream);
+      }));
+      LAUNCH(resid_gemm(m, m->ah.as<__half>(), m->al.as<__half>(), M, E, w.wo, w.sh_o, w.bo, x, w.g_mlp, &ssq_nt));
+    } else {
     LAUNCH(qgemm(m, m->xh.as<__half>(), m->xl.as<__half>(), M, E, w.wqkv, 3 * E, w.sh_qkv, e));
     aa.qn = w.qn;
     aa.kn = w.kn;
@@ -819,6 +839,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
       }));
     }
     LAUNCH(resid_gemm(m, m->ah.as<__half>(), m->al.as<__half>(), M, E, w.wo, w.sh_o, w.bo, x, w.g_mlp, &ssq_nt));
+    }
 
     Epi sg{};
     sg.kind = EPI_SWIGLU;
