@@ -161,17 +161,34 @@ class ClockSampler:
         self.indices = set(indices)
         self.path = os.path.join("/tmp", f"t0b_clocks_{os.getpid()}_{id(self)}.csv")
 
+    def _lines(self):
+        try:
+            with open(self.path) as f:
+                return sum(1 for _ in f)
+        except OSError:
+            return 0
+
+    def _wait_lines(self, more_than, timeout_s):
+        t_end = time.time() + timeout_s
+        while self._lines() <= more_than and time.time() < t_end and self.proc.poll() is None:
+            time.sleep(0.01)
+
     def start(self):
+        """Starts sampling and returns once the first sample is written, so a
+        short timed region that follows is bracketed by samples."""
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return self
+        self._wait_lines(0, 5.0)
         return self
 
     def stop(self):
         if not self.proc:
             return None
+        self._wait_lines(self._lines(), 0.5)  # one more sample after the timed region
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)

@@ -16,13 +16,45 @@
 
 // ============================================================== prep
 // One warp per variate row.  The causal scaler is the reference's Welford
-// recurrence in f32 (scaler.rs:44-118), inherently sequential: lane 0 runs it
-// over a chunk of kPrepChunk steps and records (count, mean, m2) after every
-// step in shared memory; then all 32 lanes turn those states into the
-// per-step loc / scale, the scaled value and the patch features in parallel
+// recurrence in f32 (scaler.rs:44-118).  Per chunk of kPrepChunk steps each
+// lane runs that recurrence over its own 1/32 of the chunk, starting from
+// the state before its first step: the carried state of the previous chunks
+// merged with the states of the lanes before it by the pairwise update of
+// Chan, Golub and LeVeque (a warp scan over lanes' local Welford states);
+// lane 0 continues the carried state exactly, so a row of at most
+// kPrepChunk / 32 steps per lane reproduces the sequential recurrence bit for
+// bit, and later lanes differ from it by the rounding of the merge.  The
+// states after every step go to shared memory; then all 32 lanes turn them
+// into the per-step loc / scale, the scaled value and the patch features
 // (lane = step within the patch, so feature rows are written coalesced).
 constexpr int kPrepChunk = 256;  // steps per chunk (a multiple of the patch size 32)
 constexpr int kPrepWarps = 4;
+
+// Welford state (ca, ma, qa) of earlier steps followed by (cb, mb, qb):
+// count, mean and sum of squared deviations of both, into (cb, mb, qb).
+T0B_DEV void welford_merge(float ca, float ma, float qa, float &cb, float &mb, float &qb) {
+  if (ca == 0.0f) return;
+  if (cb == 0.0f) {
+    cb = ca;
+    mb = ma;
+    qb = qa;
+    return;
+  }
+  const float n = ca + cb, d = mb - ma;
+  mb = ma + d * (cb / n);
+  qb = (qa + qb) + d * d * (ca * cb / n);
+  cb = n;
+}
+// One Welford step (the reference's operation order; NaN = not observed).
+T0B_DEV void welford_step(float x, float &count, float &mean, float &m2) {
+  if (!isnan(x)) {
+    count = __fadd_rn(count, 1.0f);
+    const float delta = __fsub_rn(x, mean);
+    mean = __fadd_rn(mean, __fdiv_rn(delta, count));
+    const float delta2 = __fsub_rn(x, mean);
+    m2 = __fadd_rn(m2, __fmul_rn(delta, delta2));
+  }
+}
 
 __global__ void __launch_bounds__(32 * kPrepWarps) prep_kernel(PrepArgs a) {
   __shared__ __align__(16) float s_x[kPrepWarps][kPrepChunk];
@@ -37,40 +69,52 @@ __global__ void __launch_bounds__(32 * kPrepWarps) prep_kernel(PrepArgs a) {
   const float *src = a.ctx + a.row_off[r];
   const int steps = a.p * 32;
   const int hp0 = a.p - a.hp - 1;  // first output patch
-  float count = 0.0f, mean = 0.0f, m2 = 0.0f;  // lane 0's recurrence state
+  float count = 0.0f, mean = 0.0f, m2 = 0.0f;  // state after the previous chunks (same in every lane)
+  // raw values of a chunk, coalesced (lane + 32 j); steps outside the context
+  // read as NaN here (not observed), which only the recurrence looks at.
+  // The next chunk's values are loaded while the current one is processed.
+  constexpr int kPer = kPrepChunk / 32;
+  float xr[kPer];
+  auto load_chunk = [&](int c0) {
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int t = c0 + lane + 32 * j;
+      xr[j] = (t < steps && t >= lead && t < lead + len) ? src[t - lead] : __int_as_float(0x7fc00000);
+    }
+  };
+  load_chunk(0);
   for (int c0 = 0; c0 < steps; c0 += kPrepChunk) {
     const int n = min(kPrepChunk, steps - c0);
-    // raw values of the chunk, coalesced; steps outside the context read as
-    // NaN here (not observed), which only the recurrence below looks at
-    for (int i = lane; i < n; i += 32) {
-      const int t = c0 + i;
-      s_x[w][i] = (t >= lead && t < lead + len) ? src[t - lead] : __int_as_float(0x7fc00000);
-    }
-    __syncwarp();
-    if (lane == 0) {  // n is a multiple of 32: four steps per 16-byte read and write
-#pragma unroll 2
-      for (int i = 0; i < n; i += 4) {
-        const float4 x4 = *reinterpret_cast<const float4 *>(&s_x[w][i]);
-        const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
-        float cs[4], ms[4], vs[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float x = xs[u];
-          if (!isnan(x)) {
-            count = __fadd_rn(count, 1.0f);
-            const float delta = __fsub_rn(x, mean);
-            mean = __fadd_rn(mean, __fdiv_rn(delta, count));
-            const float delta2 = __fsub_rn(x, mean);
-            m2 = __fadd_rn(m2, __fmul_rn(delta, delta2));
-          }
-          cs[u] = count;
-          ms[u] = mean;
-          vs[u] = m2;
-        }
-        *reinterpret_cast<float4 *>(&s_cnt[w][i]) = make_float4(cs[0], cs[1], cs[2], cs[3]);
-        *reinterpret_cast<float4 *>(&s_mean[w][i]) = make_float4(ms[0], ms[1], ms[2], ms[3]);
-        *reinterpret_cast<float4 *>(&s_m2[w][i]) = make_float4(vs[0], vs[1], vs[2], vs[3]);
+    for (int j = 0; j < kPer; ++j)
+      if (lane + 32 * j < n) s_x[w][lane + 32 * j] = xr[j];
+    if (c0 + kPrepChunk < steps) load_chunk(c0 + kPrepChunk);
+    __syncwarp();
+    {
+      // n is a multiple of 32: lane l takes steps [l seg, (l + 1) seg)
+      const int seg = n >> 5, i0 = lane * seg;
+      float lc = 0.0f, lm = 0.0f, lq = 0.0f;  // this lane's steps alone
+      for (int i = 0; i < seg; ++i) welford_step(s_x[w][i0 + i], lc, lm, lq);
+      // inclusive scan over lanes, then the state before this lane's steps
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float pc = __shfl_up_sync(0xffffffffu, lc, o), pm = __shfl_up_sync(0xffffffffu, lm, o),
+                    pq = __shfl_up_sync(0xffffffffu, lq, o);
+        if (lane >= o) welford_merge(pc, pm, pq, lc, lm, lq);
       }
+      float c = __shfl_up_sync(0xffffffffu, lc, 1), m = __shfl_up_sync(0xffffffffu, lm, 1),
+            q = __shfl_up_sync(0xffffffffu, lq, 1);
+      if (lane == 0) c = m = q = 0.0f;
+      welford_merge(count, mean, m2, c, m, q);
+      for (int i = 0; i < seg; ++i) {
+        welford_step(s_x[w][i0 + i], c, m, q);
+        s_cnt[w][i0 + i] = c;
+        s_mean[w][i0 + i] = m;
+        s_m2[w][i0 + i] = q;
+      }
+      count = __shfl_sync(0xffffffffu, c, 31);
+      mean = __shfl_sync(0xffffffffu, m, 31);
+      m2 = __shfl_sync(0xffffffffu, q, 31);
     }
     __syncwarp();
     for (int i = lane; i < n; i += 32) {
