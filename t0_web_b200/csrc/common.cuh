@@ -24,12 +24,31 @@ enum : int {
   T0B_DEVERR_WAIT_EMPTY = 4, // MMA never released a stage
   T0B_DEVERR_WAIT_ACC = 5,   // accumulator never completed
   T0B_DEVERR_SHAPE = 6,      // kernel launched with an unsupported shape
-  T0B_DEVERR_WAIT_ATTN = 7   // attention k / v tiles never arrived
+  T0B_DEVERR_WAIT_ATTN = 7,  // attention k / v tiles never arrived
+  T0B_DEVERR_BOUNDS = 8      // an index check of the checked build failed
 };
 
 T0B_DEV void record_error(int *err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
+
+// Index checks of the checked build (-DT0B_CHECKED, libt0b_checked.so): a
+// failed check records T0B_DEVERR_BOUNDS in the error word and the caller
+// skips the access, so an indexing mistake surfaces as a status at the host
+// (a skipped TMA load as a bounded wait that runs out) instead of a memory
+// fault.  In the product build every check is the constant `true`.
+#ifdef T0B_CHECKED
+#define T0B_CHECK(cond, err) t0b_check_index((cond), (err))
+#else
+#define T0B_CHECK(cond, err) true
+#endif
+T0B_DEV bool t0b_check_index(bool ok, int *err) {
+  if (!ok) record_error(err, T0B_DEVERR_BOUNDS);
+  return ok;
+}
+// TMA coordinates: the innermost one (x, in elements of `bytes` bytes) on a
+// 16-byte boundary and non-negative, the others non-negative.
+#define T0B_CHECK_TMA(x, bytes, y, err) T0B_CHECK((x) >= 0 && ((x) * (bytes)) % 16 == 0 && (y) >= 0, err)
 
 T0B_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

@@ -130,6 +130,7 @@ __global__ void __launch_bounds__(kThreads) gemm_q_small_kernel(const __half *__
     for (int r = warp; r < kRows; r += kWarps) {
       const int wrow = swiglu ? (r < 16 ? 0 : epi.F) + f0 + (r & 15) : n0 + r;
       const uint8_t *src = W + (size_t)wrow * RB + (size_t)z * L.wpitch;
+      if (!T0B_CHECK(wrow < (swiglu ? 2 * epi.F : epi.N), err)) continue;
       for (int q = lane; q < gpr; q += 32) cp_async16(wst + r * L.wpitch + q * 16, src + q * 16);
     }
     if (threadIdx.x < kRows) {
@@ -284,6 +285,7 @@ __global__ void __launch_bounds__(kThreads) gemm_q_small_kernel(const __half *__
     if (m >= M) break;
     const float denom = nt ? e_ssq[t * nt] : 1.0f;
     const int c = lane;
+    if (!T0B_CHECK(swiglu ? f0 + 16 <= epi.F : n0 + kRows <= epi.N, err)) break;
     if (swiglu) {
       if (c < 16) {
         const float gt = tile[c * LD + t] / denom + e_bias[c];
@@ -311,7 +313,7 @@ __global__ void __launch_bounds__(kThreads) gemm_q_small_kernel(const __half *__
       float ss = xn * xn;
 #pragma unroll
       for (int sh = 16; sh > 0; sh >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, sh);
-      if (c == 0) epi.ssq_out[(size_t)m * epi.ssq_out_nt + blockIdx.x] = ss;
+      if (c == 0 && T0B_CHECK((int)blockIdx.x < epi.ssq_out_nt, err)) epi.ssq_out[(size_t)m * epi.ssq_out_nt + blockIdx.x] = ss;
     }
   }
 }

@@ -369,8 +369,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             break;
           if (rank == 0) mbar_arrive_expect_tx(&x_full[xs], 4 * X_TILE);  // hi + lo of both CTAs
           const uint32_t fb = lead(&x_full[xs]);
-          tma_load_2d_pair(smem + P_OFF_XH + xs * X_TILE, &tm_xh, fb, s * BK, m0);
-          tma_load_2d_pair(smem + P_OFF_XL + xs * X_TILE, &tm_xl, fb, s * BK, m0);
+          if (T0B_CHECK_TMA(s * BK, 2, m0, prm.err) && T0B_CHECK(s * BK < prm.K, prm.err)) {
+            tma_load_2d_pair(smem + P_OFF_XH + xs * X_TILE, &tm_xh, fb, s * BK, m0);
+            tma_load_2d_pair(smem + P_OFF_XL + xs * X_TILE, &tm_xl, fb, s * BK, m0);
+          }
         }
       }
     } else if (warp == 2 && lane == 0) {
@@ -388,7 +390,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             break;
           const int x = (s * BPB) & ~15;  // aligned window holding block column s
           mbar_arrive_expect_tx(&raw_full[rs], C::RAW_SLOT);
-          tma_load_2d(smem + P_OFF_RAW + rs * C::RAW_SLOT, &tm_w, &raw_full[rs], x, wrow);
+          if (T0B_CHECK_TMA(x, 1, wrow, prm.err))
+            tma_load_2d(smem + P_OFF_RAW + rs * C::RAW_SLOT, &tm_w, &raw_full[rs], x, wrow);
         }
       }
     } else if (warp == 1 && lane == 0 && rank == 0) {
@@ -538,8 +541,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tm_zh, stg, x, row0);
-            tma_store_2d(&tm_zl, stg + 1024, x, row0);
+            if (T0B_CHECK_TMA(x, 2, row0, prm.err)) {
+              tma_store_2d(&tm_zh, stg, x, row0);
+              tma_store_2d(&tm_zl, stg + 1024, x, row0);
+            }
             bulk_commit();
           }
         };
@@ -619,7 +624,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(&tm_y, stg, col0 + 16 * c, row0);
+              if (T0B_CHECK_TMA(col0 + 16 * c, 4, row0, prm.err)) tma_store_2d(&tm_y, stg, col0 + 16 * c, row0);
               bulk_commit();
             }
 #pragma unroll
@@ -632,7 +637,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int i = 0; i < 8; ++i) split2(xv[2 * i], xv[2 * i + 1], w[2 * i], w[2 * i + 1]);
             store_hl(w, col0 + 16 * c);
           }
-          if (live) e.ssq_out[(size_t)m * e.ssq_out_nt + (col0 >> 6)] = ss;
+          if (live && T0B_CHECK((col0 >> 6) < e.ssq_out_nt, prm.err)) e.ssq_out[(size_t)m * e.ssq_out_nt + (col0 >> 6)] = ss;
         } else {  // EPI_PLAIN: bias, then f32 chunks stored (or reduce-added) by TMA
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -647,10 +652,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              if (e.reduce_add)
+              if (!T0B_CHECK_TMA(nt * BN + c0, 4, row0, prm.err)) {
+              } else if (e.reduce_add) {
                 tma_reduce_add_2d(&tm_y, stg, nt * BN + c0, row0);
-              else
+              } else {
                 tma_store_2d(&tm_y, stg, nt * BN + c0, row0);
+              }
               bulk_commit();
             }
           }

@@ -142,6 +142,7 @@ __global__ void __launch_bounds__(32 * kPrepWarps) prep_kernel(PrepArgs a) {
         sc = a.variance_offset ? __fsqrt_rn(__fadd_rn(var, a.eps)) : fmaxf(__fsqrt_rn(var), a.eps);
       }
       const float zv = __fdiv_rn(__fsub_rn(x, lo), sc);
+      if (!T0B_CHECK(patch < a.p && k < 32, a.err)) continue;
       float *f = a.feat + ((size_t)r * a.p + patch) * 96;
       f[k] = a.use_arcsinh ? asinhf(zv) : zv;
       f[32 + k] = (float)k / 32.0f;
@@ -665,11 +666,15 @@ __global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a, const
       if (threadIdx.x == 0) {
         mbar_arrive_expect_tx(bar, (uint32_t)(6 * p * 32 * sizeof(float)));
 #pragma unroll
-        for (int bx = 0; bx < 4; ++bx)
-          tma_load_2d(tb + (size_t)bx * PK * 128, &tm_qkv, bar, (bx < 2 ? E : 2 * E) + h * 64 + 32 * (bx & 1), (int)tok0);
+        for (int bx = 0; bx < 4; ++bx) {
+          const int x = (bx < 2 ? E : 2 * E) + h * 64 + 32 * (bx & 1);
+          if (T0B_CHECK_TMA(x, 4, (int)tok0, a.err)) tma_load_2d(tb + (size_t)bx * PK * 128, &tm_qkv, bar, x, (int)tok0);
+        }
         uint8_t *qt = attn_qtile(Kh, PK);  // q dims 0-31 and 32-63, kept past the staging
-        tma_load_2d(qt, &tm_qkv, bar, h * 64, (int)tok0);
-        tma_load_2d(qt + (size_t)PK * 128, &tm_qkv, bar, h * 64 + 32, (int)tok0);
+        if (T0B_CHECK_TMA(h * 64, 4, (int)tok0, a.err)) {
+          tma_load_2d(qt, &tm_qkv, bar, h * 64, (int)tok0);
+          tma_load_2d(qt + (size_t)PK * 128, &tm_qkv, bar, h * 64 + 32, (int)tok0);
+        }
       }
       const bool ok = mbar_wait(bar, 0, a.err, T0B_DEVERR_WAIT_ATTN, nullptr) && j < p;
 #pragma unroll
@@ -918,8 +923,10 @@ __global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a, const
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_store_3d(&tm_oh, sh, h * 64, qb * 16, r);
-      tma_store_3d(&tm_ol, sl, h * 64, qb * 16, r);
+      if (T0B_CHECK_TMA(h * 64, 2, qb * 16, a.err) && T0B_CHECK(r >= 0, a.err)) {
+        tma_store_3d(&tm_oh, sh, h * 64, qb * 16, r);
+        tma_store_3d(&tm_ol, sl, h * 64, qb * 16, r);
+      }
       bulk_commit();
     }
   }
@@ -1017,8 +1024,10 @@ __global__ void __launch_bounds__(512, 1) attn_time_pl_kernel(AttnArgs a, const 
     mbar_arrive_expect_tx(bar, 6 * tile);
 #pragma unroll
     for (int sg = 0; sg < 3; ++sg) {  // q, k, v
-      tma_load_3d(base + (2 * sg) * tile, &tm_h, bar, sg * E + h * 64, 0, r);
-      tma_load_3d(base + (2 * sg + 1) * tile, &tm_l, bar, sg * E + h * 64, 0, r);
+      if (T0B_CHECK_TMA(sg * E + h * 64, 2, r, a.err)) {
+        tma_load_3d(base + (2 * sg) * tile, &tm_h, bar, sg * E + h * 64, 0, r);
+        tma_load_3d(base + (2 * sg + 1) * tile, &tm_l, bar, sg * E + h * 64, 0, r);
+      }
     }
   }
   mbar_wait(bar, 0, a.err, T0B_DEVERR_WAIT_ATTN, nullptr);
@@ -1153,8 +1162,10 @@ __global__ void __launch_bounds__(512, 1) attn_time_pl_kernel(AttnArgs a, const 
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
-    tma_store_3d(&tm_oh, sh, h * 64, qb * 16, r);
-    tma_store_3d(&tm_ol, sl, h * 64, qb * 16, r);
+    if (T0B_CHECK_TMA(h * 64, 2, qb * 16, a.err) && T0B_CHECK(r >= 0, a.err)) {
+      tma_store_3d(&tm_oh, sh, h * 64, qb * 16, r);
+      tma_store_3d(&tm_ol, sl, h * 64, qb * 16, r);
+    }
     bulk_commit();
     bulk_wait_all();  // stores done before the CTA (and its shared memory) ends
   }

@@ -24,6 +24,7 @@ struct PrepArgs {
   float eps;
   float *feat;           // [R*p, 96]
   float *out_loc, *out_scale;  // [R*hp] stats at the last step of each output patch
+  int *err;              // device error word (index checks of the checked build)
 };
 
 struct SgemmArgs {

@@ -16,11 +16,24 @@
 #include <string>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "../../include/t0b.h"
 #include "gguf_host.h"
 #include "t0b_internal.h"
 
 namespace {
+
+// An NVTX range over the object's lifetime (host-side annotation for
+// profilers; a no-op when no tool is attached).  Ranges: every forecast
+// call, every pass, every layer of a pass that is launched rather than
+// replayed from its CUDA graph (graphs off, or profiling on).
+struct NvtxRange {
+  explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange &) = delete;
+  NvtxRange &operator=(const NvtxRange &) = delete;
+};
 
 thread_local std::string g_last_error;
 
@@ -628,6 +641,9 @@ t0b_status ensure_ws(t0b_model *m, size_t T, size_t R, size_t nout) {
 t0b_status run_pass(t0b_model *m, const Pass &ps) {
   const int R = ps.R, p = ps.p, hp = ps.hp, E = m->E, F = m->F;
   const size_t T = (size_t)R * p;
+  char pass_name[64];
+  std::snprintf(pass_name, sizeof(pass_name), "t0b pass rows=%d patches=%d", R, p);
+  const NvtxRange pass_range(pass_name);
   const int ns = (int)ps.s_row0.size();
   if (T == 0) return T0B_OK;
   // the previous pass must be done before buffers are grown or the pinned
@@ -710,6 +726,7 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
   pa.feat = m->feat.as<float>();
   pa.out_loc = m->loc.as<float>();
   pa.out_scale = m->scl.as<float>();
+  pa.err = m->d_err;
   LAUNCH(launch(m, KC_PREP, 0.0, (double)R * p * 32 * 4 + T * 96.0 * 4, [&] { return t0b_launch_prep(pa, m->stream); }));
 
   // 2. patch encoder: x = relu(f.hw^T+hb).ow^T + ob + f.rw^T + rb + type_emb[0]
@@ -781,6 +798,9 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
 
   for (int l = 0; l < m->L; ++l) {
     const LayerW &w = m->layers[l];
+    char layer_name[32];
+    std::snprintf(layer_name, sizeof(layer_name), "layer %d %s", l, w.group ? "GROUP" : "TIME");
+    const NvtxRange layer_range(layer_name);
     // q | k | v = rmsnorm(x) . wQKV^T + b; QK-norm and RoPE happen in the
     // attention kernels as q and k are read, or in the epilogue (planes)
     const bool planes = qkv_planes && !w.group;
@@ -961,6 +981,7 @@ struct HostIO {
 t0b_status run_series(t0b_model *m, const float *ctx_dev, const std::vector<RowSpec> &rows,
                       const std::vector<int> &series_nrows, int ctx_w, int horizon, float *out_dev,
                       size_t max_rows_hint, const HostIO *hio = nullptr) {
+  const NvtxRange range("t0b forecast");
   const int hpad = (horizon + 31) / 32 * 32;
   const int p = (ctx_w + hpad) / 32, hp = hpad / 32;
   if (m->E / m->H == 128 && p > 256)
@@ -1360,6 +1381,7 @@ std::vector<float> prob_mass(const float *levels, int n) {
 
 extern "C" t0b_status t0b_forecast_rollout(t0b_model *m, const float *ctx, size_t t_ctx, size_t prediction_length,
                                            const float *query, size_t n_query, float *out) {
+  const NvtxRange range("t0b forecast_rollout");
   if (!m || !ctx || !query || !out) return fail(T0B_ERR_INVALID, "t0b_forecast_rollout: NULL argument");
   if (t_ctx == 0 || prediction_length == 0 || n_query == 0 || n_query > 64)
     return fail(T0B_ERR_INVALID, "t0b_forecast_rollout: need t_ctx >= 1, prediction_length >= 1, 1..64 levels");

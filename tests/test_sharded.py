@@ -47,12 +47,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, nv, horizon, fail_rank, q):
+def _rank_main(rank, world, port, nv, horizon, fail_rank, q, pg_timeout_s):
     try:
         import torch
         import torch.distributed as dist
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=pg_timeout_s))
         rr = sharded.shard_rows(nv, world)
         r0, r1 = rr[rank]
         local = torch.arange(r0, r1, dtype=torch.float32)[:, None, None].expand(r1 - r0, horizon, 5).contiguous()
@@ -65,11 +65,16 @@ def _rank_main(rank, world, port, nv, horizon, fail_rank, q):
         q.put((rank, "error", f"{type(e).__name__}: {e}\n{traceback.format_exc(limit=2)}"))
 
 
-def _run(world, nv, horizon=3, fail_rank=-1, limit=90):
+def _run(world, nv, horizon=3, fail_rank=-1, limit=150, pg_timeout_s=60):
+    # healthy runs get a long process-group timeout (it also bounds the
+    # rendezvous, and a spawned rank can take seconds to import torch on a
+    # loaded machine); the dead-rank case a short one, so the survivor's
+    # collective ends with an error well within `limit`
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, nv, horizon, fail_rank, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, nv, horizon, fail_rank, q, pg_timeout_s))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = {}
@@ -106,6 +111,6 @@ def test_gather_outputs_rank_with_no_series():
 
 
 def test_dead_rank_fails_collective_with_timeout():
-    res = _run(2, np.array([2, 2, 2], np.int64), fail_rank=1)
+    res = _run(2, np.array([2, 2, 2], np.int64), fail_rank=1, pg_timeout_s=10)
     assert res[1][0] == "error" and "planted failure" in res[1][1]
     assert res[0][0] == "error", "surviving rank must get an error, not a result"
