@@ -21,7 +21,8 @@ struct Epi {
   const float *ssq_in;
   int ssq_in_nt, ssq_dim;
   // EPI_PLAIN: y [M, ldy] = acc / row denominator + bias (reduce_add: y +=
-  // that instead; tensor-core kernel only)
+  // that instead; tensor-core kernel only).  Small-M kernel with zh set: that
+  // value split into f16 planes zh / zl [M, ldy] instead of y.
   float *y;
   int ldy;
   int reduce_add;

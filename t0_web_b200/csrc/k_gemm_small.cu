@@ -301,7 +301,16 @@ __global__ void __launch_bounds__(kThreads) gemm_q_small_kernel(const __half *__
         if (epi.z32) epi.z32[o] = zv;
       }
     } else if (!resid) {
-      epi.y[(size_t)m * epi.ldy + n0 + c] = tile[c * LD + t] / denom + e_bias[c];
+      const float yv = tile[c * LD + t] / denom + e_bias[c];
+      const size_t o = (size_t)m * epi.ldy + n0 + c;
+      if (epi.zh) {  // the split straight into f16 planes (the next GEMM's operand)
+        __half h, l;
+        split_f16(yv, h, l);
+        epi.zh[o] = h;
+        epi.zl[o] = l;
+      } else {
+        epi.y[o] = yv;
+      }
     } else {
       const float xn = e_x[t * kRows + c] + (tile[c * LD + t] / denom + e_bias[c]);
       const size_t o = (size_t)m * epi.N + n0 + c;

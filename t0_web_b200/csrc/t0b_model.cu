@@ -830,19 +830,26 @@ t0b_status run_pass(t0b_model *m, const Pass &ps) {
       // every series has one variate: the group attention of a token is a
       // softmax over its own key alone, exactly 1, so its output is exactly
       // v (mask.rs:69-82 makes a lone whole-padding query average the same
-      // single v).  Only the v third of wQKV is computed, then split into
-      // the wO GEMM's f16 planes.
+      // single v).  Only the v third of wQKV is computed, as the wO GEMM's
+      // f16 planes: split in the small-M epilogue, by a split pass after
+      // the tensor-core GEMM.
       const size_t rb = (size_t)(E / 32) * (m->qt == 8 ? 34 : 18);  // bytes per weight row
       Epi ev = e;
       ev.kind = EPI_PLAIN;
       ev.N = E;
       ev.bias = w.bqkv + 2 * E;
       ev.ldy = E;
+      const bool tc_v = use_tc(m, M, E, ev);
+      if (!tc_v) {
+        ev.zh = m->ah.as<__half>();
+        ev.zl = m->al.as<__half>();
+      }
       LAUNCH(qgemm(m, m->xh.as<__half>(), m->xl.as<__half>(), M, E, w.wqkv + 2 * (size_t)E * rb, E, w.sh_qkv, ev));
-      LAUNCH(launch(m, KC_OTHER, 0.0, T * E * 8.0, [&] {
-        return t0b_launch_split_f32(m->qkv.as<float>(), m->ah.as<__half>(), m->al.as<__half>(), T * (size_t)E,
-                                    m->stream);
-      }));
+      if (tc_v)
+        LAUNCH(launch(m, KC_OTHER, 0.0, T * E * 8.0, [&] {
+          return t0b_launch_split_f32(m->qkv.as<float>(), m->ah.as<__half>(), m->al.as<__half>(), T * (size_t)E,
+                                      m->stream);
+        }));
       LAUNCH(resid_gemm(m, m->ah.as<__half>(), m->al.as<__half>(), M, E, w.wo, w.sh_o, w.bo, x, w.g_mlp, &ssq_nt));
     } else {
     LAUNCH(qgemm(m, m->xh.as<__half>(), m->xl.as<__half>(), M, E, w.wqkv, 3 * E, w.sh_qkv, e));
