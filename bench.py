@@ -693,8 +693,9 @@ def run_standalone(args, workload=None, cases=None, engine=None, emit=True):
                 "dtype": "f32-class (split-f16)", "data": "synthetic N(0,0.02) weights, N(0,1) activations",
                 "roofline": roof, "path": "tcgen05" if not small else "mma.sync small-M", "clocks": clocks,
                 "timing": f"{ncalls} calls per CUDA graph over {ncopy} rotated weight copies "
-                          f"({ncopy * wbytes / 2**20:.0f} MiB), median of 20 replays; a call = x split "
-                          "+ GEMM(s)"}
+                          f"({ncopy * wbytes / 2**20:.0f} MiB), median of 20 replays; a call = the "
+                          "GEMM(s) on f32 x (GEMM: split into f16 planes inside the small-M kernel, one split pass "
+                          "before the tensor-core kernel; SwiGLU: one split pass, then the two GEMMs)"}
         lines.append(line)
         if emit:
             print(json.dumps(line), flush=True)

@@ -44,6 +44,8 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kKGroups = 8;  // warps split a slice's blocks 8 ways and its 32 rows into 2 tiles of 16
 constexpr int kRows = 32;        // weight rows (output columns) per CTA
 constexpr int kMaxCluster = 8;   // K slices per row group (portable cluster size)
+// the partial-tile region holds the f32 activation rows of a 256-wide K slice
+static_assert(kKGroups * kRows == 256, "f32 staging of x32 calls relies on an [8][32] partial-tile region");
 constexpr size_t kSmemCap = 200 * 1024;
 
 template <int QT>
@@ -58,7 +60,7 @@ struct QInfo<4> {
 };
 
 struct SmallLayout {
-  size_t wpitch, apitch, w_off, a_off, red_off, slot_off, eb_off, eg_off, ex_off, es_off, bytes;
+  size_t wpitch, apitch, w_off, a_off, red_off, slot_off, eb_off, eg_off, ex_off, es_off, xs_off, bytes;
 };
 
 // Shared memory of one CTA: raw weights [32][KS/32 blocks], activations
@@ -66,8 +68,11 @@ struct SmallLayout {
 // [8][32][MT] f32, cluster slots [cs][32][MT+1] f32 (slot z: the tile of K
 // slice z; only the first CTA's slots are used), then the epilogue operands:
 // bias [32], next-norm gain [32], residual rows [MT][32], RMSNorm partial
-// sums [MT][nt].
-__host__ __device__ inline SmallLayout small_layout(int qt, int KS, int MT, int cs, int nt) {
+// sums [MT][nt].  With f32 input (x32, K slices of 256 only) the f32
+// activation rows [MT][256] that the planes are split from sit in the
+// per-K-group partial-tile region, which is the same size and unused until
+// the MMAs are done.
+__host__ __device__ inline SmallLayout small_layout(int qt, int KS, int MT, int cs, int nt, bool x32 = false) {
   SmallLayout L;
   L.wpitch = (size_t)(KS / 32) * (qt == 8 ? 34 : 18);  // multiple of 16: KS % 256 == 0
   L.apitch = (size_t)KS * 2 + 16;                       // 16-byte pad: conflict-free ldmatrix rows
@@ -80,6 +85,8 @@ __host__ __device__ inline SmallLayout small_layout(int qt, int KS, int MT, int 
   L.ex_off = L.eg_off + kRows * 4;
   L.es_off = L.ex_off + (size_t)MT * kRows * 4;
   L.bytes = L.es_off + (size_t)MT * nt * 4;
+  L.xs_off = L.red_off;  // (x32) MT * KS * 4 == kKGroups * kRows * MT * 4 bytes at KS == 256
+  (void)x32;
   return L;
 }
 
@@ -90,9 +97,13 @@ T0B_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.rel
 T0B_DEV void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 T0B_DEV void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
+// Activations: the f16 planes ah / al [M][K], or, when x32 is given, the
+// f32 rows x32 [M][K], which each CTA splits into the planes of its K slice
+// in shared memory (standalone calls: no separate split kernel).
 template <int QT, int NT8>
 __global__ void __launch_bounds__(kThreads) gemm_q_small_kernel(const __half *__restrict__ ah,
-                                                                const __half *__restrict__ al, int M, int K,
+                                                                const __half *__restrict__ al,
+                                                                const float *__restrict__ x32, int M, int K,
                                                                 int KS, const uint8_t *__restrict__ W, Epi epi,
                                                                 int *err) {
   constexpr int BPB = QInfo<QT>::bpb;
@@ -101,7 +112,7 @@ __global__ void __launch_bounds__(kThreads) gemm_q_small_kernel(const __half *__
   extern __shared__ __align__(16) uint8_t smem[];
   const int cs = gridDim.z, z = blockIdx.z;  // cluster = the cs K slices of one row group
   const int nt = epi.ssq_in ? epi.ssq_in_nt : 0;
-  const SmallLayout L = small_layout(QT, KS, MT, cs, nt);
+  const SmallLayout L = small_layout(QT, KS, MT, cs, nt, x32 != nullptr);
   uint8_t *wst = smem + L.w_off;
   uint8_t *act = smem + L.a_off;
   float *red = reinterpret_cast<float *>(smem + L.red_off);
@@ -147,14 +158,24 @@ __global__ void __launch_bounds__(kThreads) gemm_q_small_kernel(const __half *__
   //    RMSNorm partial sums
   pdl_wait();
   {
-    // activation rows (plane * MT + token) by warp, granules by lane
-    const int gpt = KS / 8;  // 16-byte granules per token row per plane: a multiple of 32
-    for (int row = warp; row < 2 * MT; row += kWarps) {
-      const int pl = row >= MT, t = row - pl * MT;
-      const int m = min(m0 + t, M - 1);  // rows past M duplicate a valid row; their outputs are dropped
-      const __half *src = (pl ? al : ah) + (size_t)m * K + (size_t)z * KS;
-      uint8_t *dst = act + (size_t)row * L.apitch;
-      for (int q = lane; q < gpt; q += 32) cp_async16(dst + q * 16, src + q * 8);
+    if (x32) {
+      // f32 activation rows (token) by warp, 16-byte granules by lane
+      float *xs = reinterpret_cast<float *>(smem + L.xs_off);
+      for (int t = warp; t < MT; t += kWarps) {
+        const int m = min(m0 + t, M - 1);  // rows past M duplicate a valid row; their outputs are dropped
+        const float *src = x32 + (size_t)m * K + (size_t)z * KS;
+        for (int q = lane; q < KS / 4; q += 32) cp_async16(xs + (size_t)t * KS + 4 * q, src + 4 * q);
+      }
+    } else {
+      // activation rows (plane * MT + token) by warp, granules by lane
+      const int gpt = KS / 8;  // 16-byte granules per token row per plane: a multiple of 32
+      for (int row = warp; row < 2 * MT; row += kWarps) {
+        const int pl = row >= MT, t = row - pl * MT;
+        const int m = min(m0 + t, M - 1);  // rows past M duplicate a valid row; their outputs are dropped
+        const __half *src = (pl ? al : ah) + (size_t)m * K + (size_t)z * KS;
+        uint8_t *dst = act + (size_t)row * L.apitch;
+        for (int q = lane; q < gpt; q += 32) cp_async16(dst + q * 16, src + q * 8);
+      }
     }
     if (z == 0) {
       if (resid) {
@@ -175,6 +196,18 @@ __global__ void __launch_bounds__(kThreads) gemm_q_small_kernel(const __half *__
   pdl_launch_dependents();
   cp_async_wait<0>();
   __syncthreads();
+  if (x32) {  // split the f32 rows into the two planes, two values per thread and step
+    const float *xs = reinterpret_cast<const float *>(smem + L.xs_off);
+    for (int i = threadIdx.x; i < MT * KS / 2; i += kThreads) {
+      const int t = i / (KS / 2), k2 = i - t * (KS / 2);
+      const float2 v = *reinterpret_cast<const float2 *>(xs + (size_t)t * KS + 2 * k2);
+      uint32_t hw, lw;
+      split2(v.x, v.y, hw, lw);
+      *reinterpret_cast<uint32_t *>(act + (size_t)t * L.apitch + 4 * k2) = hw;
+      *reinterpret_cast<uint32_t *>(act + (size_t)(MT + t) * L.apitch + 4 * k2) = lw;
+    }
+    __syncthreads();
+  }
   // RMSNorm row denominators, one thread per token (slot order); read by the
   // epilogue after the barriers below
   if (z == 0 && nt && threadIdx.x < MT) {
@@ -337,11 +370,11 @@ int small_slice(int K) {
 }
 
 template <int QT, int NT8>
-cudaError_t launch_small_t(const __half *ah, const __half *al, int M, int K, int KS, const uint8_t *W,
-                           const Epi &epi, int *err, cudaStream_t st) {
+cudaError_t launch_small_t(const __half *ah, const __half *al, const float *x32, int M, int K, int KS,
+                           const uint8_t *W, const Epi &epi, int *err, cudaStream_t st) {
   constexpr int MT = 8 * NT8;
   const int cs = K / KS;
-  const SmallLayout L = small_layout(QT, KS, MT, cs, epi.ssq_in ? epi.ssq_in_nt : 0);
+  const SmallLayout L = small_layout(QT, KS, MT, cs, epi.ssq_in ? epi.ssq_in_nt : 0, x32 != nullptr);
   auto kfn = gemm_q_small_kernel<QT, NT8>;
   cudaError_t e = t0b_smem_limit((const void *)kfn, L.bytes);
   if (e != cudaSuccess) return e;
@@ -362,46 +395,49 @@ cudaError_t launch_small_t(const __half *ah, const __half *al, int M, int K, int
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kfn, ah, al, M, K, KS, W, epi, err);
+  return cudaLaunchKernelEx(&cfg, kfn, ah, al, x32, M, K, KS, W, epi, err);
 }
 
 // Tokens per CTA (8 * nt8) that fit in shared memory for this K; 0 if none.
 template <int QT>
-int small_nt8(int M, int K, const Epi &epi) {
+int small_nt8(int M, int K, const Epi &epi, bool x32 = false) {
   const int KS = small_slice(K);
   int nt8 = (M + 7) / 8 < 4 ? (M + 7) / 8 : 4;
   const int cs = K / KS, nt = epi.ssq_in ? epi.ssq_in_nt : 0;
-  while (nt8 > 1 && small_layout(QT, KS, 8 * nt8, cs, nt).bytes > kSmemCap) --nt8;
-  return small_layout(QT, KS, 8 * nt8, cs, nt).bytes > kSmemCap ? 0 : nt8;
+  while (nt8 > 1 && small_layout(QT, KS, 8 * nt8, cs, nt, x32).bytes > kSmemCap) --nt8;
+  return small_layout(QT, KS, 8 * nt8, cs, nt, x32).bytes > kSmemCap ? 0 : nt8;
 }
 
 template <int QT>
-cudaError_t launch_small_q(const __half *ah, const __half *al, int M, int K, const uint8_t *W, const Epi &epi,
-                           int *err, cudaStream_t st) {
+cudaError_t launch_small_q(const __half *ah, const __half *al, const float *x32, int M, int K, const uint8_t *W,
+                           const Epi &epi, int *err, cudaStream_t st) {
   const int KS = small_slice(K);
   // tokens per CTA: up to 32, fewer when a wide slice would not fit in
   // shared memory
-  const int nt8 = small_nt8<QT>(M, K, epi);
+  const int nt8 = small_nt8<QT>(M, K, epi, x32 != nullptr);
   if (!nt8) return cudaErrorInvalidValue;
   switch (nt8) {
-    case 1: return launch_small_t<QT, 1>(ah, al, M, K, KS, W, epi, err, st);
-    case 2: return launch_small_t<QT, 2>(ah, al, M, K, KS, W, epi, err, st);
-    case 3: return launch_small_t<QT, 3>(ah, al, M, K, KS, W, epi, err, st);
-    default: return launch_small_t<QT, 4>(ah, al, M, K, KS, W, epi, err, st);
+    case 1: return launch_small_t<QT, 1>(ah, al, x32, M, K, KS, W, epi, err, st);
+    case 2: return launch_small_t<QT, 2>(ah, al, x32, M, K, KS, W, epi, err, st);
+    case 3: return launch_small_t<QT, 3>(ah, al, x32, M, K, KS, W, epi, err, st);
+    default: return launch_small_t<QT, 4>(ah, al, x32, M, K, KS, W, epi, err, st);
   }
 }
 
 }  // namespace
 
-bool t0b_small_supports(int qt, int M, int K, const Epi &epi) {
+bool t0b_small_supports(int qt, int M, int K, const Epi &epi, bool x32) {
   if (M <= 0 || K <= 0 || K % 256) return false;
-  return (qt == 8 ? small_nt8<8>(M, K, epi) : small_nt8<4>(M, K, epi)) > 0;
+  if (x32 && small_slice(K) != 256) return false;  // the f32 rows are staged in the 256-wide partial-tile region
+  return (qt == 8 ? small_nt8<8>(M, K, epi, x32) : small_nt8<4>(M, K, epi, x32)) > 0;
 }
 
 // Host entry.  qt: 8 = Q8_0, 4 = Q4_0.  Requires K % 256 == 0 and the output
 // column count (N, or F for SWIGLU) a multiple of 32 (16 for SWIGLU).
 cudaError_t t0b_launch_gemm_small(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W,
-                                  const Epi &epi, int *err, cudaStream_t st) {
+                                  const Epi &epi, int *err, cudaStream_t st, const float *x32) {
   if (M <= 0 || K <= 0 || K % 256) return cudaErrorInvalidValue;
-  return qt == 8 ? launch_small_q<8>(ah, al, M, K, W, epi, err, st) : launch_small_q<4>(ah, al, M, K, W, epi, err, st);
+  if (x32 && small_slice(K) != 256) return cudaErrorInvalidValue;
+  return qt == 8 ? launch_small_q<8>(ah, al, x32, M, K, W, epi, err, st)
+                 : launch_small_q<4>(ah, al, x32, M, K, W, epi, err, st);
 }

@@ -75,13 +75,16 @@ bool t0b_make_tmap_f16_3d(CUtensorMap *tm, const void *ptr, uint64_t d0, uint64_
                           uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2, bool swizzle128);
 
 // Small-M dequant GEMM (k_gemm_small.cu): thread-block clusters along K,
-// launched as a programmatic dependent of the previous kernel on `st`.
+// launched as a programmatic dependent of the previous kernel on `st`.  The
+// activations are the f16 planes ah / al, or, when x32 is given, f32 rows
+// that the kernel splits itself (ah / al unused).
 cudaError_t t0b_launch_gemm_small(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W,
-                                  const Epi &epi, int *err, cudaStream_t st);
+                                  const Epi &epi, int *err, cudaStream_t st, const float *x32 = nullptr);
 // Whether the small-M kernel runs this shape: K is split into at most 8
 // slices of a multiple of 256 values (a divisor of K), which must fit in
-// shared memory; otherwise callers use the tensor-core kernel.
-bool t0b_small_supports(int qt, int M, int K, const Epi &epi);
+// shared memory (x32: f32 input, K slices of 256 values only); otherwise
+// callers use the tensor-core kernel (or, for x32, the planes of a split pass).
+bool t0b_small_supports(int qt, int M, int K, const Epi &epi, bool x32 = false);
 cudaError_t t0b_launch_gemm_tc(int qt, const __half *ah, const __half *al, int M, int K, const uint8_t *W, int wrows,
                                int wshift, const Epi &epi, int *err, cudaStream_t st);
 cudaError_t t0b_launch_absmax_scale(const uint8_t *W, size_t nblocks, int bpb, unsigned int *out, cudaStream_t st);

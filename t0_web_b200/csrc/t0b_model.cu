@@ -1490,6 +1490,22 @@ cudaError_t engine_qgemm(t0b_engine *e, int qt, const __half *ah, const __half *
   return t0b_launch_gemm_small(qt, ah, al, M, K, W, epi, err, st);
 }
 
+// GEMM on f32 activations x [M][K]: the small-M kernel splits them into its
+// f16 planes itself (no separate launch); the tensor-core kernel reads the
+// planes of one split pass into the engine's scratch.
+t0b_status engine_qgemm_x(t0b_engine *e, int qt, const float *x, int M, int K, const uint8_t *W, int wrows,
+                          int wshift, Epi &epi, int *err, cudaStream_t st) {
+  if (!engine_use_tc(qt, M, K, epi) && t0b_small_supports(qt, M, K, epi, true)) {
+    CUDA_TRY(t0b_launch_gemm_small(qt, nullptr, nullptr, M, K, W, epi, err, st, x));
+    return T0B_OK;
+  }
+  const t0b_status s = split_input(e, x, (size_t)M * K, st);
+  if (s != T0B_OK) return s;
+  CUDA_TRY(engine_qgemm(e, qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, W, wrows, wshift, epi,
+                        err, st));
+  return T0B_OK;
+}
+
 t0b_status engine_check(t0b_engine *e, cudaStream_t st) {
   CUDA_TRY(cudaStreamSynchronize(st));
   int herr = 0;
@@ -1512,8 +1528,7 @@ extern "C" t0b_status t0b_gemm_q(t0b_engine *e, int ggml_type, const void *w_dev
   if (N % 256) return fail(T0B_ERR_UNSUPPORTED, "t0b_gemm_q: N must be a multiple of 256");
   CUDA_TRY(cudaSetDevice(e->device));
   cudaStream_t st = (cudaStream_t)stream;
-  t0b_status s = split_input(e, x_dev, (size_t)M * K, st);
-  if (s != T0B_OK) return s;
+  t0b_status s;
   Epi ep{};
   ep.kind = EPI_PLAIN;
   ep.M = M;
@@ -1525,8 +1540,7 @@ extern "C" t0b_status t0b_gemm_q(t0b_engine *e, int ggml_type, const void *w_dev
   if (engine_use_tc(qt, M, K, ep) &&
       (s = device_weight_shift(e, qt, (const uint8_t *)w_dev, (size_t)N * K, st, &sh)) != T0B_OK)
     return s;
-  CUDA_TRY(engine_qgemm(e, qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, (const uint8_t *)w_dev, N,
-                        sh, ep, e->d_err, st));
+  if ((s = engine_qgemm_x(e, qt, x_dev, M, K, (const uint8_t *)w_dev, N, sh, ep, e->d_err, st)) != T0B_OK) return s;
   return engine_check(e, st);
 }
 
@@ -1541,8 +1555,7 @@ extern "C" t0b_status t0b_swiglu_q(t0b_engine *e, int ggml_type, const void *w0_
     return fail(T0B_ERR_UNSUPPORTED, "t0b_swiglu_q: K, F and N2 must be multiples of 256");
   CUDA_TRY(cudaSetDevice(e->device));
   cudaStream_t st = (cudaStream_t)stream;
-  t0b_status s = split_input(e, x_dev, (size_t)M * K, st);
-  if (s != T0B_OK) return s;
+  t0b_status s;
   if ((s = qm_reserve(e->scratch_zh, (size_t)M * F * 2, st)) != T0B_OK ||
       (s = qm_reserve(e->scratch_zl, (size_t)M * F * 2, st)) != T0B_OK)
     return s;
@@ -1569,6 +1582,12 @@ extern "C" t0b_status t0b_swiglu_q(t0b_engine *e, int ggml_type, const void *w0_
   if (engine_use_tc(qt, M, F, dn) &&
       (s = device_weight_shift(e, qt, (const uint8_t *)w2_dev, (size_t)N2 * F, st, &sh2)) != T0B_OK)
     return s;
+  // the gate / up GEMM reads the planes of a split pass even on the small-M
+  // path: launched as the split's programmatic dependent it prefetches its
+  // weights while the split runs (M = 16: 23.6 us per call, 26.4 us with
+  // the split inside the GEMM, whose CTAs then wait for the previous
+  // kernel's to leave the SMs)
+  if ((s = split_input(e, x_dev, (size_t)M * K, st)) != T0B_OK) return s;
   CUDA_TRY(engine_qgemm(e, qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, (const uint8_t *)w0_dev,
                         2 * F, sh0, sg, e->d_err, st));
   CUDA_TRY(engine_qgemm(e, qt, e->scratch_zh.as<__half>(), e->scratch_zl.as<__half>(), M, F, (const uint8_t *)w2_dev, N2,
@@ -1626,12 +1645,6 @@ extern "C" t0b_status t0b_qmatrix_gemm(t0b_qmatrix *q, const float *x_dev, int M
   if (M < 1) return fail(T0B_ERR_INVALID, "t0b_qmatrix_gemm: empty shape");
   CUDA_TRY(cudaSetDevice(q->eng->device));
   cudaStream_t st = (cudaStream_t)stream;
-  const size_t n = (size_t)M * q->K;
-  t0b_status s;
-  t0b_engine *e = q->eng;
-  if ((s = qm_reserve(e->scratch_xh, n * 2, st)) != T0B_OK || (s = qm_reserve(e->scratch_xl, n * 2, st)) != T0B_OK)
-    return s;
-  CUDA_TRY(t0b_launch_split_f32(x_dev, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), n, st));
   Epi ep{};
   ep.kind = EPI_PLAIN;
   ep.M = M;
@@ -1639,9 +1652,7 @@ extern "C" t0b_status t0b_qmatrix_gemm(t0b_qmatrix *q, const float *x_dev, int M
   ep.bias = bias_dev;
   ep.y = y_dev;
   ep.ldy = q->N;
-  CUDA_TRY(engine_qgemm(e, q->qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, q->K, q->W, q->N,
-                        q->shift, ep, q->d_err, st));
-  return T0B_OK;
+  return engine_qgemm_x(q->eng, q->qt, x_dev, M, q->K, q->W, q->N, q->shift, ep, q->d_err, st);
 }
 
 extern "C" t0b_status t0b_qmatrix_swiglu(t0b_qmatrix *q0, t0b_qmatrix *q2, const float *x_dev, int M,
@@ -1655,14 +1666,11 @@ extern "C" t0b_status t0b_qmatrix_swiglu(t0b_qmatrix *q0, t0b_qmatrix *q2, const
   if (F % 256) return fail(T0B_ERR_UNSUPPORTED, "t0b_qmatrix_swiglu: F must be a multiple of 256");
   CUDA_TRY(cudaSetDevice(q0->eng->device));
   cudaStream_t st = (cudaStream_t)stream;
-  const size_t n = (size_t)M * K;
   t0b_status s;
   t0b_engine *e = q0->eng;
-  if ((s = qm_reserve(e->scratch_xh, n * 2, st)) != T0B_OK || (s = qm_reserve(e->scratch_xl, n * 2, st)) != T0B_OK ||
-      (s = qm_reserve(e->scratch_zh, (size_t)M * F * 2, st)) != T0B_OK ||
+  if ((s = qm_reserve(e->scratch_zh, (size_t)M * F * 2, st)) != T0B_OK ||
       (s = qm_reserve(e->scratch_zl, (size_t)M * F * 2, st)) != T0B_OK)
     return s;
-  CUDA_TRY(t0b_launch_split_f32(x_dev, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), n, st));
   Epi sg{};
   sg.kind = EPI_SWIGLU;
   sg.M = M;
@@ -1672,6 +1680,8 @@ extern "C" t0b_status t0b_qmatrix_swiglu(t0b_qmatrix *q0, t0b_qmatrix *q2, const
   sg.zh = e->scratch_zh.as<__half>();
   sg.zl = e->scratch_zl.as<__half>();
   sg.z32 = z_dev;
+  // a split pass first, as in t0b_swiglu_q
+  if ((s = split_input(e, x_dev, (size_t)M * K, st)) != T0B_OK) return s;
   CUDA_TRY(engine_qgemm(e, q0->qt, e->scratch_xh.as<__half>(), e->scratch_xl.as<__half>(), M, K, q0->W, 2 * F,
                         q0->shift, sg, q0->d_err, st));
   Epi dn{};
