@@ -14,6 +14,25 @@
 
 #include "t0b_internal.h"
 
+// Launch as a programmatic dependent of the previous kernel on `st`: the
+// kernel may start while that one finishes, and waits (griddepcontrol.wait)
+// before it reads anything the previous kernel writes.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // ============================================================== prep
 // One warp per variate row.  The causal scaler is the reference's Welford
 // recurrence in f32 (scaler.rs:44-118).  Per chunk of kPrepChunk steps each
@@ -224,17 +243,22 @@ __global__ void __launch_bounds__(32 * kSgemmSmallWarps) sgemm_small_kernel(Sgem
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * MT, n0 = blockIdx.x * 32;
   const int g4 = a.K / 4;  // 16-byte granules per row
-  for (int i = threadIdx.x; i < (MT + 32) * g4; i += blockDim.x) {
+  // the weight rows first: they never change, so they are fetched while the
+  // previous kernel (launched before this programmatic dependent) finishes
+  for (int i = threadIdx.x; i < 32 * g4; i += blockDim.x) {
     const int row = i / g4, q = i - row * g4;
-    if (row < MT) {
-      const int m = min(m0 + row, a.M - 1);  // rows past M duplicate a valid row; outputs dropped
-      cp_async16(As + (size_t)row * KP + 4 * q, a.A + (size_t)m * a.lda + 4 * q);
-    } else {
-      const int n = min(n0 + row - MT, a.N - 1);
-      cp_async16(Bs + (size_t)(row - MT) * KP + 4 * q, a.B + (size_t)n * a.ldb + 4 * q);
-    }
+    const int n = min(n0 + row, a.N - 1);
+    cp_async16(Bs + (size_t)row * KP + 4 * q, a.B + (size_t)n * a.ldb + 4 * q);
   }
   cp_async_commit();
+  pdl_wait();
+  for (int i = threadIdx.x; i < MT * g4; i += blockDim.x) {
+    const int row = i / g4, q = i - row * g4;
+    const int m = min(m0 + row, a.M - 1);  // rows past M duplicate a valid row; outputs dropped
+    cp_async16(As + (size_t)row * KP + 4 * q, a.A + (size_t)m * a.lda + 4 * q);
+  }
+  cp_async_commit();
+  pdl_launch_dependents();
   cp_async_wait<0>();
   __syncthreads();
   float acc[MT];
@@ -400,6 +424,7 @@ __global__ void __launch_bounds__(256, 2) sgemm_h_kernel(SgemmArgs a) {
 __global__ void rownorm_split_kernel(const float *x, const float *g, __half *xh, __half *xl, float *ssq, int M,
                                      int E) {
   pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
+  pdl_wait();               // x comes from the previous kernel
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
@@ -628,6 +653,7 @@ __global__ void __launch_bounds__(512, 1) attn_time_mma_kernel(AttnArgs a, const
   const bool use_tma = (use_tma_flags & 1) != 0;
   const bool tma_out = use_tma && (use_tma_flags & 2) != 0;
   pdl_launch_dependents();  // the next small-M GEMM may prefetch its weights
+  pdl_wait();               // q, k, v come from the previous kernel
   extern __shared__ __align__(128) uint4 smem_u4[];
   const int r = blockIdx.x, h = blockIdx.y;
   const int p = a.p, E = a.E;
@@ -1854,6 +1880,8 @@ __global__ void __launch_bounds__(256) attn_group_reg_kernel(AttnArgs a) {
 // Gather the output-patch tokens of every row and apply out_norm (one warp
 // per output token): xo[r*hp + j] = rmsnorm(x[r*p + p-hp-1+j]) * g.
 __global__ void dec_gather_kernel(const float *x, const float *g, float *xo, int R, int p, int hp, int E) {
+  pdl_launch_dependents();
+  pdl_wait();  // x comes from the previous kernel
   const int o = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (o >= R * hp) return;
@@ -1871,6 +1899,8 @@ __global__ void dec_gather_kernel(const float *x, const float *g, float *xo, int
 // dec [R*hp, 32*nq]; out [R, horizon, nq] (rows remapped by out_row).
 __global__ void dec_head_kernel(const float *dec, const float *loc, const float *scale, float *out,
                                 const int *out_row, int R, int hp, int horizon, int nq, int use_arcsinh) {
+  pdl_launch_dependents();
+  pdl_wait();  // dec comes from the previous kernel
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;  // (r, step)
   if (idx >= R * hp * 32) return;
   const int r = idx / (hp * 32), step = idx % (hp * 32);
@@ -1899,8 +1929,7 @@ static cudaError_t launch_sgemm_small(const SgemmArgs &a, cudaStream_t st) {
   cudaError_t e = t0b_smem_limit((const void *)sgemm_small_kernel<MT>, smem);
   if (e != cudaSuccess) return e;
   dim3 grid((a.N + 31) / 32, (a.M + MT - 1) / MT);
-  sgemm_small_kernel<MT><<<grid, 32 * kSgemmSmallWarps, smem, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(sgemm_small_kernel<MT>, grid, dim3(32 * kSgemmSmallWarps), smem, st, a);
 }
 
 cudaError_t t0b_launch_sgemm(const SgemmArgs &a, cudaStream_t st) {
@@ -1927,8 +1956,7 @@ cudaError_t t0b_launch_sgemm(const SgemmArgs &a, cudaStream_t st) {
 cudaError_t t0b_launch_rownorm_split(const float *x, const float *g, __half *xh, __half *xl, float *ssq, int M, int E,
                                      cudaStream_t st) {
   if (E % 4) return cudaErrorInvalidValue;
-  rownorm_split_kernel<<<(M + 7) / 8, 256, 0, st>>>(x, g, xh, xl, ssq, M, E);
-  return cudaGetLastError();
+  return launch_pdl(rownorm_split_kernel, dim3((M + 7) / 8), dim3(256), 0, st, x, g, xh, xl, ssq, M, E);
 }
 cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
   if (a.E / a.H == 128) {
@@ -1966,8 +1994,8 @@ cudaError_t t0b_launch_attn_time(const AttnArgs &a, cudaStream_t st) {
         t0b_make_tmap_f16_3d(&tol, a.ol, (uint64_t)a.E, (uint64_t)a.p, (uint64_t)a.R, rs, ss, 64, 16, 1, true);
     const int use_tma = t0b_make_tmap_f32_2d(&tm, a.qkv, (uint64_t)3 * a.E, (uint64_t)a.R * a.p,
                                              (uint64_t)3 * a.E * sizeof(float), 32, (uint32_t)a.p, true) ? 1 : 0;
-    attn_time_mma_kernel<<<dim3(a.R, a.H), 32 * QB, smem, st>>>(a, tm, toh, tol, use_tma | (use_tma && out_ok ? 2 : 0));
-    return cudaGetLastError();
+    return launch_pdl(attn_time_mma_kernel, dim3(a.R, a.H), dim3(32 * QB), smem, st, a, tm, toh, tol,
+                      use_tma | (use_tma && out_ok ? 2 : 0));
   }
   size_t smem = (size_t)(a.p * (65 + 64 + 64) + 4 * a.p) * sizeof(float);
   cudaError_t e = t0b_smem_limit((const void *)attn_time_kernel, smem);
@@ -1999,14 +2027,13 @@ cudaError_t t0b_launch_attn_group(const AttnArgs &a, cudaStream_t st) {
 cudaError_t t0b_launch_dec_gather(const float *x, const float *g, float *xo, int R, int p, int hp, int E,
                                   cudaStream_t st) {
   int n = R * hp;
-  dec_gather_kernel<<<(n + 7) / 8, 256, 0, st>>>(x, g, xo, R, p, hp, E);
-  return cudaGetLastError();
+  return launch_pdl(dec_gather_kernel, dim3((n + 7) / 8), dim3(256), 0, st, x, g, xo, R, p, hp, E);
 }
 cudaError_t t0b_launch_dec_head(const float *dec, const float *loc, const float *scale, float *out, const int *out_row,
                                 int R, int hp, int horizon, int nq, int use_arcsinh, cudaStream_t st) {
   int n = R * hp * 32;
-  dec_head_kernel<<<(n + 255) / 256, 256, 0, st>>>(dec, loc, scale, out, out_row, R, hp, horizon, nq, use_arcsinh);
-  return cudaGetLastError();
+  return launch_pdl(dec_head_kernel, dim3((n + 255) / 256), dim3(256), 0, st, dec, loc, scale, out, out_row, R, hp,
+                    horizon, nq, use_arcsinh);
 }
 
 // ============================================================== split
