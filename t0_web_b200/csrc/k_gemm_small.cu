@@ -360,13 +360,14 @@ __global__ void __launch_bounds__(kThreads) gemm_q_small_kernel(const __half *__
   }
 }
 
-// K slice per CTA: K itself up to 512 (one CTA per row group: at K = 512 a
-// 2-CTA cluster's reduction through distributed shared memory cost more
-// than the doubled MMA work per CTA, 0.704 -> 0.655 ms per single forecast),
-// else the smallest multiple of 256 dividing K that leaves at most
-// kMaxCluster slices.
+// K slice per CTA: K itself up to 1024 (one CTA per row group: a cluster's
+// reduction through distributed shared memory cost more than the extra MMA
+// work per CTA, 0.704 -> 0.655 ms per single forecast at K = 512; at
+// K = 1024, M = 16 a GEMM 8.1 -> 6.0 us with the split pass, a SwiGLU MLP
+// 24.1 -> 13.6 us), else the smallest multiple of 256 dividing K that leaves
+// at most kMaxCluster slices.
 int small_slice(int K) {
-  if (K <= 512) return K;
+  if (K <= 1024) return K;
   const int c = K / 256;
   for (int d = (c + kMaxCluster - 1) / kMaxCluster; d <= c; ++d)
     if (c % d == 0) return 256 * d;

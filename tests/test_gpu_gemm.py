@@ -50,12 +50,13 @@ def test_gemm_vs_oracle(engine, qtype, M):
 
 
 @pytest.mark.parametrize("qtype", [Q8_0, Q4_0], ids=["q8_0", "q4_0"])
-@pytest.mark.parametrize("K", [256, 768, 4096, 4352])
+@pytest.mark.parametrize("K", [256, 768, 1536, 4096, 4352])
 @pytest.mark.parametrize("M", [5, 19, 77])
 def test_small_m_k_slices(engine, qtype, K, M):
-    """Small-M K slicing: one slice (K = 256), a 3-CTA cluster (768), eight
-    slices of 512 (4096), and K = 17 x 256, which has no split into at most 8
-    slices and goes to the tensor-core kernel instead."""
+    """Small-M K slicing: one CTA over the whole K (256, with the f32 input
+    split inside the kernel; 768), a 6-CTA cluster of 256-wide slices (1536),
+    eight slices of 512 (4096), and K = 17 x 256, which has no split into at
+    most 8 slices and goes to the tensor-core kernel instead."""
     N = 512
     w, x = S.gemm_case(N, K, M, seed=K + M)
     wb = gguf.quantize(w, qtype)
