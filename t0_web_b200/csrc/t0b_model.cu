@@ -1490,9 +1490,11 @@ cudaError_t engine_qgemm(t0b_engine *e, int qt, const __half *ah, const __half *
   return t0b_launch_gemm_small(qt, ah, al, M, K, W, epi, err, st);
 }
 
-// GEMM on f32 activations x [M][K]: the small-M kernel splits them into its
-// f16 planes itself (no separate launch); the tensor-core kernel reads the
-// planes of one split pass into the engine's scratch.
+// GEMM on f32 activations x [M][K]: where the small-M kernel's K slices are
+// 256 wide, it splits them into its f16 planes itself (no separate launch);
+// otherwise (whole-K CTAs for 256 < K <= 1024, wider slices, the tensor-core
+// kernel) the GEMM reads the planes of one split pass into the engine's
+// scratch.
 t0b_status engine_qgemm_x(t0b_engine *e, int qt, const float *x, int M, int K, const uint8_t *W, int wrows,
                           int wshift, Epi &epi, int *err, cudaStream_t st) {
   if (!engine_use_tc(qt, M, K, epi) && t0b_small_supports(qt, M, K, epi, true)) {
